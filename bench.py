@@ -1,0 +1,329 @@
+"""Benchmark of the B200 routed-expert MoE layer (BASELINE metric: MoE-layer tokens/s and % of FP8 tensor peak at
+T=5120; HBM GB/s at T=128).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One step = one call of the routed FP8 layer (router projection, softmax/top-k, expert alignment, activation
+quantisation, gate_up GEMM + silu*mul + requantisation, down GEMM + routing weight, top-k sum) on T=5120 tokens
+of H=2048 with E=128 experts, top-8, I=768, synthetic seeded data, expert weights 128x128
+block-FP8.  The weights (604 MB) exceed the 126 MB L2, so every step streams them from HBM; no L2 flush is added.
+Under torchrun each rank runs its own replica (weak scaling) and the step time is the max over ranks.
+
+``--impl reference`` times the reference's own CPU implementation of the same layer (transformers' fallback
+block, float32, all host threads) on a bounded sample of the workload and prints the same JSON line with
+``"impl": "reference"``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer tokens/s and % FP8/FP4 tensor peak at T=5120; HBM GB/s at T=128"
+H, I, E, K = 2048, 768, 128, 8
+T_CTX, T_BRANCH, T_CPU_SAMPLE = 5120, 128, 512
+KERNELS_PER_STEP = 8  # router+top-k, 3 alignment passes, permute+quant, gate_up GEMM, down GEMM, combine
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def dist_init():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws == 1:
+        return 0, 1, 0
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    rank, local = int(os.environ["RANK"]), int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return rank, ws, local
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        rows = []
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), float(f[3]), f[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower().startswith("active")})
+        mhz = sorted(r[0] for r in rows)
+        return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(r[2] for r in rows)}
+
+
+def cpu_baseline(layer_cpu: dict, min_seconds: float = 12.0) -> dict:
+    """The reference's CPU fallback (transformers block, float32) on a 512-token sample of the workload."""
+    import torch
+
+    from oracle import torch_fallback
+    from prismyra_b200 import synth
+
+    w1 = synth.dequantize_fp8_blocks(layer_cpu["w1"], layer_cpu["w1_s"])
+    w2 = synth.dequantize_fp8_blocks(layer_cpu["w2"], layer_cpu["w2_s"])
+    router, experts = torch_fallback.build_block(layer_cpu["router_w"].float(), w1, w2, K)
+    x = layer_cpu["x"][:T_CPU_SAMPLE].float()
+    r = torch_fallback.time_routed(router, experts, x, min_seconds=min_seconds)
+    del w1, w2, router, experts
+    return {"value": r["tokens_per_s"], "unit": "tokens/s", "cores": r["threads"], "kind": "reference",
+            "sample": f"{T_CPU_SAMPLE} of the {T_CTX} tokens, {r['calls']} calls in {r['seconds']:.1f} s: "
+                      "transformers Qwen3_5MoeTopKRouter + Qwen3_5MoeExperts (the reference's CPU fallback) in "
+                      f"float32 on dequantised FP8 weights; os.cpu_count()={r['cpu_count']}"}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    import torch
+
+    from prismyra_b200 import synth
+
+    layer = synth.make_fp8_layer(T_CTX, H, I, E, seed=0, device="cpu")
+    per_step = max(3.0, min(20.0, 150.0 / max(1, args.steps + args.warmup)))
+    cb = cpu_baseline(layer, min_seconds=per_step * max(1, args.steps))
+    line = {
+        "metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": T_CPU_SAMPLE / cb["value"] * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": f"routed-expert layer, T={T_CTX} (timed on a {T_CPU_SAMPLE}-token sample), H={H}, "
+                               f"I={I}, E={E}, top-{K}", "tokens": T_CTX, "hidden": H, "intermediate": I,
+                   "experts": E, "top_k": K},
+        "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "torch_threads": torch.get_num_threads(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def time_region(fn, steps: int, stream) -> float:
+    """ms per call of fn over `steps` calls, CUDA events on the launching stream, synchronised both sides."""
+    import torch
+
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        fn()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def stage_times(layer: dict, T: int, reps: int = 10) -> dict:
+    """Per-stage device time (ms) of one forward, each stage timed alone with CUDA events."""
+    import torch
+
+    from prismyra_b200 import ops
+
+    s = torch.cuda.current_stream()
+    x, rw = layer["x"][:T].contiguous(), layer["router_w"]
+    logits, w, ids = ops.router_topk(x, rw, K)
+    srt, eids, npp, _ = ops.align(ids, E)
+    a_q, a_s = ops.permute_quant_fp8(x, srt, npp, K)
+    o_q, o_s, _ = ops.gemm1_fp8(a_q, a_s, layer["w1"], layer["w1_s"], eids, npp)
+    c3, _ = ops.gemm2_fp8(o_q, o_s, layer["w2"], layer["w2_s"], eids, npp, srt, w.reshape(-1), T, K)
+    ops.combine(c3, T, K)
+    out = {
+        "router_topk": time_region(lambda: ops.router_topk(x, rw, K), reps, s),
+        "align": time_region(lambda: ops.align(ids, E), reps, s),
+        "permute_quant": time_region(lambda: ops.permute_quant_fp8(x, srt, npp, K), reps, s),
+        "gemm1": time_region(lambda: ops.gemm1_fp8(a_q, a_s, layer["w1"], layer["w1_s"], eids, npp), reps, s),
+        "gemm2": time_region(lambda: ops.gemm2_fp8(o_q, o_s, layer["w2"], layer["w2_s"], eids, npp, srt,
+                                                   w.reshape(-1), T, K), reps, s),
+        "combine": time_region(lambda: ops.combine(c3, T, K), reps, s),
+    }
+    out["experts_hit"] = int((torch.bincount(ids.reshape(-1).long(), minlength=E) > 0).sum().item())
+    out["slots"] = int(npp.item())
+    return out
+
+
+def run_b200(args, rank: int, world: int, local: int) -> None:
+    import torch
+
+    from prismyra_b200 import ops, synth
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    pk = peaks()
+    fp8_peak = 2.0 * pk["bf16_tflops"]  # B200 FP8 dense rate is twice its BF16 dense rate
+    layer = synth.make_fp8_layer(T_CTX, H, I, E, seed=0, device=dev, gen_device="cuda")
+    x = layer["x"]
+    stream = torch.cuda.current_stream()
+
+    def step():
+        return ops.forward_fp8(x, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K, router_w=layer["router_w"])
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    ws, _ = ops.workspace_for(x, T_CTX, H, I, E, K)
+    ops.read_status(ws)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    barrier()
+    with Clocks(local) as clk:
+        ms = time_region(step, args.steps, stream)
+        barrier()
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * T_CTX / (ms * 1e-3)
+
+    # end to end through the public call with host buffers: pinned x in, out back to pinned memory
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty(T_CTX, H, dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        o = ops.forward_fp8(x_dev, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K,
+                            router_w=layer["router_w"])
+        out_host.copy_(o, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e2e_ms = time_region(e2e_step, args.steps, stream)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    st = stage_times(layer, T_CTX)
+    fl = synth.layer_flops(T_CTX, H, I, K)
+    g1_tflops = fl["gemm1"] / (st["gemm1"] * 1e-3) / 1e12
+    layer_tflops = fl["total"] / (ms * 1e-3) / 1e12
+
+    # the branch-readout shape: weight streaming, reported in GB/s of algorithmic bytes
+    xb = x[:T_BRANCH].contiguous()
+
+    def branch_step():
+        return ops.forward_fp8(xb, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K,
+                               router_w=layer["router_w"])
+
+    for _ in range(5):
+        branch_step()
+    b_ms = time_region(branch_step, max(20, args.steps), stream)
+    b_st = stage_times(layer, T_BRANCH)
+    b_bytes = synth.layer_bytes(T_BRANCH, b_st["experts_hit"], H, I, E)
+    b_gbs = b_bytes / (b_ms * 1e-3) / 1e9
+
+    if rank != 0:
+        return
+    cb = None
+    if world == 1 and not args.no_cpu_baseline:
+        layer_cpu = synth.make_fp8_layer(T_CTX, H, I, E, seed=0, device="cpu")
+        cb = cpu_baseline(layer_cpu)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
+        "config": {"workload": f"FP8 block-scaled routed-expert layer, T={T_CTX} tokens per GPU (BASELINE configs[1])",
+                   "tokens": T_CTX, "hidden": H, "intermediate": I, "experts": E, "top_k": K,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "no flush: 604 MB of expert weights (> 126 MB L2) stream from HBM every step"},
+        "tflops": layer_tflops,
+        "frac_fp8_peak": layer_tflops / fp8_peak,
+        "roofline": {"bound": "tensor", "kernel": "moe_gemm_fp8_kernel<0> (gate_up)", "achieved": g1_tflops,
+                     "peak": fp8_peak, "unit": "TFLOP/s", "frac": g1_tflops / fp8_peak, "traffic": None,
+                     "peak_source": f"2 x bf16_tflops of {pk['source']} MEASURED_PEAKS.json ({pk['bf16_tflops']})",
+                     "flops_per_launch": fl["gemm1"]},
+        "stages_ms": {k: round(v, 4) for k, v in st.items() if isinstance(v, float)},
+        "branch_t128": {"ms": b_ms, "tokens_per_s": T_BRANCH / (b_ms * 1e-3), "gbs": b_gbs,
+                        "frac_hbm": b_gbs / pk["hbm_gbs"], "experts_hit": b_st["experts_hit"],
+                        "algorithmic_bytes": b_bytes,
+                        "stages_ms": {k: round(v, 4) for k, v in b_st.items() if isinstance(v, float)}},
+        "e2e": {"value": world * T_CTX / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": T_CTX * H * 2, "d2h_bytes_per_step": T_CTX * H * 2},
+        "gpu_launches": KERNELS_PER_STEP * args.steps,
+        "clocks": clk.summary(),
+    }
+    if cb is not None:
+        line["cpu_baseline"] = cb
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        # the CPU reference runs on rank 0 only; other ranks exit without work or a process group
+        run_reference(args, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
+        return
+    rank, world, local = dist_init()
+    try:
+        run_b200(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

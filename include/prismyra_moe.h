@@ -1,0 +1,139 @@
+/*
+ * prismyra_moe.h -- C ABI of the B200 (sm_100a) routed-expert MoE layer.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream handle (cudaStream_t passed as
+ * void*; NULL = the legacy default stream), launches asynchronously on that stream, allocates nothing and
+ * returns a status code (PM_OK = 0).  Scratch memory is caller-owned: size it with pm_moe_workspace_bytes and
+ * pass it to the calls that need it.  No call synchronises the stream except pm_moe_read_status.
+ *
+ * Layouts (row-major, bf16 = 16-bit brain float bit pattern, e4m3 = float8 e4m3fn byte):
+ *   x          bf16  [T, H]            hidden states of T tokens
+ *   router_w   bf16  [E, H]            the router's projection weight (reference: block.gate.weight)
+ *   logits     bf16  [T, E]
+ *   topk_w     f32   [T, k]            renormalised routing weights;  topk_ids  i32 [T, k]
+ *   w1         e4m3  [E, 2I, H]        gate rows 0..I-1, up rows I..2I-1 (reference: experts.gate_up_proj)
+ *   w1_s       f32   [E, 2I/128, H/128] per 128x128 block multiplier (reference: gate_up_proj_scale_inv)
+ *   w2         e4m3  [E, H, I]          (reference: experts.down_proj);  w2_s f32 [E, H/128, I/128]
+ *   out        bf16  [T, H]            routed-expert output (the shared expert is not part of this layer)
+ * Shape limits: H % 256 == 0, I % 128 == 0, 1 <= k <= 16, k <= E <= 256.  Pointers 16-byte aligned.
+ *
+ * The references cited beside each declaration are files of the Prismyra reference (prismyra/...) and of the
+ * vLLM release it calls (vllm/...).
+ */
+#ifndef PRISMYRA_MOE_H
+#define PRISMYRA_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void *pm_stream_t;
+
+enum pm_status {
+    PM_OK = 0,
+    PM_ERR_INVALID = 1,   /* a NULL pointer or negative size */
+    PM_ERR_SHAPE = 2,     /* dimensions outside the supported set */
+    PM_ERR_ALIGN = 3,     /* a pointer is not 16-byte aligned */
+    PM_ERR_WORKSPACE = 4, /* workspace too small */
+    PM_ERR_CUDA = 5,      /* a CUDA launch or driver call failed */
+    PM_ERR_DEVICE = 6,    /* the current device is not sm_100 */
+    PM_ERR_TIMEOUT = 7    /* a kernel gave up on a bounded wait (reported by pm_moe_read_status) */
+};
+
+enum pm_format { PM_FMT_FP8 = 0, PM_FMT_NVFP4 = 1 };
+
+/* Workspace regions, for callers that want to inspect intermediates (pm_moe_workspace_region). */
+enum pm_region {
+    PM_WS_STATUS = 0,   /* i32 [4]: [0] = timeout flag */
+    PM_WS_LOGITS = 1,   /* bf16 [T, E] */
+    PM_WS_TOPK_W = 2,   /* f32 [T, k] */
+    PM_WS_TOPK_IDS = 3, /* i32 [T, k] */
+    PM_WS_COUNTS = 4,   /* i32 [chunks, E] */
+    PM_WS_EXPERT_OFF = 5, /* i32 [E + 1] first slot of each expert, padded total last */
+    PM_WS_SORTED = 6,   /* i32 [max_slots] flat index t*k+j per slot, T*k = padding */
+    PM_WS_EXPERT_IDS = 7, /* i32 [max_slots / 128] expert of each 128-slot block */
+    PM_WS_NUM_POST_PAD = 8, /* i32 [1] slots in use */
+    PM_WS_A1 = 9,       /* e4m3 [max_slots, H] activations in slot order (NVFP4: packed e2m1 [max_slots, H/2]) */
+    PM_WS_A1_SCALE = 10, /* f32 [max_slots, H/128] (NVFP4: e4m3 [max_slots, H/16]) */
+    PM_WS_A2 = 11,      /* e4m3 [max_slots, I] down-projection input (NVFP4: packed e2m1 [max_slots, I/2]) */
+    PM_WS_A2_SCALE = 12, /* f32 [max_slots, I/128] (NVFP4: e4m3 [max_slots, I/16]) */
+    PM_WS_C3 = 13       /* bf16 [T*k, H] weighted expert outputs per (token, slot) */
+};
+
+/* Version of this ABI; bumped on any incompatible change. */
+int pm_moe_abi_version(void);
+const char *pm_moe_status_string(int status);
+
+/* Maximum slots after per-expert padding to 128: T*k + E*127, rounded up to 128
+ * (vllm/model_executor/layers/fused_moe/moe_align_block_size.py:74 max_num_tokens_padded). */
+int pm_moe_max_slots(int T, int E, int k);
+
+/* Bytes of caller-owned scratch the layer needs for T tokens; the reference sizes its per-thread workspace
+ * the same way from the token count (prismyra/kernels/nvfp4.py:213-245 FusedExpertsFp4._workspace). */
+size_t pm_moe_workspace_bytes(int T, int H, int I, int E, int k, int fmt);
+/* Offset and size of one region inside that workspace. */
+int pm_moe_workspace_region(int T, int H, int I, int E, int k, int fmt, int region, size_t *offset, size_t *bytes);
+
+/* Router projection + softmax + top-k + renormalise, row-count invariant.  Replaces
+ * prismyra/kernels/qwen3_moe.py:169-171 (FusedExperts._route) followed by :196 (vllm fused_topk,
+ * renormalize=True; vllm/model_executor/layers/fused_moe/router/fused_topk_router.py:69-113).
+ * logits may be NULL when the caller does not want them. */
+int pm_moe_router_topk(const void *x, const void *router_w, int T, int H, int E, int k, void *logits,
+                       float *topk_w, int32_t *topk_ids, pm_stream_t stream);
+
+/* Softmax + top-k + renormalise from given bf16 logits: prismyra/kernels/qwen3_moe.py:196 (fused_topk). */
+int pm_moe_topk(const void *logits, int T, int E, int k, float *topk_w, int32_t *topk_ids, pm_stream_t stream);
+
+/* Expert alignment: vllm/model_executor/layers/fused_moe/moe_align_block_size.py:11-99 with block 128, the
+ * reference's call at vllm/model_executor/layers/fused_moe/fused_moe.py:1536-1585.  Flat indices grouped by
+ * expert in ascending order, padded with T*k.  Needs the workspace for its per-chunk counts.  expert_off may
+ * be NULL. */
+int pm_moe_align(const int32_t *topk_ids, int T, int k, int E, int32_t *sorted_ids, int32_t *expert_ids,
+                 int32_t *num_post_pad, int32_t *expert_off, void *workspace, size_t workspace_bytes,
+                 pm_stream_t stream);
+
+/* Activation gather + per-128-column e4m3 quantisation in slot order:
+ * vllm/model_executor/layers/quantization/utils/fp8_utils.py:110-150 (per_token_group_quant_fp8), applied
+ * by vllm/model_executor/layers/fused_moe/fused_moe.py:1780-1786 before the gate_up GEMM. */
+int pm_moe_permute_quant_fp8(const void *x, int T, int H, int k, const int32_t *sorted_ids,
+                             const int32_t *num_post_pad, int max_slots, uint8_t *a_q, float *a_s,
+                             pm_stream_t stream);
+
+/* Grouped gate_up GEMM with fused silu*mul and e4m3 re-quantisation:
+ * vllm/model_executor/layers/fused_moe/fused_moe.py:1801-1822 (GEMM1), :1825-1827 (silu_and_mul),
+ * :1829-1835 (requantisation).  a_q/a_s in slot order; out_q e4m3 [max_slots, I], out_s f32 [max_slots, I/128].
+ * err (may be NULL) is set to 1 if the kernel gave up on a bounded wait. */
+int pm_moe_gemm1_fp8(const uint8_t *a_q, const float *a_s, const uint8_t *w1, const float *w1_s,
+                     const int32_t *expert_ids, const int32_t *num_post_pad, int max_slots, int H, int I, int E,
+                     uint8_t *out_q, float *out_s, int32_t *err, pm_stream_t stream);
+
+/* Grouped down GEMM with the routing weight applied in fp32 before the bf16 cast, scattered to the
+ * (token, slot) row: vllm/model_executor/layers/fused_moe/fused_moe.py:1840-1861, :538-548. */
+int pm_moe_gemm2_fp8(const uint8_t *a_q, const float *a_s, const uint8_t *w2, const float *w2_s,
+                     const int32_t *expert_ids, const int32_t *num_post_pad, const int32_t *sorted_ids,
+                     const float *topk_w, int max_slots, int T, int k, int H, int I, int E, void *c3, int32_t *err,
+                     pm_stream_t stream);
+
+/* out[t] = bf16(sum_j c3[t*k + j]) accumulated in fp32: vllm/model_executor/layers/fused_moe/fused_moe.py:1864
+ * (ops.moe_sum). */
+int pm_moe_combine(const void *c3, int T, int k, int H, void *out, pm_stream_t stream);
+
+/* The whole routed FP8 layer: prismyra/kernels/qwen3_moe.py:184-199 (FusedExperts.forward) minus the shared
+ * expert, i.e. logits -> fused_topk -> fused_experts (vllm/model_executor/layers/fused_moe/fused_moe.py:
+ * 1664-1869).  Give either router_w (the router runs in-kernel) or logits (bf16 [T, E], router_w ignored). */
+int pm_moe_forward_fp8(const void *x, const void *router_w, const void *logits, const uint8_t *w1,
+                       const float *w1_s, const uint8_t *w2, const float *w2_s, int T, int H, int I, int E, int k,
+                       void *out, void *workspace, size_t workspace_bytes, pm_stream_t stream);
+
+/* Synchronise the stream and report PM_ERR_TIMEOUT if any kernel of the last calls on this workspace gave up
+ * on a bounded wait (the flag is cleared by each pm_moe_forward_* call). */
+int pm_moe_read_status(const void *workspace, pm_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PRISMYRA_MOE_H */

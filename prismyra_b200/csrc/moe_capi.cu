@@ -1,0 +1,351 @@
+// C-ABI entry points (include/prismyra_moe.h): argument checks, workspace carving, tensor-map encoding and the
+// launch sequence of the routed-expert layer.  Nothing here allocates device memory or synchronises, except
+// pm_moe_read_status.
+#include <cudaTypedefs.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "../../include/prismyra_moe.h"
+#include "moe_internal.h"
+
+namespace pm {
+
+// ------------------------------------------------------------------------------------------- tensor maps
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static std::once_flag g_encode_once;
+
+bool encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                       uint32_t box_inner, uint32_t box_outer) {
+    std::call_once(g_encode_once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (g_encode == nullptr) return false;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// ------------------------------------------------------------------------------------------- device facts
+struct DeviceInfo {
+    int sms = 0;
+    int ok = -1;  // -1 unknown, 0 not sm_100, 1 sm_100
+};
+static DeviceInfo g_dev[64];
+static std::mutex g_dev_mu;
+
+static int current_device_info(DeviceInfo* out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PM_ERR_CUDA;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    DeviceInfo& d = g_dev[dev];
+    if (d.ok < 0) {
+        int major = 0, minor = 0, sms = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return PM_ERR_CUDA;
+        d.ok = (major == 10 && minor == 0) ? 1 : 0;
+        d.sms = sms;
+    }
+    *out = d;
+    return d.ok ? PM_OK : PM_ERR_DEVICE;
+}
+
+// ------------------------------------------------------------------------------------------- workspace
+struct Layout {
+    size_t off[14];
+    size_t len[14];
+    size_t total;
+    int max_slots;
+};
+
+static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+static int max_slots_of(int T, int E, int k) {
+    const long s = (long)T * k + (long)E * (kBlockM - 1);
+    return (int)((s + kBlockM - 1) / kBlockM * kBlockM);
+}
+
+static Layout layout_of(int T, int H, int I, int E, int k, int fmt) {
+    Layout L;
+    const long n = (long)T * k;
+    const int ms = max_slots_of(T, E, k);
+    const int chunks = n > 0 ? cdiv(n, kAlignChunk) : 1;
+    const bool fp4 = fmt == PM_FMT_NVFP4;
+    L.len[PM_WS_STATUS] = 4 * sizeof(int32_t);
+    L.len[PM_WS_LOGITS] = (size_t)T * E * 2;
+    L.len[PM_WS_TOPK_W] = (size_t)n * 4;
+    L.len[PM_WS_TOPK_IDS] = (size_t)n * 4;
+    L.len[PM_WS_COUNTS] = (size_t)chunks * E * 4;
+    L.len[PM_WS_EXPERT_OFF] = (size_t)(E + 1) * 4;
+    L.len[PM_WS_SORTED] = (size_t)ms * 4;
+    L.len[PM_WS_EXPERT_IDS] = (size_t)(ms / kBlockM) * 4;
+    L.len[PM_WS_NUM_POST_PAD] = 4;
+    L.len[PM_WS_A1] = (size_t)ms * (fp4 ? H / 2 : H);
+    L.len[PM_WS_A1_SCALE] = (size_t)ms * (fp4 ? H / 16 : (H / 128) * 4);
+    L.len[PM_WS_A2] = (size_t)ms * (fp4 ? I / 2 : I);
+    L.len[PM_WS_A2_SCALE] = (size_t)ms * (fp4 ? I / 16 : (I / 128) * 4);
+    L.len[PM_WS_C3] = (size_t)n * H * 2;
+    size_t o = 0;
+    for (int r = 0; r < 14; ++r) {
+        L.off[r] = o;
+        o = align256(o + L.len[r]);
+    }
+    L.total = o;
+    L.max_slots = ms;
+    return L;
+}
+
+static bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static int check_dims(int T, int H, int I, int E, int k) {
+    if (T < 0 || H <= 0 || I <= 0 || E <= 0 || k <= 0) return PM_ERR_INVALID;
+    if (H % 256 != 0 || I % 128 != 0 || k > kMaxTopK || k > E || E > kMaxExperts) return PM_ERR_SHAPE;
+    if ((long)T * k > (1L << 30)) return PM_ERR_SHAPE;
+    return PM_OK;
+}
+
+static int cuda_status(cudaError_t e) { return e == cudaSuccess ? PM_OK : PM_ERR_CUDA; }
+
+static GemmArgs gemm_args_common(const float* a_s, const float* b_s, const int32_t* expert_ids,
+                                 const int32_t* npp, int n_total, int K, int n_tiles, int max_slots, int inter,
+                                 int32_t* err) {
+    GemmArgs g;
+    memset(&g, 0, sizeof(g));
+    g.a_scale = a_s;
+    g.b_scale = b_s;
+    g.expert_ids = expert_ids;
+    g.num_post_pad = npp;
+    g.n_total = n_total;
+    g.K = K;
+    g.n_tiles = n_tiles;
+    g.max_tiles = (max_slots / kBlockM) * n_tiles;
+    g.inter = inter;
+    g.err = err;
+    return g;
+}
+
+}  // namespace pm
+
+using namespace pm;
+
+extern "C" {
+
+int pm_moe_abi_version(void) { return 1; }
+
+const char* pm_moe_status_string(int status) {
+    switch (status) {
+        case PM_OK: return "ok";
+        case PM_ERR_INVALID: return "invalid argument (NULL pointer or negative size)";
+        case PM_ERR_SHAPE: return "unsupported shape (need H%256==0, I%128==0, 1<=k<=16, k<=E<=256)";
+        case PM_ERR_ALIGN: return "pointer not 16-byte aligned";
+        case PM_ERR_WORKSPACE: return "workspace too small";
+        case PM_ERR_CUDA: return "CUDA launch or driver call failed";
+        case PM_ERR_DEVICE: return "current device is not sm_100 (B200)";
+        case PM_ERR_TIMEOUT: return "a kernel gave up on a bounded wait";
+        default: return "unknown status";
+    }
+}
+
+int pm_moe_max_slots(int T, int E, int k) { return max_slots_of(T, E, k); }
+
+size_t pm_moe_workspace_bytes(int T, int H, int I, int E, int k, int fmt) {
+    if (check_dims(T, H, I, E, k) != PM_OK) return 0;
+    return layout_of(T, H, I, E, k, fmt).total;
+}
+
+int pm_moe_workspace_region(int T, int H, int I, int E, int k, int fmt, int region, size_t* offset, size_t* bytes) {
+    const int st = check_dims(T, H, I, E, k);
+    if (st != PM_OK) return st;
+    if (region < 0 || region > PM_WS_C3 || offset == nullptr || bytes == nullptr) return PM_ERR_INVALID;
+    const Layout L = layout_of(T, H, I, E, k, fmt);
+    *offset = L.off[region];
+    *bytes = L.len[region];
+    return PM_OK;
+}
+
+int pm_moe_router_topk(const void* x, const void* router_w, int T, int H, int E, int k, void* logits,
+                       float* topk_w, int32_t* topk_ids, pm_stream_t stream) {
+    if (T < 0 || H <= 0 || E <= 0 || k <= 0) return PM_ERR_INVALID;
+    if (H % 128 != 0 || E > kMaxExperts || k > kMaxTopK || k > E) return PM_ERR_SHAPE;
+    if (T == 0) return PM_OK;
+    if (!x || !router_w || !topk_w || !topk_ids) return PM_ERR_INVALID;
+    if (!a16(x) || !a16(router_w)) return PM_ERR_ALIGN;
+    DeviceInfo d;
+    const int st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    return cuda_status(launch_router_topk(x, router_w, T, H, E, k, logits, topk_w, topk_ids, (cudaStream_t)stream));
+}
+
+int pm_moe_topk(const void* logits, int T, int E, int k, float* topk_w, int32_t* topk_ids, pm_stream_t stream) {
+    if (T < 0 || E <= 0 || k <= 0) return PM_ERR_INVALID;
+    if (E > kMaxExperts || k > kMaxTopK || k > E) return PM_ERR_SHAPE;
+    if (T == 0) return PM_OK;
+    if (!logits || !topk_w || !topk_ids) return PM_ERR_INVALID;
+    DeviceInfo d;
+    const int st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    return cuda_status(launch_topk(logits, T, E, k, topk_w, topk_ids, (cudaStream_t)stream));
+}
+
+int pm_moe_align(const int32_t* topk_ids, int T, int k, int E, int32_t* sorted_ids, int32_t* expert_ids,
+                 int32_t* num_post_pad, int32_t* expert_off, void* workspace, size_t workspace_bytes,
+                 pm_stream_t stream) {
+    if (T < 0 || k <= 0 || E <= 0 || E > 1024) return PM_ERR_INVALID;
+    if (!sorted_ids || !expert_ids || !num_post_pad || !workspace || (T > 0 && !topk_ids)) return PM_ERR_INVALID;
+    const long n = (long)T * k;
+    const int chunks = n > 0 ? cdiv(n, kAlignChunk) : 1;
+    if (workspace_bytes < (size_t)chunks * E * 4) return PM_ERR_WORKSPACE;
+    DeviceInfo d;
+    const int st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    return cuda_status(launch_align(topk_ids, (int)n, E, static_cast<int32_t*>(workspace), sorted_ids, expert_ids,
+                                    num_post_pad, expert_off, (cudaStream_t)stream));
+}
+
+int pm_moe_permute_quant_fp8(const void* x, int T, int H, int k, const int32_t* sorted_ids,
+                             const int32_t* num_post_pad, int max_slots, uint8_t* a_q, float* a_s,
+                             pm_stream_t stream) {
+    if (T < 0 || H <= 0 || k <= 0 || max_slots < 0) return PM_ERR_INVALID;
+    if (H % 128 != 0) return PM_ERR_SHAPE;
+    if (max_slots == 0) return PM_OK;
+    if (!sorted_ids || !num_post_pad || !a_q || !a_s || (T > 0 && !x)) return PM_ERR_INVALID;
+    if ((T > 0 && !a16(x)) || !a16(a_q)) return PM_ERR_ALIGN;
+    DeviceInfo d;
+    const int st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    return cuda_status(launch_permute_quant_fp8(x, H, k, T * k, sorted_ids, num_post_pad, max_slots, a_q, a_s,
+                                                (cudaStream_t)stream));
+}
+
+int pm_moe_gemm1_fp8(const uint8_t* a_q, const float* a_s, const uint8_t* w1, const float* w1_s,
+                     const int32_t* expert_ids, const int32_t* num_post_pad, int max_slots, int H, int I, int E,
+                     uint8_t* out_q, float* out_s, int32_t* err, pm_stream_t stream) {
+    int st = check_dims(0, H, I, E, 1);
+    if (st != PM_OK) return st;
+    if (max_slots < 0 || max_slots % kBlockM != 0) return PM_ERR_SHAPE;
+    if (max_slots == 0) return PM_OK;
+    if (!a_q || !a_s || !w1 || !w1_s || !expert_ids || !num_post_pad || !out_q || !out_s) return PM_ERR_INVALID;
+    if (!a16(a_q) || !a16(w1) || !a16(out_q)) return PM_ERR_ALIGN;
+    DeviceInfo d;
+    st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    CUtensorMap ta, tb;
+    if (!encode_tmap_2d_u8(&ta, a_q, (uint64_t)H, (uint64_t)max_slots, (uint64_t)H, 128, 128) ||
+        !encode_tmap_2d_u8(&tb, w1, (uint64_t)H, (uint64_t)E * 2 * I, (uint64_t)H, 128, 128))
+        return PM_ERR_CUDA;
+    GemmArgs g = gemm_args_common(a_s, w1_s, expert_ids, num_post_pad, 2 * I, H, I / 128, max_slots, I, err);
+    g.out_q = out_q;
+    g.out_s = out_s;
+    return cuda_status(launch_gemm_fp8(0, ta, tb, g, d.sms, (cudaStream_t)stream));
+}
+
+int pm_moe_gemm2_fp8(const uint8_t* a_q, const float* a_s, const uint8_t* w2, const float* w2_s,
+                     const int32_t* expert_ids, const int32_t* num_post_pad, const int32_t* sorted_ids,
+                     const float* topk_w, int max_slots, int T, int k, int H, int I, int E, void* c3, int32_t* err,
+                     pm_stream_t stream) {
+    int st = check_dims(T, H, I, E, k);
+    if (st != PM_OK) return st;
+    if (max_slots < 0 || max_slots % kBlockM != 0) return PM_ERR_SHAPE;
+    if (max_slots == 0 || T == 0) return PM_OK;
+    if (!a_q || !a_s || !w2 || !w2_s || !expert_ids || !num_post_pad || !sorted_ids || !topk_w || !c3)
+        return PM_ERR_INVALID;
+    if (!a16(a_q) || !a16(w2) || !a16(c3)) return PM_ERR_ALIGN;
+    DeviceInfo d;
+    st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    CUtensorMap ta, tb;
+    if (!encode_tmap_2d_u8(&ta, a_q, (uint64_t)I, (uint64_t)max_slots, (uint64_t)I, 128, 128) ||
+        !encode_tmap_2d_u8(&tb, w2, (uint64_t)I, (uint64_t)E * H, (uint64_t)I, 128, 128))
+        return PM_ERR_CUDA;
+    GemmArgs g = gemm_args_common(a_s, w2_s, expert_ids, num_post_pad, H, I, H / 256, max_slots, I, err);
+    g.sorted_ids = sorted_ids;
+    g.topk_w = topk_w;
+    g.c3 = static_cast<__nv_bfloat16*>(c3);
+    g.n_valid = T * k;
+    return cuda_status(launch_gemm_fp8(1, ta, tb, g, d.sms, (cudaStream_t)stream));
+}
+
+int pm_moe_combine(const void* c3, int T, int k, int H, void* out, pm_stream_t stream) {
+    if (T < 0 || k <= 0 || H <= 0) return PM_ERR_INVALID;
+    if (H % 8 != 0) return PM_ERR_SHAPE;
+    if (T == 0) return PM_OK;
+    if (!c3 || !out) return PM_ERR_INVALID;
+    if (!a16(c3) || !a16(out)) return PM_ERR_ALIGN;
+    DeviceInfo d;
+    const int st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    return cuda_status(launch_combine(c3, T, k, H, out, (cudaStream_t)stream));
+}
+
+int pm_moe_forward_fp8(const void* x, const void* router_w, const void* logits, const uint8_t* w1,
+                       const float* w1_s, const uint8_t* w2, const float* w2_s, int T, int H, int I, int E, int k,
+                       void* out, void* workspace, size_t workspace_bytes, pm_stream_t stream) {
+    int st = check_dims(T, H, I, E, k);
+    if (st != PM_OK) return st;
+    if (T == 0) return PM_OK;
+    if (!x || !w1 || !w1_s || !w2 || !w2_s || !out || !workspace || (!router_w && !logits)) return PM_ERR_INVALID;
+    if (!a16(x) || !a16(w1) || !a16(w2) || !a16(out) || !a16(workspace) || (router_w && !logits && !a16(router_w)))
+        return PM_ERR_ALIGN;
+    const Layout L = layout_of(T, H, I, E, k, PM_FMT_FP8);
+    if (workspace_bytes < L.total) return PM_ERR_WORKSPACE;
+    DeviceInfo d;
+    st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    auto R = [&](int r) { return ws + L.off[r]; };
+    int32_t* status = reinterpret_cast<int32_t*>(R(PM_WS_STATUS));
+    float* topk_w = reinterpret_cast<float*>(R(PM_WS_TOPK_W));
+    int32_t* topk_ids = reinterpret_cast<int32_t*>(R(PM_WS_TOPK_IDS));
+    int32_t* sorted = reinterpret_cast<int32_t*>(R(PM_WS_SORTED));
+    int32_t* expert_ids = reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_IDS));
+    int32_t* npp = reinterpret_cast<int32_t*>(R(PM_WS_NUM_POST_PAD));
+    uint8_t* a1 = R(PM_WS_A1);
+    float* a1s = reinterpret_cast<float*>(R(PM_WS_A1_SCALE));
+    uint8_t* a2 = R(PM_WS_A2);
+    float* a2s = reinterpret_cast<float*>(R(PM_WS_A2_SCALE));
+    void* c3 = R(PM_WS_C3);
+
+    if (cudaMemsetAsync(status, 0, L.len[PM_WS_STATUS], s) != cudaSuccess) return PM_ERR_CUDA;
+    cudaError_t e;
+    if (logits != nullptr)
+        e = launch_topk(logits, T, E, k, topk_w, topk_ids, s);
+    else
+        e = launch_router_topk(x, router_w, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, s);
+    if (e != cudaSuccess) return PM_ERR_CUDA;
+    e = launch_align(topk_ids, T * k, E, reinterpret_cast<int32_t*>(R(PM_WS_COUNTS)), sorted, expert_ids, npp,
+                     reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_OFF)), s);
+    if (e != cudaSuccess) return PM_ERR_CUDA;
+    e = launch_permute_quant_fp8(x, H, k, T * k, sorted, npp, L.max_slots, a1, a1s, s);
+    if (e != cudaSuccess) return PM_ERR_CUDA;
+    st = pm_moe_gemm1_fp8(a1, a1s, w1, w1_s, expert_ids, npp, L.max_slots, H, I, E, a2, a2s, status, stream);
+    if (st != PM_OK) return st;
+    st = pm_moe_gemm2_fp8(a2, a2s, w2, w2_s, expert_ids, npp, sorted, topk_w, L.max_slots, T, k, H, I, E, c3,
+                          status, stream);
+    if (st != PM_OK) return st;
+    return cuda_status(launch_combine(c3, T, k, H, out, s));
+}
+
+int pm_moe_read_status(const void* workspace, pm_stream_t stream) {
+    if (!workspace) return PM_ERR_INVALID;
+    int32_t flag = 0;
+    if (cudaMemcpyAsync(&flag, workspace, sizeof(flag), cudaMemcpyDeviceToHost, (cudaStream_t)stream) != cudaSuccess)
+        return PM_ERR_CUDA;
+    if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return PM_ERR_CUDA;
+    return flag ? PM_ERR_TIMEOUT : PM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,310 @@
+// Persistent grouped GEMM for the FP8 (e4m3, 128x128 fp32 block scales) routed experts on sm_100a.
+//
+// Arithmetic (vLLM fused_moe_kernel, fused_moe.py:483-548, the kernel the reference's FusedExperts calls):
+//   acc = sum over 128-wide K blocks kb of  (A_q[row, kb] . B_q[n, kb]) * a_scale[row, kb] * b_scale[n/128, kb]
+// The block scales are fp32 (not powers of two), so the tensor core cannot apply them: every K block is one
+// tcgen05 MMA chain into a fresh TMEM accumulator, and the epilogue warps promote it into fp32 registers with the
+// block's scale ("software promotion").  Two TMEM accumulators alternate so the MMA of block kb+1 runs while
+// block kb is being promoted.
+//
+// Tiles: 128 rows (one alignment block, one expert) x 256 columns x 128 K per pipeline stage.
+//   mode 0 (gate_up, K = H): the 256 columns are 128 gate rows n0.. and the matching 128 up rows I+n0..,
+//           the epilogue applies bf16 -> silu(gate)*up -> bf16 and re-quantises to e4m3 with one scale per
+//           128 output columns (exactly one tile), writing the down GEMM's A operand in slot order.
+//   mode 1 (down, K = I): the 256 columns are hidden columns n0..n0+255; the epilogue multiplies by the routing
+//           weight in fp32, rounds to bf16 and scatters the row to c3[flat index].
+// Warp roles (384 threads, three warpgroups): warp 0 issues TMA loads, warp 1 owns TMEM and issues the MMAs
+// (warps 2-3 idle); warpgroups 1 and 2 (warps 4-11) promote and run the epilogue.  Epilogue warp w reads TMEM
+// lanes 32*(w%4).. and one half of the tile's columns.  Registers are rebalanced with setmaxnreg: 56 for
+// warpgroup 0 and 224 for the epilogue warpgroups (56*128 + 224*256 = 64512 = 168 * 384, the launch's total).
+#include "moe_internal.h"
+#include "ptx.cuh"
+
+namespace pm {
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kBK = 128;
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBK;          // 16 KB
+constexpr int kBBytes = kBN * kBK;          // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kThreads = 384;
+constexpr int kEpiWarp0 = 4;          // first epilogue warp
+constexpr int kEpiWarps = 8;
+constexpr uint32_t kTmemCols = 512;         // two 256-column fp32 accumulators
+constexpr uint32_t kIdesc = idesc_f32acc(0 /*e4m3*/, 0 /*e4m3*/, kBM, kBN);
+
+struct SmemTail {
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    uint64_t tfull[2];
+    uint64_t tempty[2];
+    uint64_t drain;
+    uint64_t xbar[2];         // epilogue amax exchange, one per tile parity
+    uint32_t tmem_base;
+    int abort;
+    float amax_x[2][2][kBM];  // [tile parity][column half][row]
+};
+
+constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + (size_t)kStages * kStageBytes + sizeof(SmemTail);
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    const float s = bf16_round(__fdiv_rn(g, 1.0f + expf(-g)));
+    return bf16_round(s * u);
+}
+
+// acc[c] += scale * TMEM[lane, col + c] for 32 consecutive columns.
+__device__ __forceinline__ void promote32(uint32_t taddr, float scale, float* acc) {
+    uint32_t r[32];
+    tmem_ld32(taddr, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = fmaf(__uint_as_float(r[i]), scale, acc[i]);
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                        const GemmArgs args) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+    const uint32_t sbase = smem_u32(smem);
+    SmemTail* tail = reinterpret_cast<SmemTail*>(smem + (size_t)kStages * kStageBytes);
+    volatile int* abort = &tail->abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t bar_full = smem_u32(tail->full), bar_empty = smem_u32(tail->empty);
+    const uint32_t bar_tfull = smem_u32(tail->tfull), bar_tempty = smem_u32(tail->tempty);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(bar_tfull + 8 * b, 1);
+            mbar_init(bar_tempty + 8 * b, kEpiWarps);
+        }
+        mbar_init(smem_u32(&tail->drain), 1);
+        mbar_init(smem_u32(&tail->xbar[0]), kEpiWarps * 32);
+        mbar_init(smem_u32(&tail->xbar[1]), kEpiWarps * 32);
+        tail->abort = 0;
+        fence_barrier_init();
+        fence_proxy_async_smem();
+        prefetch_tensormap(&tm_a);
+        prefetch_tensormap(&tm_b);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&tail->tmem_base), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = tail->tmem_base;
+
+    const int KB = args.K / kBK;
+    const int num_tiles = (*args.num_post_pad / kBM) * args.n_tiles;
+
+    if (warp < kEpiWarp0) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+      if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                const int mb = tile / args.n_tiles, nt = tile % args.n_tiles;
+                const int e = args.expert_ids[mb];
+                const int row0 = e * args.n_total + (MODE == 0 ? nt * 128 : nt * kBN);
+                const int row1 = (MODE == 0) ? e * args.n_total + args.inter + nt * 128 : row0 + 128;
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, abort)) { ok = false; break; }
+                    const uint32_t a_dst = sbase + stage * kStageBytes;
+                    const uint32_t b_dst = a_dst + kABytes;
+                    const uint32_t fb = bar_full + 8 * stage;
+                    mbar_arrive_expect_tx(fb, kStageBytes);
+                    tma_load_2d(a_dst, &tm_a, fb, kb * kBK, mb * kBM);
+                    tma_load_2d(b_dst, &tm_b, fb, kb * kBK, row0);
+                    tma_load_2d(b_dst + kBBytes / 2, &tm_b, fb, kb * kBK, row1);
+                    if (++stage == kStages) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (!ok) {
+                // Unwind: let every load this thread issued land before the CTA exits (bounded).
+                for (int s = 0; s < kStages; ++s) {
+                    const uint64_t t0 = globaltimer();
+                    while (!mbar_try_wait(bar_full + 8 * s, phase ^ (s < stage ? 0u : 1u)) &&
+                           globaltimer() - t0 < PM_WAIT_TIMEOUT_NS) {
+                    }
+                }
+            }
+        }
+      } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                for (int kb = 0; kb < KB; ++kb, ++it) {
+                    const uint32_t buf = it & 1u, use = it >> 1;
+                    if (!mbar_wait(bar_tempty + 8 * buf, (use & 1u) ^ 1u, abort)) { ok = false; break; }
+                    if (!mbar_wait(bar_full + 8 * stage, phase, abort)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = sbase + stage * kStageBytes;
+                    const uint64_t da = desc_kmajor_sw128(a_addr);
+                    const uint64_t db = desc_kmajor_sw128(a_addr + kABytes);
+                    const uint32_t d_tmem = tmem_base + buf * kBN;
+#pragma unroll
+                    for (int k = 0; k < kBK / 32; ++k)  // 32 e4m3 (32 bytes) of K per instruction
+                        mma_f8f6f4(d_tmem, da + 2 * k, db + 2 * k, kIdesc, k > 0 ? 1u : 0u);
+                    mma_commit(bar_empty + 8 * stage);
+                    mma_commit(bar_tfull + 8 * buf);
+                    if (++stage == kStages) { stage = 0; phase ^= 1u; }
+                }
+            }
+            // Every MMA this thread issued completes before TMEM is released.
+            mma_commit(smem_u32(&tail->drain));
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try_wait(smem_u32(&tail->drain), 0) && globaltimer() - t0 < PM_WAIT_TIMEOUT_NS) {
+            }
+        }
+      }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
+        // ------------------------------------------------------------------ promotion + epilogue
+        const int q = warp & 3;                    // TMEM lane quarter
+        const int half = (warp - kEpiWarp0) >> 2;  // column half
+        const int row = q * 32 + lane;
+        const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
+        const int nb_total = args.n_total / 128;
+        uint32_t it = 0;
+        int local = 0;
+        float acc[128];
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+            const int mb = tile / args.n_tiles, nt = tile % args.n_tiles;
+            const int e = args.expert_ids[mb];
+            const int grow = mb * kBM + row;
+            const float* bs = args.b_scale + (size_t)e * nb_total * KB;
+            const float* as = args.a_scale + (size_t)grow * KB;
+#pragma unroll
+            for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+            bool ok = true;
+            for (int kb = 0; kb < KB; ++kb, ++it) {
+                const uint32_t buf = it & 1u, use = it >> 1;
+                const float sa = as[kb];
+                float s0, s1;
+                if (MODE == 0) {
+                    s0 = sa * bs[(size_t)nt * KB + kb];
+                    s1 = sa * bs[(size_t)(args.inter / 128 + nt) * KB + kb];
+                } else {
+                    s0 = sa * bs[(size_t)(nt * 2 + half) * KB + kb];
+                    s1 = s0;
+                }
+                if (!mbar_wait(bar_tfull + 8 * buf, use & 1u, abort)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t tb = t_lane + buf * kBN;
+                if (MODE == 0) {
+                    // gate columns [64*half, 64*half+64) and up columns [128+64*half, ...+64) of the tile
+                    promote32(tb + 64 * half, s0, acc);
+                    promote32(tb + 64 * half + 32, s0, acc + 32);
+                    promote32(tb + 128 + 64 * half, s1, acc + 64);
+                    promote32(tb + 128 + 64 * half + 32, s1, acc + 96);
+                } else {
+                    promote32(tb + 128 * half, s0, acc);
+                    promote32(tb + 128 * half + 32, s0, acc + 32);
+                    promote32(tb + 128 * half + 64, s0, acc + 64);
+                    promote32(tb + 128 * half + 96, s0, acc + 96);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar_tempty + 8 * buf);
+            }
+            if (!ok) break;
+
+            if (MODE == 0) {
+                // bf16(gate), bf16(up) -> silu(gate) * up in bf16 -> e4m3 with one scale per 128 columns.
+                float amax = 0.0f;
+#pragma unroll
+                for (int c = 0; c < 64; ++c) {
+                    const float y = silu_mul(bf16_round(acc[c]), bf16_round(acc[64 + c]));
+                    acc[c] = y;
+                    amax = fmaxf(amax, fabsf(y));
+                }
+                // The other column half of this row lives in another warp: exchange the half maxima through
+                // shared memory, synchronised by an mbarrier (a bounded wait, unlike a named barrier).
+                tail->amax_x[local & 1][half][row] = amax;
+                const uint32_t xb = smem_u32(&tail->xbar[local & 1]);
+                mbar_arrive(xb);
+                if (!mbar_wait(xb, (uint32_t)(local >> 1) & 1u, abort)) break;
+                amax = fmaxf(tail->amax_x[local & 1][0][row], tail->amax_x[local & 1][1][row]);
+                const float sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
+                uint32_t packed[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float q0 = fminf(fmaxf(__fdiv_rn(acc[4 * i + 0], sc), -448.0f), 448.0f);
+                    const float q1 = fminf(fmaxf(__fdiv_rn(acc[4 * i + 1], sc), -448.0f), 448.0f);
+                    const float q2 = fminf(fmaxf(__fdiv_rn(acc[4 * i + 2], sc), -448.0f), 448.0f);
+                    const float q3 = fminf(fmaxf(__fdiv_rn(acc[4 * i + 3], sc), -448.0f), 448.0f);
+                    packed[i] = (uint32_t)e4m3x2(q0, q1) | ((uint32_t)e4m3x2(q2, q3) << 16);
+                }
+                uint4* dst = reinterpret_cast<uint4*>(args.out_q + (size_t)grow * args.inter + nt * 128 + 64 * half);
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    dst[u] = make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
+                if (half == 0) args.out_s[(size_t)grow * (args.inter / 128) + nt] = sc;
+            } else {
+                const int flat = args.sorted_ids[grow];
+                if (flat < args.n_valid) {
+                    const float w = args.topk_w[flat];
+                    const int H = args.n_total;
+                    uint4* dst = reinterpret_cast<uint4*>(args.c3 + (size_t)flat * H + nt * kBN + 128 * half);
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) {
+                        uint4 o;
+                        __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            ob[i] = __floats2bfloat162_rn(acc[8 * u + 2 * i] * w, acc[8 * u + 2 * i + 1] * w);
+                        dst[u] = o;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+    if (threadIdx.x == 0 && tail->abort && args.err != nullptr) atomicExch(args.err, 1);
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_fp8(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, const GemmArgs& args,
+                            int num_sms, cudaStream_t s) {
+    static bool configured[64][2] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !configured[dev][mode]) {
+        cudaError_t e = cudaFuncSetAttribute(mode == 0 ? moe_gemm_fp8_kernel<0> : moe_gemm_fp8_kernel<1>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+        if (e != cudaSuccess) return e;
+        configured[dev][mode] = true;
+    }
+    const int grid = args.max_tiles < num_sms ? (args.max_tiles > 0 ? args.max_tiles : 1) : num_sms;
+    if (mode == 0)
+        moe_gemm_fp8_kernel<0><<<grid, kThreads, kSmemBytes, s>>>(tm_a, tm_b, args);
+    else
+        moe_gemm_fp8_kernel<1><<<grid, kThreads, kSmemBytes, s>>>(tm_a, tm_b, args);
+    return cudaGetLastError();
+}
+
+}  // namespace pm

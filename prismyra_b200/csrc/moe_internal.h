@@ -1,0 +1,62 @@
+// Internal launch interface between the kernel translation units and the C-ABI layer (moe_capi.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace pm {
+
+constexpr int kBlockM = 128;  // rows of one GEMM tile == the alignment block of the expert permutation
+constexpr int kMaxExperts = 256;
+constexpr int kMaxTopK = 16;
+constexpr int kAlignChunk = 4096;  // flat (token, slot) indices handled by one CTA of the alignment kernels
+
+inline int cdiv(long a, long b) { return static_cast<int>((a + b - 1) / b); }
+
+// Router projection (bf16, fp32 accumulation in a fixed order per row) fused with softmax / top-k.
+cudaError_t launch_router_topk(const void* x, const void* w, int T, int H, int E, int k, void* logits, float* topk_w,
+                               int32_t* topk_ids, cudaStream_t s);
+// Softmax / top-k / renormalise from given bf16 logits.
+cudaError_t launch_topk(const void* logits, int T, int E, int k, float* topk_w, int32_t* topk_ids, cudaStream_t s);
+// Stable counting sort of the flat (token, slot) indices by expert, padded per expert to kBlockM.
+cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int32_t* sorted, int32_t* expert_ids,
+                         int32_t* num_post_pad, int32_t* expert_off, cudaStream_t s);
+// Gather x rows into expert order and quantise them to e4m3 with one fp32 scale per 128 columns.
+cudaError_t launch_permute_quant_fp8(const void* x, int H, int k, int n_valid, const int32_t* sorted,
+                                     const int32_t* num_post_pad, int max_slots, uint8_t* a_q, float* a_s,
+                                     cudaStream_t s);
+// out[t] = bf16(sum_j c3[t*k + j]) in fp32, j ascending.
+cudaError_t launch_combine(const void* c3, int T, int k, int H, void* out, cudaStream_t s);
+
+struct GemmArgs {
+    const float* a_scale;     // [rows, K/128]
+    const float* b_scale;     // [E, N_total/128, K/128]
+    const int32_t* expert_ids;   // [blocks]
+    const int32_t* num_post_pad; // [1]
+    int n_total;              // rows of one expert's weight matrix (2I for gate_up, H for down)
+    int K;                    // reduction length (H for gate_up, I for down)
+    int n_tiles;              // tiles along N
+    int max_tiles;            // upper bound of tiles (grid sizing)
+    int inter;                // I (gate_up: column offset of the up rows; width of the output)
+    // gate_up epilogue
+    uint8_t* out_q;           // [rows, I] e4m3
+    float* out_s;             // [rows, I/128]
+    // down epilogue
+    const int32_t* sorted_ids;   // [rows] flat index per row (n_valid = padding)
+    const float* topk_w;      // [n_valid]
+    __nv_bfloat16* c3;        // [n_valid, H]
+    int n_valid;
+    int* err;                 // set to 1 when a wait timed out
+};
+
+cudaError_t launch_gemm_fp8(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, const GemmArgs& args,
+                            int num_sms, cudaStream_t s);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+bool encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                       uint32_t box_inner, uint32_t box_outer);
+
+}  // namespace pm

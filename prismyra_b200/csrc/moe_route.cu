@@ -1,0 +1,325 @@
+// Routing stage of the routed-expert layer: router projection, softmax / top-k / renormalise, and the stable
+// expert alignment of the flat (token, slot) indices.
+//
+// Reference behaviour (restated here, see the oracle for the executable statement):
+//   router  prismyra/kernels/qwen3_moe.py:169-171 (_route: bf16 x . W^T, fp32 accumulation, bf16 logits)
+//   top-k   prismyra/kernels/qwen3_moe.py:196 -> vLLM fused_topk(renormalize=True): fp32 softmax over the experts,
+//           the k largest (equal values: lower expert index first), divided by their sum
+//   align   prismyra/kernels/qwen3_moe.py:197 -> vLLM moe_align_block_size: flat indices grouped by expert in
+//           ascending order, each expert padded to a multiple of the block with the value T*k
+#include <math.h>
+
+#include "moe_internal.h"
+#include "ptx.cuh"
+
+namespace pm {
+namespace {
+
+constexpr int kMaxEPT = kMaxExperts / 32;  // logits held per lane
+
+// One warp ranks one token.  v[i] holds the logit of expert lane + 32 i (or -inf past E).
+__device__ __forceinline__ void warp_topk(const float (&v)[kMaxEPT], int E, int k, float* w_out, int32_t* id_out) {
+    const int lane = threadIdx.x & 31;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kMaxEPT; ++i) mx = fmaxf(mx, v[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float ex[kMaxEPT];
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kMaxEPT; ++i) {
+        ex[i] = (lane + 32 * i < E) ? expf(v[i] - mx) : 0.0f;
+        sum += ex[i];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+
+    uint32_t used = 0;
+    float sel = 0.0f, my_p = 0.0f;
+    int my_id = 0;
+    for (int j = 0; j < k; ++j) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < kMaxEPT; ++i) {
+            const int e = lane + 32 * i;
+            if (e < E && !((used >> i) & 1u) && (v[i] > bv || bi == 0x7fffffff)) {
+                bv = v[i];
+                bi = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        float mine = 0.0f;
+        if ((bi & 31) == lane) {
+            const int slot = bi >> 5;
+            used |= 1u << slot;
+#pragma unroll
+            for (int i = 0; i < kMaxEPT; ++i)
+                if (i == slot) mine = ex[i];
+        }
+        const float p = __shfl_sync(0xffffffffu, mine, bi & 31) / sum;
+        sel += p;
+        if (lane == j) {
+            my_p = p;
+            my_id = bi;
+        }
+    }
+    if (lane < k) {
+        w_out[lane] = my_p / sel;
+        id_out[lane] = my_id;
+    }
+}
+
+__global__ void __launch_bounds__(256) topk_kernel(const __nv_bfloat16* __restrict__ logits, int T, int E, int k,
+                                                   float* __restrict__ topk_w, int32_t* __restrict__ topk_ids) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= T) return;
+    float v[kMaxEPT];
+#pragma unroll
+    for (int i = 0; i < kMaxEPT; ++i) {
+        const int e = lane + 32 * i;
+        v[i] = e < E ? __bfloat162float(logits[(size_t)warp * E + e]) : -INFINITY;
+    }
+    warp_topk(v, E, k, topk_w + (size_t)warp * k, topk_ids + (size_t)warp * k);
+}
+
+// Router projection on CUDA cores: a CTA computes 32 tokens x all experts with every output reduced over H in
+// ascending order (a row's logits never depend on which other rows share the call), rounds to bf16, then ranks
+// its 32 tokens with one warp per token.
+constexpr int kRTM = 32;   // tokens per CTA
+constexpr int kRKC = 64;   // H chunk
+constexpr int kRPad = 4;
+
+__global__ void __launch_bounds__(256) router_topk_kernel(const __nv_bfloat16* __restrict__ x,
+                                                          const __nv_bfloat16* __restrict__ w, int T, int H, int E,
+                                                          int k, __nv_bfloat16* __restrict__ logits,
+                                                          float* __restrict__ topk_w,
+                                                          int32_t* __restrict__ topk_ids) {
+    extern __shared__ float rsm[];
+    float* xs = rsm;                              // [kRTM][kRKC + kRPad]
+    float* ws = rsm + kRTM * (kRKC + kRPad);      // [E][kRKC + kRPad]
+    const int tid = threadIdx.x, ty = tid >> 5, tx = tid & 31;
+    const int t0 = blockIdx.x * kRTM;
+    float acc[4][kMaxEPT];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int j = 0; j < kMaxEPT; ++j) acc[r][j] = 0.0f;
+
+    for (int h0 = 0; h0 < H; h0 += kRKC) {
+        {   // 32 x 64 activations: one 16-byte load per thread
+            const int r = tid >> 3, c = (tid & 7) * 8;
+            uint4 u = make_uint4(0, 0, 0, 0);
+            if (t0 + r < T) u = *reinterpret_cast<const uint4*>(x + (size_t)(t0 + r) * H + h0 + c);
+            const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+            float* d = xs + r * (kRKC + kRPad) + c;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) d[i] = __bfloat162float(b[i]);
+        }
+        for (int q = tid; q < E * 8; q += 256) {
+            const int r = q >> 3, c = (q & 7) * 8;
+            const uint4 u = *reinterpret_cast<const uint4*>(w + (size_t)r * H + h0 + c);
+            const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+            float* d = ws + r * (kRKC + kRPad) + c;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) d[i] = __bfloat162float(b[i]);
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int kk = 0; kk < kRKC; kk += 4) {
+            float4 xv[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+                xv[r] = *reinterpret_cast<const float4*>(xs + (ty * 4 + r) * (kRKC + kRPad) + kk);
+#pragma unroll
+            for (int j = 0; j < kMaxEPT; ++j) {
+                const int e = tx + 32 * j;
+                if (e < E) {
+                    const float4 wv = *reinterpret_cast<const float4*>(ws + e * (kRKC + kRPad) + kk);
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        float a = acc[r][j];
+                        a = fmaf(xv[r].x, wv.x, a);
+                        a = fmaf(xv[r].y, wv.y, a);
+                        a = fmaf(xv[r].z, wv.z, a);
+                        a = fmaf(xv[r].w, wv.w, a);
+                        acc[r][j] = a;
+                    }
+                }
+            }
+        }
+        __syncthreads();
+    }
+    // bf16 logits into shared memory (and global when asked), then rank.
+    float* lg = rsm;  // [kRTM][E]
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int j = 0; j < kMaxEPT; ++j) {
+            const int e = tx + 32 * j, t = ty * 4 + r;
+            if (e < E) {
+                const __nv_bfloat16 b = __float2bfloat16_rn(acc[r][j]);
+                lg[t * E + e] = __bfloat162float(b);
+                if (logits != nullptr && t0 + t < T) logits[(size_t)(t0 + t) * E + e] = b;
+            }
+        }
+    __syncthreads();
+    for (int r = 0; r < 4; ++r) {
+        const int t = ty * 4 + r;
+        if (t0 + t >= T) break;
+        float v[kMaxEPT];
+#pragma unroll
+        for (int i = 0; i < kMaxEPT; ++i) {
+            const int e = tx + 32 * i;
+            v[i] = e < E ? lg[t * E + e] : -INFINITY;
+        }
+        warp_topk(v, E, k, topk_w + (size_t)(t0 + t) * k, topk_ids + (size_t)(t0 + t) * k);
+    }
+}
+
+// ------------------------------------------------------------------------------------------- alignment
+// Pass 1: per-chunk expert histogram.
+__global__ void __launch_bounds__(256) align_count_kernel(const int32_t* __restrict__ ids, int n, int E,
+                                                          int32_t* __restrict__ counts) {
+    extern __shared__ int32_t cnt[];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    const int lo = blockIdx.x * kAlignChunk, hi = min(n, lo + kAlignChunk);
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const int e = ids[i];
+        if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) counts[(size_t)blockIdx.x * E + e] = cnt[e];
+}
+
+// Pass 2 (one CTA, one thread per expert): expert totals, padded offsets, per-chunk bases, block -> expert
+// table, padding slots and the padded total.
+__global__ void __launch_bounds__(1024) align_scan_kernel(int32_t* __restrict__ counts, int nchunks, int n, int E,
+                                                          int32_t* __restrict__ sorted,
+                                                          int32_t* __restrict__ expert_ids,
+                                                          int32_t* __restrict__ num_post_pad,
+                                                          int32_t* __restrict__ expert_off) {
+    __shared__ int32_t scan[1024];
+    const int e = threadIdx.x;
+    int total = 0;
+    if (e < E)
+        for (int c = 0; c < nchunks; ++c) {
+            const int v = counts[(size_t)c * E + e];
+            counts[(size_t)c * E + e] = total;  // exclusive prefix over chunks, relative to the expert's start
+            total += v;
+        }
+    const int padded = (total + kBlockM - 1) / kBlockM * kBlockM;
+    scan[e] = (e < E) ? padded : 0;
+    __syncthreads();
+    for (int o = 1; o < 1024; o <<= 1) {  // inclusive Hillis-Steele scan
+        const int v = (e >= o) ? scan[e - o] : 0;
+        __syncthreads();
+        scan[e] += v;
+        __syncthreads();
+    }
+    const int off = scan[e] - ((e < E) ? padded : 0);
+    if (e < E) {
+        for (int c = 0; c < nchunks; ++c) counts[(size_t)c * E + e] += off;
+        for (int b = off / kBlockM; b < (off + padded) / kBlockM; ++b) expert_ids[b] = e;
+        for (int i = off + total; i < off + padded; ++i) sorted[i] = n;
+        if (expert_off != nullptr) {
+            expert_off[e] = off;
+            if (e == E - 1) expert_off[E] = off + padded;
+        }
+    }
+    if (e == 1023) *num_post_pad = scan[1023];
+}
+
+// Pass 3: scatter each chunk's indices to their slots.  Ranks are stable: within a round of 256 indices,
+// equal experts are ordered by warp (via per-warp counts) and by lane (via the match mask).
+__global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __restrict__ ids, int n, int E,
+                                                            const int32_t* __restrict__ bases,
+                                                            int32_t* __restrict__ sorted) {
+    extern __shared__ int32_t sm[];
+    int32_t* base = sm;            // [E]
+    int32_t* wcnt = sm + E;        // [8][E]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int e = tid; e < E; e += 256) base[e] = bases[(size_t)blockIdx.x * E + e];
+    const int lo = blockIdx.x * kAlignChunk, hi = min(n, lo + kAlignChunk);
+    for (int r0 = lo; r0 < hi; r0 += 256) {
+        for (int q = tid; q < 8 * E; q += 256) wcnt[q] = 0;
+        __syncthreads();
+        const int i = r0 + tid;
+        const int e = (i < hi) ? ids[i] : -1 - lane;  // distinct sentinels keep idle lanes apart
+        const uint32_t peers = __match_any_sync(0xffffffffu, e);
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        const bool valid = (i < hi) && e >= 0 && e < E;
+        if (valid && rank == 0) wcnt[warp * E + e] = __popc(peers);
+        __syncthreads();
+        if (valid) {
+            int pos = base[e] + rank;
+            for (int w = 0; w < warp; ++w) pos += wcnt[w * E + e];
+            sorted[pos] = i;
+        }
+        __syncthreads();
+        for (int q = tid; q < E; q += 256) {
+            int s = 0;
+            for (int w = 0; w < 8; ++w) s += wcnt[w * E + q];
+            base[q] += s;
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_topk(const void* logits, int T, int E, int k, float* topk_w, int32_t* topk_ids, cudaStream_t s) {
+    if (T == 0) return cudaSuccess;
+    const int blocks = cdiv((long)T * 32, 256);
+    topk_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(logits), T, E, k, topk_w, topk_ids);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_router_topk(const void* x, const void* w, int T, int H, int E, int k, void* logits, float* topk_w,
+                               int32_t* topk_ids, cudaStream_t s) {
+    if (T == 0) return cudaSuccess;
+    size_t smem = sizeof(float) * (size_t)(kRTM + E) * (kRKC + kRPad);
+    const size_t need_lg = sizeof(float) * (size_t)kRTM * E;
+    if (need_lg > smem) smem = need_lg;
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(router_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)(sizeof(float) * (kRTM + kMaxExperts) * (kRKC + kRPad)));
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    router_topk_kernel<<<cdiv(T, kRTM), 256, smem, s>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), T, H, E, k,
+        static_cast<__nv_bfloat16*>(logits), topk_w, topk_ids);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int32_t* sorted, int32_t* expert_ids,
+                         int32_t* num_post_pad, int32_t* expert_off, cudaStream_t s) {
+    const int nchunks = n > 0 ? cdiv(n, kAlignChunk) : 0;
+    if (nchunks > 0) {
+        align_count_kernel<<<nchunks, 256, sizeof(int32_t) * E, s>>>(ids, n, E, counts);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    align_scan_kernel<<<1, 1024, 0, s>>>(counts, nchunks, n, E, sorted, expert_ids, num_post_pad, expert_off);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || nchunks == 0) return e;
+    align_scatter_kernel<<<nchunks, 256, sizeof(int32_t) * 9 * E, s>>>(ids, n, E, counts, sorted);
+    return cudaGetLastError();
+}
+
+}  // namespace pm

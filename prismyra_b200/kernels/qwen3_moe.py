@@ -1,0 +1,134 @@
+"""The routed-expert layer of Qwen3.5/3.6-MoE checkpoints on B200 kernels, and its adapter.
+
+``FusedExperts`` is a drop-in for the reference's module of the same name (prismyra/kernels/qwen3_moe.py:
+142-199): it is built from the framework's ``Qwen3_5MoeSparseMoeBlock`` and ``top_k``, exposes ``gate``,
+``shared_expert``, ``shared_expert_gate``, ``top_k``, ``w1`` and ``w2``, and its ``forward`` maps bf16
+``[..., H]`` to bf16 of the same shape.  The routed path (router projection, softmax / top-k, expert alignment,
+both grouped FP8 GEMMs with silu-and-mul between them, and the weighted top-k sum) runs in
+``libprismyra_moe.so``; the shared expert and its gate stay the framework's own modules, as in the reference.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from .. import ops
+from . import AdapterError, Applied, Swap, register
+
+BLOCK = (128, 128)
+
+#: Shapes the B200 kernels accept (include/prismyra_moe.h).
+LIMITS = {"max_experts": 256, "max_top_k": 16, "hidden_multiple": 256, "intermediate_multiple": 128}
+
+
+def _fp8_expert_tensors(experts: nn.Module):
+    """(w1, w1_scale, w2, w2_scale) from a framework experts module holding 128x128 block-FP8 weights, or None.
+    ``*_scale_inv`` is the multiplier that restores a stored value (reference qwen3_moe.py:158-161)."""
+    w1 = getattr(experts, "gate_up_proj", None)
+    w2 = getattr(experts, "down_proj", None)
+    s1 = getattr(experts, "gate_up_proj_scale_inv", None)
+    s2 = getattr(experts, "down_proj_scale_inv", None)
+    if any(t is None for t in (w1, w2, s1, s2)):
+        return None
+    if w1.dtype != torch.float8_e4m3fn or w2.dtype != torch.float8_e4m3fn:
+        return None
+    return w1, s1, w2, s2
+
+
+class FusedExperts(nn.Module):
+    """Routed experts through the B200 kernels; router and shared expert kept as in the framework block."""
+
+    def __init__(self, block: nn.Module, top_k: int):
+        super().__init__()
+        tensors = _fp8_expert_tensors(block.experts)
+        if tensors is None:
+            raise AdapterError("FusedExperts needs 128x128 block-FP8 expert weights (gate_up_proj[_scale_inv], "
+                               "down_proj[_scale_inv])")
+        w1, s1, w2, s2 = tensors
+        self.gate = block.gate
+        self.shared_expert = block.shared_expert
+        self.shared_expert_gate = block.shared_expert_gate
+        self.top_k = int(top_k)
+        self.w1 = w1.detach().contiguous()
+        self.w2 = w2.detach().contiguous()
+        self.w1_scale = s1.detach().to(torch.float32).contiguous()
+        self.w2_scale = s2.detach().to(torch.float32).contiguous()
+        E, I2, H = self.w1.shape
+        self.num_experts, self.hidden, self.inter = E, H, I2 // 2
+        if (E > LIMITS["max_experts"] or self.top_k > min(LIMITS["max_top_k"], E)
+                or H % LIMITS["hidden_multiple"] or self.inter % LIMITS["intermediate_multiple"]):
+            raise AdapterError(f"shape outside the kernel's range: E={E} k={self.top_k} H={H} I={self.inter}")
+
+    def _route(self, x: torch.Tensor) -> torch.Tensor:
+        """Router logits (bf16 [T, E]), row-count invariant: each logit is reduced over H in a fixed order."""
+        logits, _, _ = ops.router_topk(x.contiguous(), self.gate.weight.contiguous(), self.top_k)
+        return logits
+
+    def routed(self, x: torch.Tensor, logits: torch.Tensor | None = None) -> torch.Tensor:
+        """The routed-expert output for x [T, H] (no shared expert)."""
+        return ops.forward_fp8(x.contiguous(), self.w1, self.w1_scale, self.w2, self.w2_scale, self.top_k,
+                               router_w=None if logits is not None else self.gate.weight.contiguous(),
+                               logits=logits)
+
+    def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        shape = hidden_states.shape
+        x = hidden_states.reshape(-1, shape[-1])
+        routed = self.routed(x)
+        shared = torch.sigmoid(F.linear(x, self.shared_expert_gate.weight)) * self.shared_expert(x)
+        return (routed + shared).reshape(shape)
+
+
+def _swap_children(root: nn.Module, class_name: str, make) -> int:
+    count = 0
+    for parent in list(root.modules()):
+        for name, child in list(parent.named_children()):
+            if type(child).__name__ == class_name:
+                setattr(parent, name, make(child))
+                count += 1
+    return count
+
+
+class Qwen3MoeAdapter:
+    """Installs ``FusedExperts`` into Qwen3.5/3.6-MoE models whose per-layer shape the kernels accept."""
+
+    name = "qwen3-moe-b200"
+
+    def supports(self, config) -> bool:
+        names = getattr(config, "architectures", None) or []
+        if not any("Qwen3_5Moe" in n for n in names):
+            return False
+        d = getattr(config, "text_config", config)
+        E = getattr(d, "num_experts", 0) or 0
+        k = getattr(d, "num_experts_per_tok", 0) or 0
+        H = getattr(d, "hidden_size", 0) or 0
+        I = getattr(d, "moe_intermediate_size", 0) or 0
+        return (0 < k <= min(E, LIMITS["max_top_k"]) and E <= LIMITS["max_experts"] and H > 0
+                and H % LIMITS["hidden_multiple"] == 0 and I > 0 and I % LIMITS["intermediate_multiple"] == 0)
+
+    def replace(self, model: nn.Module, config) -> Applied:
+        d = getattr(config, "text_config", config)
+        applied = Applied(adapter=self.name)
+        text = getattr(model, "language_model", model)
+        if text is not model:
+            applied.notes.append("replacements were applied to the text decoder; the vision tower is untouched")
+        already = sum(1 for m in text.modules() if type(m).__name__ in ("FusedExperts", "FusedExpertsFp4"))
+        if already:
+            applied.swaps.append(Swap("routed_experts", already, d.num_hidden_layers))
+            return applied
+        blocks = [m for m in text.modules() if type(m).__name__ == "Qwen3_5MoeSparseMoeBlock"]
+        if blocks and _fp8_expert_tensors(blocks[0].experts) is None:
+            applied.skipped.append("routed experts are not 128x128 block-FP8 (the B200 FP8 kernels need them)")
+            return applied
+        if not torch.cuda.is_available():
+            applied.skipped.append("no CUDA device: the B200 kernels need one")
+            return applied
+        n = _swap_children(text, "Qwen3_5MoeSparseMoeBlock", lambda m: FusedExperts(m, d.num_experts_per_tok))
+        applied.swaps.append(Swap("routed_experts", n, d.num_hidden_layers))
+        applied.notes.append("only the routed experts are replaced; attention, norms and dense projections keep "
+                             "the framework's modules")
+        return applied
+
+
+register(Qwen3MoeAdapter())

@@ -1,0 +1,208 @@
+"""Torch-facing calls into the C ABI: tensors in, tensors out, on the caller's current CUDA stream.
+
+PyTorch is used for device memory and streams only; all arithmetic runs in ``libprismyra_moe.so``.  Each
+function checks dtypes, shapes and devices before calling, so a wrong argument raises here rather than
+inside a kernel.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+
+FP8 = torch.float8_e4m3fn
+_NULL = None
+
+
+def _p(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(dev: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _need(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def _cuda(t: torch.Tensor, name: str, dtype, shape=None) -> None:
+    _need(t.is_cuda, f"{name} must be a CUDA tensor")
+    if isinstance(dtype, tuple):
+        _need(t.dtype in dtype, f"{name} must have dtype in {dtype}, got {t.dtype}")
+    else:
+        _need(t.dtype == dtype, f"{name} must be {dtype}, got {t.dtype}")
+    _need(t.is_contiguous(), f"{name} must be contiguous")
+    if shape is not None:
+        _need(tuple(t.shape) == tuple(shape), f"{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
+
+
+def _u8(t: torch.Tensor) -> torch.Tensor:
+    return t.view(torch.uint8) if t.dtype != torch.uint8 else t
+
+
+# ------------------------------------------------------------------------------------------- workspace
+class WorkspacePool:
+    """One scratch buffer per (device, calling thread, format), grown to the largest token count seen and never
+    released.  A CUDA graph captured over a forward keeps the buffer's address, so a superseded buffer stays
+    referenced for the life of the process instead of being returned to the allocator -- the same policy as the
+    reference's per-thread NVFP4 workspace (prismyra/kernels/nvfp4.py:213-245)."""
+
+    def __init__(self):
+        self._bufs: dict = {}
+        self._retired: list = []
+        self._lock = threading.Lock()
+
+    def get(self, device: torch.device, nbytes: int, fmt: int) -> torch.Tensor:
+        key = (device.index, threading.get_ident(), fmt)
+        with self._lock:
+            buf = self._bufs.get(key)
+            if buf is None or buf.numel() < nbytes:
+                if buf is not None:
+                    self._retired.append(buf)
+                buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+                self._bufs[key] = buf
+            return buf
+
+
+POOL = WorkspacePool()
+
+
+def workspace_for(x: torch.Tensor, T: int, H: int, I: int, E: int, k: int, fmt: int = _lib.FMT_FP8):
+    n = _lib.workspace_bytes(T, H, I, E, k, fmt)
+    _need(n > 0, f"unsupported MoE shape T={T} H={H} I={I} E={E} k={k}")
+    return POOL.get(x.device, n, fmt), n
+
+
+def region(ws: torch.Tensor, T, H, I, E, k, fmt, name: str, dtype, shape) -> torch.Tensor:
+    """A typed view of one workspace region (for inspection of intermediates)."""
+    off, n = _lib.workspace_region(T, H, I, E, k, fmt, name)
+    numel = 1
+    for s in shape:
+        numel *= s
+    elem = torch.tensor([], dtype=dtype).element_size()
+    _need(numel * elem <= n, f"region {name} holds {n} bytes, asked for {numel * elem}")
+    return ws[off: off + numel * elem].view(dtype).view(*shape)
+
+
+# ------------------------------------------------------------------------------------------- the layer
+def forward_fp8(x: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch.Tensor, w2_s: torch.Tensor,
+                top_k: int, router_w: torch.Tensor | None = None, logits: torch.Tensor | None = None,
+                out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed FP8 experts for x [T, H] bf16; give ``router_w`` [E, H] bf16 or ``logits`` [T, E] bf16."""
+    _need(x.dim() == 2, "x must be [T, H]")
+    T, H = x.shape
+    E, I2, H1 = w1.shape
+    I = I2 // 2
+    _cuda(x, "x", torch.bfloat16)
+    _cuda(w1, "w1", (FP8, torch.uint8), (E, 2 * I, H))
+    _cuda(w2, "w2", (FP8, torch.uint8), (E, H, I))
+    _cuda(w1_s, "w1_s", torch.float32, (E, 2 * I // 128, H // 128))
+    _cuda(w2_s, "w2_s", torch.float32, (E, H // 128, I // 128))
+    _need(router_w is not None or logits is not None, "give router_w or logits")
+    if logits is not None:
+        _cuda(logits, "logits", torch.bfloat16, (T, E))
+    else:
+        _cuda(router_w, "router_w", torch.bfloat16, (E, H))
+    if out is None:
+        out = torch.empty_like(x)
+    _cuda(out, "out", torch.bfloat16, (T, H))
+    if T == 0:
+        return out
+    if workspace is None:
+        workspace, nbytes = workspace_for(x, T, H, I, E, top_k, _lib.FMT_FP8)
+    else:
+        nbytes = workspace.numel()
+    _lib.call(
+        "pm_moe_forward_fp8", _p(x), _p(router_w), _p(logits), _p(_u8(w1)), _p(w1_s), _p(_u8(w2)), _p(w2_s),
+        T, H, I, E, top_k, _p(out), _p(workspace), nbytes, _stream(x.device),
+    )
+    return out
+
+
+def read_status(workspace: torch.Tensor) -> None:
+    """Synchronise and raise if a kernel of the last forward on this workspace gave up on a bounded wait."""
+    _lib.call("pm_moe_read_status", _p(workspace), _stream(workspace.device))
+
+
+# ------------------------------------------------------------------------------------------- stages
+def router_topk(x: torch.Tensor, router_w: torch.Tensor, k: int):
+    T, H = x.shape
+    E = router_w.shape[0]
+    _cuda(x, "x", torch.bfloat16)
+    _cuda(router_w, "router_w", torch.bfloat16, (E, H))
+    logits = torch.empty(T, E, dtype=torch.bfloat16, device=x.device)
+    w = torch.empty(T, k, dtype=torch.float32, device=x.device)
+    ids = torch.empty(T, k, dtype=torch.int32, device=x.device)
+    _lib.call("pm_moe_router_topk", _p(x), _p(router_w), T, H, E, k, _p(logits), _p(w), _p(ids),
+              _stream(x.device))
+    return logits, w, ids
+
+
+def topk(logits: torch.Tensor, k: int):
+    T, E = logits.shape
+    _cuda(logits, "logits", torch.bfloat16)
+    w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+    ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+    _lib.call("pm_moe_topk", _p(logits), T, E, k, _p(w), _p(ids), _stream(logits.device))
+    return w, ids
+
+
+def align(ids: torch.Tensor, E: int):
+    """-> sorted_ids [max_slots], expert_ids [max_slots/128], num_post_pad [1], expert_off [E+1]."""
+    _cuda(ids, "ids", torch.int32)
+    T, k = ids.shape
+    ms = _lib.max_slots(T, E, k)
+    dev = ids.device
+    sorted_ids = torch.full((ms,), -1, dtype=torch.int32, device=dev)
+    expert_ids = torch.full((ms // 128,), -1, dtype=torch.int32, device=dev)
+    npp = torch.zeros(1, dtype=torch.int32, device=dev)
+    off = torch.zeros(E + 1, dtype=torch.int32, device=dev)
+    scratch = torch.zeros(max(1, -(-T * k // 4096)) * E, dtype=torch.int32, device=dev)
+    _lib.call("pm_moe_align", _p(ids), T, k, E, _p(sorted_ids), _p(expert_ids), _p(npp), _p(off), _p(scratch),
+              scratch.numel() * 4, _stream(dev))
+    return sorted_ids, expert_ids, npp, off
+
+
+def permute_quant_fp8(x: torch.Tensor, sorted_ids: torch.Tensor, npp: torch.Tensor, k: int):
+    T, H = x.shape
+    ms = sorted_ids.numel()
+    a_q = torch.zeros(ms, H, dtype=torch.uint8, device=x.device)
+    a_s = torch.zeros(ms, H // 128, dtype=torch.float32, device=x.device)
+    _lib.call("pm_moe_permute_quant_fp8", _p(x), T, H, k, _p(sorted_ids), _p(npp), ms, _p(a_q), _p(a_s),
+              _stream(x.device))
+    return a_q, a_s
+
+
+def gemm1_fp8(a_q, a_s, w1, w1_s, expert_ids, npp):
+    ms, H = a_q.shape
+    E, I2, _ = w1.shape
+    I = I2 // 2
+    out_q = torch.zeros(ms, I, dtype=torch.uint8, device=a_q.device)
+    out_s = torch.zeros(ms, I // 128, dtype=torch.float32, device=a_q.device)
+    err = torch.zeros(1, dtype=torch.int32, device=a_q.device)
+    _lib.call("pm_moe_gemm1_fp8", _p(a_q), _p(a_s), _p(_u8(w1)), _p(w1_s), _p(expert_ids), _p(npp), ms, H, I, E,
+              _p(out_q), _p(out_s), _p(err), _stream(a_q.device))
+    return out_q, out_s, err
+
+
+def gemm2_fp8(a_q, a_s, w2, w2_s, expert_ids, npp, sorted_ids, topk_w, T: int, k: int):
+    ms, I = a_q.shape
+    E, H, _ = w2.shape
+    c3 = torch.zeros(T * k, H, dtype=torch.bfloat16, device=a_q.device)
+    err = torch.zeros(1, dtype=torch.int32, device=a_q.device)
+    _lib.call("pm_moe_gemm2_fp8", _p(a_q), _p(a_s), _p(_u8(w2)), _p(w2_s), _p(expert_ids), _p(npp),
+              _p(sorted_ids), _p(topk_w), ms, T, k, H, I, E, _p(c3), _p(err), _stream(a_q.device))
+    return c3, err
+
+
+def combine(c3: torch.Tensor, T: int, k: int):
+    H = c3.shape[1]
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=c3.device)
+    _lib.call("pm_moe_combine", _p(c3), T, k, H, _p(out), _stream(c3.device))
+    return out
