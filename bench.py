@@ -58,53 +58,74 @@ def dist_init():
 
 
 class Clocks:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """nvidia-smi sampling of SM clocks and throttle reasons, running from before the warm-up until after the
+    timed region; summary() keeps the samples taken inside [mark_start, mark_end] (host time), or the nearest
+    one when the timed region is shorter than the sampling interval."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.rows: list = []
+        self.t0 = self.t1 = None
 
-    def __enter__(self):
+    def _reader(self):
+        for ln in self.proc.stdout:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) >= 7:
+                try:
+                    self.rows.append((time.time(), float(f[0]), float(f[1]), float(f[2]), f[3:7]))
+                except ValueError:
+                    pass
+
+    def start(self):
+        import threading
+
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
+            return self
+        threading.Thread(target=self._reader, daemon=True).start()
+        t = time.time()
+        while not self.rows and time.time() - t < 10:
+            time.sleep(0.02)
         return self
 
-    def __exit__(self, *a):
-        self.lines = []
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+        t = time.time()
+        while self.proc is not None and not any(r[0] > self.t1 for r in self.rows) and time.time() - t < 2:
+            time.sleep(0.02)
+
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
 
     def summary(self) -> dict:
-        rows = []
-        for ln in getattr(self, "lines", []):
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                rows.append((float(f[1]), float(f[2]), float(f[3]), f[5:9]))
-            except ValueError:
-                continue
-        if not rows:
+        if not self.rows or self.t0 is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        inside = [r for r in self.rows if self.t0 - 0.05 <= r[0] <= self.t1 + 0.05]
+        if not inside:
+            mid = 0.5 * (self.t0 + self.t1)
+            inside = [min(self.rows, key=lambda r: abs(r[0] - mid))]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower().startswith("active")})
-        mhz = sorted(r[0] for r in rows)
-        return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(r[2] for r in rows)}
+        reasons = sorted({names[i] for r in inside for i, v in enumerate(r[4]) if v.lower().startswith("active")})
+        mhz = sorted(r[1] for r in inside)
+        return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": max(r[2] for r in inside), "reasons": reasons,
+                "samples": len(inside), "power_w_max": max(r[3] for r in inside)}
 
 
 def cpu_baseline(layer_cpu: dict, min_seconds: float = 12.0) -> dict:
@@ -164,28 +185,32 @@ def time_region(fn, steps: int, stream) -> float:
     return a.elapsed_time(b) / steps
 
 
-def stage_times(layer: dict, T: int, reps: int = 10) -> dict:
-    """Per-stage device time (ms) of one forward, each stage timed alone with CUDA events."""
+def stage_times(layer: dict, T: int, reps: int = 20) -> dict:
+    """Per-stage device time (ms) of one forward, each stage re-run alone on preallocated buffers and timed with
+    CUDA events on the launching stream."""
     import torch
 
     from prismyra_b200 import ops
 
     s = torch.cuda.current_stream()
     x, rw = layer["x"][:T].contiguous(), layer["router_w"]
-    logits, w, ids = ops.router_topk(x, rw, K)
-    srt, eids, npp, _ = ops.align(ids, E)
-    a_q, a_s = ops.permute_quant_fp8(x, srt, npp, K)
-    o_q, o_s, _ = ops.gemm1_fp8(a_q, a_s, layer["w1"], layer["w1_s"], eids, npp)
-    c3, _ = ops.gemm2_fp8(o_q, o_s, layer["w2"], layer["w2_s"], eids, npp, srt, w.reshape(-1), T, K)
-    ops.combine(c3, T, K)
+    r_out = ops.router_topk(x, rw, K)
+    _, w, ids = r_out
+    a_out = ops.align(ids, E)
+    srt, eids, npp, _, _ = a_out
+    p_out = ops.permute_quant_fp8(x, srt, npp, K)
+    g1_out = ops.gemm1_fp8(*p_out, layer["w1"], layer["w1_s"], eids, npp)
+    g2_out = ops.gemm2_fp8(g1_out[0], g1_out[1], layer["w2"], layer["w2_s"], eids, npp, srt, w.reshape(-1), T, K)
+    c_out = ops.combine(g2_out[0], T, K)
     out = {
-        "router_topk": time_region(lambda: ops.router_topk(x, rw, K), reps, s),
-        "align": time_region(lambda: ops.align(ids, E), reps, s),
-        "permute_quant": time_region(lambda: ops.permute_quant_fp8(x, srt, npp, K), reps, s),
-        "gemm1": time_region(lambda: ops.gemm1_fp8(a_q, a_s, layer["w1"], layer["w1_s"], eids, npp), reps, s),
-        "gemm2": time_region(lambda: ops.gemm2_fp8(o_q, o_s, layer["w2"], layer["w2_s"], eids, npp, srt,
-                                                   w.reshape(-1), T, K), reps, s),
-        "combine": time_region(lambda: ops.combine(c3, T, K), reps, s),
+        "router_topk": time_region(lambda: ops.router_topk(x, rw, K, out=r_out), reps, s),
+        "align": time_region(lambda: ops.align(ids, E, out=a_out), reps, s),
+        "permute_quant": time_region(lambda: ops.permute_quant_fp8(x, srt, npp, K, out=p_out), reps, s),
+        "gemm1": time_region(lambda: ops.gemm1_fp8(*p_out, layer["w1"], layer["w1_s"], eids, npp, out=g1_out),
+                             reps, s),
+        "gemm2": time_region(lambda: ops.gemm2_fp8(g1_out[0], g1_out[1], layer["w2"], layer["w2_s"], eids, npp, srt,
+                                                   w.reshape(-1), T, K, out=g2_out), reps, s),
+        "combine": time_region(lambda: ops.combine(g2_out[0], T, K, out=c_out), reps, s),
     }
     out["experts_hit"] = int((torch.bincount(ids.reshape(-1).long(), minlength=E) > 0).sum().item())
     out["slots"] = int(npp.item())
@@ -208,6 +233,7 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
     def step():
         return ops.forward_fp8(x, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K, router_w=layer["router_w"])
 
+    clk = Clocks(local).start()
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
@@ -220,9 +246,12 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
         torch.cuda.synchronize()
 
     barrier()
-    with Clocks(local) as clk:
-        ms = time_region(step, args.steps, stream)
-        barrier()
+    clk.mark_start()
+    ms = time_region(step, args.steps, stream)
+    barrier()
+    clk.mark_end()
+    clk.stop()
+    ops.read_status(ws)
     if world > 1:
         t = torch.tensor([ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -306,8 +335,8 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

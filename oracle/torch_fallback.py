@@ -23,7 +23,7 @@ def build_block(router_w: torch.Tensor, w1_deq: torch.Tensor, w2_deq: torch.Tens
 
     E, I2, H = w1_deq.shape
     cfg = SimpleNamespace(num_experts=E, num_experts_per_tok=top_k, hidden_size=H, moe_intermediate_size=I2 // 2,
-                          hidden_act="silu")
+                          hidden_act="silu", _experts_implementation="eager")
     router = Qwen3_5MoeTopKRouter(cfg)
     experts = Qwen3_5MoeExperts(cfg)
     with torch.no_grad():

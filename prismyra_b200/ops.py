@@ -131,14 +131,16 @@ def read_status(workspace: torch.Tensor) -> None:
 
 
 # ------------------------------------------------------------------------------------------- stages
-def router_topk(x: torch.Tensor, router_w: torch.Tensor, k: int):
+def router_topk(x: torch.Tensor, router_w: torch.Tensor, k: int, out=None):
     T, H = x.shape
     E = router_w.shape[0]
     _cuda(x, "x", torch.bfloat16)
     _cuda(router_w, "router_w", torch.bfloat16, (E, H))
-    logits = torch.empty(T, E, dtype=torch.bfloat16, device=x.device)
-    w = torch.empty(T, k, dtype=torch.float32, device=x.device)
-    ids = torch.empty(T, k, dtype=torch.int32, device=x.device)
+    if out is None:
+        out = (torch.empty(T, E, dtype=torch.bfloat16, device=x.device),
+               torch.empty(T, k, dtype=torch.float32, device=x.device),
+               torch.empty(T, k, dtype=torch.int32, device=x.device))
+    logits, w, ids = out
     _lib.call("pm_moe_router_topk", _p(x), _p(router_w), T, H, E, k, _p(logits), _p(w), _p(ids),
               _stream(x.device))
     return logits, w, ids
@@ -153,56 +155,65 @@ def topk(logits: torch.Tensor, k: int):
     return w, ids
 
 
-def align(ids: torch.Tensor, E: int):
-    """-> sorted_ids [max_slots], expert_ids [max_slots/128], num_post_pad [1], expert_off [E+1]."""
+def align(ids: torch.Tensor, E: int, out=None):
+    """-> sorted_ids [max_slots], expert_ids [max_slots/128], num_post_pad [1], expert_off [E+1] (and the
+    per-chunk count scratch when ``out`` is given as a 5-tuple)."""
     _cuda(ids, "ids", torch.int32)
     T, k = ids.shape
     ms = _lib.max_slots(T, E, k)
     dev = ids.device
-    sorted_ids = torch.full((ms,), -1, dtype=torch.int32, device=dev)
-    expert_ids = torch.full((ms // 128,), -1, dtype=torch.int32, device=dev)
-    npp = torch.zeros(1, dtype=torch.int32, device=dev)
-    off = torch.zeros(E + 1, dtype=torch.int32, device=dev)
-    scratch = torch.zeros(max(1, -(-T * k // 4096)) * E, dtype=torch.int32, device=dev)
+    if out is None:
+        out = (torch.full((ms,), -1, dtype=torch.int32, device=dev),
+               torch.full((ms // 128,), -1, dtype=torch.int32, device=dev),
+               torch.zeros(1, dtype=torch.int32, device=dev), torch.zeros(E + 1, dtype=torch.int32, device=dev),
+               torch.zeros(max(1, -(-T * k // 4096)) * E, dtype=torch.int32, device=dev))
+    sorted_ids, expert_ids, npp, off, scratch = out
     _lib.call("pm_moe_align", _p(ids), T, k, E, _p(sorted_ids), _p(expert_ids), _p(npp), _p(off), _p(scratch),
               scratch.numel() * 4, _stream(dev))
-    return sorted_ids, expert_ids, npp, off
+    return sorted_ids, expert_ids, npp, off, scratch
 
 
-def permute_quant_fp8(x: torch.Tensor, sorted_ids: torch.Tensor, npp: torch.Tensor, k: int):
+def permute_quant_fp8(x: torch.Tensor, sorted_ids: torch.Tensor, npp: torch.Tensor, k: int, out=None):
     T, H = x.shape
     ms = sorted_ids.numel()
-    a_q = torch.zeros(ms, H, dtype=torch.uint8, device=x.device)
-    a_s = torch.zeros(ms, H // 128, dtype=torch.float32, device=x.device)
+    if out is None:
+        out = (torch.zeros(ms, H, dtype=torch.uint8, device=x.device),
+               torch.zeros(ms, H // 128, dtype=torch.float32, device=x.device))
+    a_q, a_s = out
     _lib.call("pm_moe_permute_quant_fp8", _p(x), T, H, k, _p(sorted_ids), _p(npp), ms, _p(a_q), _p(a_s),
               _stream(x.device))
     return a_q, a_s
 
 
-def gemm1_fp8(a_q, a_s, w1, w1_s, expert_ids, npp):
+def gemm1_fp8(a_q, a_s, w1, w1_s, expert_ids, npp, out=None):
     ms, H = a_q.shape
     E, I2, _ = w1.shape
     I = I2 // 2
-    out_q = torch.zeros(ms, I, dtype=torch.uint8, device=a_q.device)
-    out_s = torch.zeros(ms, I // 128, dtype=torch.float32, device=a_q.device)
-    err = torch.zeros(1, dtype=torch.int32, device=a_q.device)
+    if out is None:
+        out = (torch.zeros(ms, I, dtype=torch.uint8, device=a_q.device),
+               torch.zeros(ms, I // 128, dtype=torch.float32, device=a_q.device),
+               torch.zeros(1, dtype=torch.int32, device=a_q.device))
+    out_q, out_s, err = out
     _lib.call("pm_moe_gemm1_fp8", _p(a_q), _p(a_s), _p(_u8(w1)), _p(w1_s), _p(expert_ids), _p(npp), ms, H, I, E,
               _p(out_q), _p(out_s), _p(err), _stream(a_q.device))
     return out_q, out_s, err
 
 
-def gemm2_fp8(a_q, a_s, w2, w2_s, expert_ids, npp, sorted_ids, topk_w, T: int, k: int):
+def gemm2_fp8(a_q, a_s, w2, w2_s, expert_ids, npp, sorted_ids, topk_w, T: int, k: int, out=None):
     ms, I = a_q.shape
     E, H, _ = w2.shape
-    c3 = torch.zeros(T * k, H, dtype=torch.bfloat16, device=a_q.device)
-    err = torch.zeros(1, dtype=torch.int32, device=a_q.device)
+    if out is None:
+        out = (torch.zeros(T * k, H, dtype=torch.bfloat16, device=a_q.device),
+               torch.zeros(1, dtype=torch.int32, device=a_q.device))
+    c3, err = out
     _lib.call("pm_moe_gemm2_fp8", _p(a_q), _p(a_s), _p(_u8(w2)), _p(w2_s), _p(expert_ids), _p(npp),
               _p(sorted_ids), _p(topk_w), ms, T, k, H, I, E, _p(c3), _p(err), _stream(a_q.device))
     return c3, err
 
 
-def combine(c3: torch.Tensor, T: int, k: int):
+def combine(c3: torch.Tensor, T: int, k: int, out=None):
     H = c3.shape[1]
-    out = torch.empty(T, H, dtype=torch.bfloat16, device=c3.device)
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=c3.device)
     _lib.call("pm_moe_combine", _p(c3), T, k, H, _p(out), _stream(c3.device))
     return out

@@ -1,0 +1,40 @@
+"""Run the routed-expert layer on synthetic data a fixed number of times (for profilers and quick checks).
+
+    python -m prismyra_b200.run --tokens 5120 --iters 3 [--format fp8]
+
+Builds the seeded synthetic layer (H=2048, I=768, E=128, top-8 by default) on the current GPU, runs the forward
+``--iters`` times on the current stream and prints the output checksum and the device status.
+"""
+
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+from . import ops, synth
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--tokens", type=int, default=5120)
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--hidden", type=int, default=2048)
+    ap.add_argument("--inter", type=int, default=768)
+    ap.add_argument("--experts", type=int, default=128)
+    ap.add_argument("--top-k", type=int, default=8)
+    ap.add_argument("--seed", type=int, default=0)
+    a = ap.parse_args()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    L = synth.make_fp8_layer(a.tokens, a.hidden, a.inter, a.experts, seed=a.seed, device=dev, gen_device="cuda")
+    torch.cuda.synchronize()
+    out = None
+    for _ in range(a.iters):
+        out = ops.forward_fp8(L["x"], L["w1"], L["w1_s"], L["w2"], L["w2_s"], a.top_k, router_w=L["router_w"])
+    ws, _ = ops.workspace_for(L["x"], a.tokens, a.hidden, a.inter, a.experts, a.top_k)
+    ops.read_status(ws)
+    print(f"tokens={a.tokens} iters={a.iters} checksum={out.float().abs().sum().item():.6e} status=ok")
+
+
+if __name__ == "__main__":
+    main()
