@@ -40,7 +40,8 @@ enum pm_status {
     PM_ERR_WORKSPACE = 4, /* workspace too small */
     PM_ERR_CUDA = 5,      /* a CUDA launch or driver call failed */
     PM_ERR_DEVICE = 6,    /* the current device is not sm_100 */
-    PM_ERR_TIMEOUT = 7    /* a kernel gave up on a bounded wait (reported by pm_moe_read_status) */
+    PM_ERR_TIMEOUT = 7,   /* a kernel gave up on a bounded wait (reported by pm_moe_read_status) */
+    PM_ERR_TOO_LARGE = 8  /* beyond the fixed scratch of pm_moe_align_noalloc */
 };
 
 enum pm_format { PM_FMT_FP8 = 0, PM_FMT_NVFP4 = 1 };
@@ -127,6 +128,17 @@ int pm_moe_combine(const void *c3, int T, int k, int H, void *out, pm_stream_t s
 int pm_moe_forward_fp8(const void *x, const void *router_w, const void *logits, const uint8_t *w1,
                        const float *w1_s, const uint8_t *w2, const float *w2_s, int T, int H, int I, int E, int k,
                        void *out, void *workspace, size_t workspace_bytes, pm_stream_t stream);
+
+/* Expert alignment that allocates nothing -- no counterpart in the reference.  Same results as pm_moe_align,
+ * for callers that cannot hand the library scratch memory on demand: hosts that route every device byte through
+ * their own pool and forbid library allocations, and latency-critical loops that cannot afford the implicit
+ * device synchronisation of cudaMalloc/cudaFree.  The per-chunk count table lives in a fixed 256 KiB device array
+ * inside the library (held on every GPU that loads it until the process exits).  Limits: T*k <= 2^20 and
+ * E <= 256, else PM_ERR_TOO_LARGE.  All calls share that array: calls whose kernels overlap on the GPU (e.g. on
+ * two streams) race and must be serialised by the caller.  The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress, with that device current); make it before any stream capture begins. */
+int pm_moe_align_noalloc(const int32_t *topk_ids, int T, int k, int E, int32_t *sorted_ids, int32_t *expert_ids,
+                         int32_t *num_post_pad, int32_t *expert_off, pm_stream_t stream);
 
 /* Synchronise the stream and report PM_ERR_TIMEOUT if any kernel of the last calls on this workspace gave up
  * on a bounded wait (the flag is cleared by each pm_moe_forward_* call). */

@@ -44,6 +44,7 @@ SIGNATURES: dict[str, tuple] = {
     "pm_moe_combine": (_I, [_P, _I, _I, _I, _P, _P]),
     "pm_moe_forward_fp8": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _Z, _P]),
     "pm_moe_read_status": (_I, [_P, _P]),
+    "pm_moe_align_noalloc": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P]),
 }
 
 

@@ -155,6 +155,7 @@ const char* pm_moe_status_string(int status) {
         case PM_ERR_CUDA: return "CUDA launch or driver call failed";
         case PM_ERR_DEVICE: return "current device is not sm_100 (B200)";
         case PM_ERR_TIMEOUT: return "a kernel gave up on a bounded wait";
+        case PM_ERR_TOO_LARGE: return "beyond the no-allocation entry point's fixed scratch (T*k <= 2^20, E <= 256)";
         default: return "unknown status";
     }
 }
