@@ -17,7 +17,7 @@
 //     device current) and caches it; make that first call before any stream capture begins.
 #include <mutex>
 
-#include "../../include/prismyra_moe.h"
+#include "prismyra_moe.h"
 #include "moe_internal.h"
 
 namespace pm {

@@ -7,7 +7,7 @@
 
 #include <mutex>
 
-#include "../../include/prismyra_moe.h"
+#include "prismyra_moe.h"
 #include "moe_internal.h"
 
 namespace pm {

@@ -24,7 +24,13 @@ namespace pm {
 namespace {
 
 constexpr int kBM = 128, kBN = 256, kBK = 128;
-constexpr int kStages = 4;
+template <int MODE> struct Cfg {
+    // gate_up keeps four pipeline stages; down gives one up for the 64 KB bf16 staging of its output rows.
+    static constexpr int kStages = MODE == 0 ? 4 : 3;
+    static constexpr int kStageRowBytes = 272;  // 128 bf16 + 16 B pad: conflict-free row-per-thread writes
+    static constexpr int kStagingBytes = MODE == 0 ? 0 : 8 * 32 * kStageRowBytes;
+};
+constexpr int kMaxStages = 4;
 constexpr int kABytes = kBM * kBK;          // 16 KB
 constexpr int kBBytes = kBN * kBK;          // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;
@@ -35,8 +41,8 @@ constexpr uint32_t kTmemCols = 512;         // two 256-column fp32 accumulators
 constexpr uint32_t kIdesc = idesc_f32acc(0 /*e4m3*/, 0 /*e4m3*/, kBM, kBN);
 
 struct SmemTail {
-    uint64_t full[kStages];
-    uint64_t empty[kStages];
+    uint64_t full[kMaxStages];
+    uint64_t empty[kMaxStages];
     uint64_t tfull[2];
     uint64_t tempty[2];
     uint64_t drain;
@@ -46,10 +52,17 @@ struct SmemTail {
     float amax_x[2][2][kBM];  // [tile parity][column half][row]
 };
 
-constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + (size_t)kStages * kStageBytes + sizeof(SmemTail);
+template <int MODE>
+constexpr size_t smem_bytes() {
+    return 1024 /*alignment slack*/ + (size_t)Cfg<MODE>::kStages * kStageBytes + Cfg<MODE>::kStagingBytes +
+           sizeof(SmemTail);
+}
 
+// silu(g) * u on bf16 values with bf16 rounding after each step (vLLM silu_and_mul semantics).  The sigmoid uses
+// the fast exponential and division: the result is rounded to bf16 (8 significant bits) right after, so their
+// last-bit fp32 error changes an output only when it straddles a bf16 rounding boundary.
 __device__ __forceinline__ float silu_mul(float g, float u) {
-    const float s = bf16_round(__fdiv_rn(g, 1.0f + expf(-g)));
+    const float s = bf16_round(__fdividef(g, 1.0f + __expf(-g)));
     return bf16_round(s * u);
 }
 
@@ -66,11 +79,13 @@ template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                         const GemmArgs args) {
+    constexpr int kStages = Cfg<MODE>::kStages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(smem);
-    SmemTail* tail = reinterpret_cast<SmemTail*>(smem + (size_t)kStages * kStageBytes);
+    uint8_t* staging = smem + (size_t)kStages * kStageBytes;
+    SmemTail* tail = reinterpret_cast<SmemTail*>(staging + Cfg<MODE>::kStagingBytes);
     volatile int* abort = &tail->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -191,19 +206,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int grow = mb * kBM + row;
             const float* bs = args.b_scale + (size_t)e * nb_total * KB;
             const float* as = args.a_scale + (size_t)grow * KB;
+            // the two block-scale rows this thread multiplies by (gate/up halves, or its column half)
+            const float* bs0 = bs + (size_t)(MODE == 0 ? nt : nt * 2 + half) * KB;
+            const float* bs1 = bs + (size_t)(MODE == 0 ? args.inter / 128 + nt : nt * 2 + half) * KB;
 #pragma unroll
             for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
             bool ok = true;
+            float sa_n = as[0], b0_n = bs0[0], b1_n = bs1[0];  // scales of the next K block, loaded ahead
             for (int kb = 0; kb < KB; ++kb, ++it) {
                 const uint32_t buf = it & 1u, use = it >> 1;
-                const float sa = as[kb];
-                float s0, s1;
-                if (MODE == 0) {
-                    s0 = sa * bs[(size_t)nt * KB + kb];
-                    s1 = sa * bs[(size_t)(args.inter / 128 + nt) * KB + kb];
-                } else {
-                    s0 = sa * bs[(size_t)(nt * 2 + half) * KB + kb];
-                    s1 = s0;
+                const float s0 = sa_n * b0_n, s1 = sa_n * b1_n;
+                if (kb + 1 < KB) {
+                    sa_n = as[kb + 1];
+                    b0_n = bs0[kb + 1];
+                    b1_n = bs1[kb + 1];
                 }
                 if (!mbar_wait(bar_tfull + 8 * buf, use & 1u, abort)) { ok = false; break; }
                 tc_fence_after();
@@ -243,13 +259,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!mbar_wait(xb, (uint32_t)(local >> 1) & 1u, abort)) break;
                 amax = fmaxf(tail->amax_x[local & 1][0][row], tail->amax_x[local & 1][1][row]);
                 const float sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
+                // y * (1/s) instead of y / s: the e4m3 code keeps 3 significand bits, so the quotient's last-bit
+                // difference moves a code only when it lies on an e4m3 rounding midpoint.
+                const float inv = __frcp_rn(sc);
                 uint32_t packed[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float q0 = fminf(fmaxf(__fdiv_rn(acc[4 * i + 0], sc), -448.0f), 448.0f);
-                    const float q1 = fminf(fmaxf(__fdiv_rn(acc[4 * i + 1], sc), -448.0f), 448.0f);
-                    const float q2 = fminf(fmaxf(__fdiv_rn(acc[4 * i + 2], sc), -448.0f), 448.0f);
-                    const float q3 = fminf(fmaxf(__fdiv_rn(acc[4 * i + 3], sc), -448.0f), 448.0f);
+                    const float q0 = fminf(fmaxf(acc[4 * i + 0] * inv, -448.0f), 448.0f);
+                    const float q1 = fminf(fmaxf(acc[4 * i + 1] * inv, -448.0f), 448.0f);
+                    const float q2 = fminf(fmaxf(acc[4 * i + 2] * inv, -448.0f), 448.0f);
+                    const float q3 = fminf(fmaxf(acc[4 * i + 3] * inv, -448.0f), 448.0f);
                     packed[i] = (uint32_t)e4m3x2(q0, q1) | ((uint32_t)e4m3x2(q2, q3) << 16);
                 }
                 uint4* dst = reinterpret_cast<uint4*>(args.out_q + (size_t)grow * args.inter + nt * 128 + 64 * half);
@@ -258,21 +277,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                     dst[u] = make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
                 if (half == 0) args.out_s[(size_t)grow * (args.inter / 128) + nt] = sc;
             } else {
+                // Weight, round, and stage this warp's 32 rows x 128 columns in shared memory (one row per
+                // thread), then write the rows out as coalesced 256-byte segments, two rows per instruction.
                 const int flat = args.sorted_ids[grow];
-                if (flat < args.n_valid) {
-                    const float w = args.topk_w[flat];
-                    const int H = args.n_total;
-                    uint4* dst = reinterpret_cast<uint4*>(args.c3 + (size_t)flat * H + nt * kBN + 128 * half);
+                const float w = flat < args.n_valid ? args.topk_w[flat] : 0.0f;
+                constexpr int RB = Cfg<MODE>::kStageRowBytes;
+                uint8_t* wst = staging + (size_t)(warp - kEpiWarp0) * 32 * RB;
 #pragma unroll
-                    for (int u = 0; u < 16; ++u) {
-                        uint4 o;
-                        __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o);
+                for (int u = 0; u < 16; ++u) {
+                    uint4 o;
+                    __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            ob[i] = __floats2bfloat162_rn(acc[8 * u + 2 * i] * w, acc[8 * u + 2 * i + 1] * w);
-                        dst[u] = o;
+                    for (int i = 0; i < 4; ++i)
+                        ob[i] = __floats2bfloat162_rn(acc[8 * u + 2 * i] * w, acc[8 * u + 2 * i + 1] * w);
+                    *reinterpret_cast<uint4*>(wst + lane * RB + u * 16) = o;
+                }
+                __syncwarp();
+                // A row's half is 128 bf16 = 256 bytes = 16 lanes x 16 bytes: lanes 0-15 write row r,
+                // lanes 16-31 row r+1.  Columns stay within [nt*256, nt*256 + 256) of an H-wide row.
+                const int H = args.n_total;
+                const int sub = lane >> 4, chunk = lane & 15;
+                for (int r = 0; r < 32; r += 2) {
+                    const int f = __shfl_sync(0xffffffffu, flat, r + sub);
+                    if (f < args.n_valid) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(wst + (r + sub) * RB + chunk * 16);
+                        *reinterpret_cast<uint4*>(args.c3 + (size_t)f * H + nt * kBN + 128 * half + chunk * 8) = v;
                     }
                 }
+                __syncwarp();
             }
         }
     }
@@ -294,16 +326,20 @@ cudaError_t launch_gemm_fp8(int mode, const CUtensorMap& tm_a, const CUtensorMap
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !configured[dev][mode]) {
-        cudaError_t e = cudaFuncSetAttribute(mode == 0 ? moe_gemm_fp8_kernel<0> : moe_gemm_fp8_kernel<1>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+        cudaError_t e = mode == 0 ? cudaFuncSetAttribute(moe_gemm_fp8_kernel<0>,
+                                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                         (int)smem_bytes<0>())
+                                  : cudaFuncSetAttribute(moe_gemm_fp8_kernel<1>,
+                                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                         (int)smem_bytes<1>());
         if (e != cudaSuccess) return e;
         configured[dev][mode] = true;
     }
     const int grid = args.max_tiles < num_sms ? (args.max_tiles > 0 ? args.max_tiles : 1) : num_sms;
     if (mode == 0)
-        moe_gemm_fp8_kernel<0><<<grid, kThreads, kSmemBytes, s>>>(tm_a, tm_b, args);
+        moe_gemm_fp8_kernel<0><<<grid, kThreads, smem_bytes<0>(), s>>>(tm_a, tm_b, args);
     else
-        moe_gemm_fp8_kernel<1><<<grid, kThreads, kSmemBytes, s>>>(tm_a, tm_b, args);
+        moe_gemm_fp8_kernel<1><<<grid, kThreads, smem_bytes<1>(), s>>>(tm_a, tm_b, args);
     return cudaGetLastError();
 }
 
