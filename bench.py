@@ -30,7 +30,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "MoE-layer tokens/s and % FP8/FP4 tensor peak at T=5120; HBM GB/s at T=128"
 H, I, E, K = 2048, 768, 128, 8
 T_CTX, T_BRANCH, T_CPU_SAMPLE = 5120, 128, 512
-KERNELS_PER_STEP = 8  # router+top-k, 3 alignment passes, permute+quant, gate_up GEMM, down GEMM, combine
+KERNELS_PER_STEP = 8  # router+top-k, 3 alignment passes, activation quant, gate_up GEMM, down GEMM, combine
 
 
 def peaks() -> dict:
@@ -197,16 +197,16 @@ def stage_times(layer: dict, T: int, reps: int = 20) -> dict:
     r_out = ops.router_topk(x, rw, K)
     _, w, ids = r_out
     a_out = ops.align(ids, E)
-    srt, eids, npp, _, _ = a_out
-    p_out = ops.permute_quant_fp8(x, srt, npp, K)
-    g1_out = ops.gemm1_fp8(*p_out, layer["w1"], layer["w1_s"], eids, npp)
+    srt, eids, npp, _, slot_of, _ = a_out
+    q_out = ops.quant_fp8(x, slot_of, K, srt.numel())
+    g1_out = ops.gemm1_fp8(*q_out, layer["w1"], layer["w1_s"], eids, npp)
     g2_out = ops.gemm2_fp8(g1_out[0], g1_out[1], layer["w2"], layer["w2_s"], eids, npp, srt, w.reshape(-1), T, K)
     c_out = ops.combine(g2_out[0], T, K)
     out = {
         "router_topk": time_region(lambda: ops.router_topk(x, rw, K, out=r_out), reps, s),
         "align": time_region(lambda: ops.align(ids, E, out=a_out), reps, s),
-        "permute_quant": time_region(lambda: ops.permute_quant_fp8(x, srt, npp, K, out=p_out), reps, s),
-        "gemm1": time_region(lambda: ops.gemm1_fp8(*p_out, layer["w1"], layer["w1_s"], eids, npp, out=g1_out),
+        "quant_dispatch": time_region(lambda: ops.quant_fp8(x, slot_of, K, srt.numel(), out=q_out), reps, s),
+        "gemm1": time_region(lambda: ops.gemm1_fp8(*q_out, layer["w1"], layer["w1_s"], eids, npp, out=g1_out),
                              reps, s),
         "gemm2": time_region(lambda: ops.gemm2_fp8(g1_out[0], g1_out[1], layer["w2"], layer["w2_s"], eids, npp, srt,
                                                    w.reshape(-1), T, K, out=g2_out), reps, s),

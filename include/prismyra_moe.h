@@ -61,7 +61,8 @@ enum pm_region {
     PM_WS_A1_SCALE = 10, /* f32 [max_slots, H/128] (NVFP4: e4m3 [max_slots, H/16]) */
     PM_WS_A2 = 11,      /* e4m3 [max_slots, I] down-projection input (NVFP4: packed e2m1 [max_slots, I/2]) */
     PM_WS_A2_SCALE = 12, /* f32 [max_slots, I/128] (NVFP4: e4m3 [max_slots, I/16]) */
-    PM_WS_C3 = 13       /* bf16 [T*k, H] weighted expert outputs per (token, slot) */
+    PM_WS_C3 = 13,      /* bf16 [T*k, H] weighted expert outputs per (token, slot) */
+    PM_WS_SLOT_OF = 14  /* i32 [T*k] slot of each flat index (the inverse of PM_WS_SORTED) */
 };
 
 /* Version of this ABI; bumped on any incompatible change. */
@@ -90,18 +91,20 @@ int pm_moe_topk(const void *logits, int T, int E, int k, float *topk_w, int32_t 
 
 /* Expert alignment: vllm/model_executor/layers/fused_moe/moe_align_block_size.py:11-99 with block 128, the
  * reference's call at vllm/model_executor/layers/fused_moe/fused_moe.py:1536-1585.  Flat indices grouped by
- * expert in ascending order, padded with T*k.  Needs the workspace for its per-chunk counts.  expert_off may
- * be NULL. */
+ * expert in ascending order, padded with T*k.  Needs the workspace for its per-chunk counts.  expert_off and
+ * slot_of (the inverse permutation, slot_of[t*k + j] = slot) may be NULL. */
 int pm_moe_align(const int32_t *topk_ids, int T, int k, int E, int32_t *sorted_ids, int32_t *expert_ids,
-                 int32_t *num_post_pad, int32_t *expert_off, void *workspace, size_t workspace_bytes,
-                 pm_stream_t stream);
+                 int32_t *num_post_pad, int32_t *expert_off, int32_t *slot_of, void *workspace,
+                 size_t workspace_bytes, pm_stream_t stream);
 
-/* Activation gather + per-128-column e4m3 quantisation in slot order:
- * vllm/model_executor/layers/quantization/utils/fp8_utils.py:110-150 (per_token_group_quant_fp8), applied
- * by vllm/model_executor/layers/fused_moe/fused_moe.py:1780-1786 before the gate_up GEMM. */
-int pm_moe_permute_quant_fp8(const void *x, int T, int H, int k, const int32_t *sorted_ids,
-                             const int32_t *num_post_pad, int max_slots, uint8_t *a_q, float *a_s,
-                             pm_stream_t stream);
+/* Per-token, per-128-column e4m3 quantisation of the activations:
+ * vllm/model_executor/layers/quantization/utils/fp8_utils.py:110-150 (per_token_group_quant_fp8), applied by
+ * vllm/model_executor/layers/fused_moe/fused_moe.py:1780-1786 before the gate_up GEMM.  slot_of == NULL: row t of
+ * a_q e4m3 [T, H] / a_s f32 [T, H/128]; otherwise each token's row is written to its k slots
+ * (a_q [max_slots, H], a_s [max_slots, H/128]; vLLM reads the same rows through sorted_ids // top_k,
+ * fused_moe.py:437-439) and padding slots are left unwritten. */
+int pm_moe_quant_fp8(const void *x, int T, int H, int k, const int32_t *slot_of, uint8_t *a_q, float *a_s,
+                     pm_stream_t stream);
 
 /* Grouped gate_up GEMM with fused silu*mul and e4m3 re-quantisation:
  * vllm/model_executor/layers/fused_moe/fused_moe.py:1801-1822 (GEMM1), :1825-1827 (silu_and_mul),

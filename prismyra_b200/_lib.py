@@ -22,6 +22,7 @@ FMT_NVFP4 = 1
 WS = {
     "status": 0, "logits": 1, "topk_w": 2, "topk_ids": 3, "counts": 4, "expert_off": 5, "sorted": 6,
     "expert_ids": 7, "num_post_pad": 8, "a1": 9, "a1_scale": 10, "a2": 11, "a2_scale": 12, "c3": 13,
+    "slot_of": 14,
 }
 
 _P = ctypes.c_void_p
@@ -37,8 +38,8 @@ SIGNATURES: dict[str, tuple] = {
     "pm_moe_workspace_region": (_I, [_I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_Z), ctypes.POINTER(_Z)]),
     "pm_moe_router_topk": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "pm_moe_topk": (_I, [_P, _I, _I, _I, _P, _P, _P]),
-    "pm_moe_align": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _Z, _P]),
-    "pm_moe_permute_quant_fp8": (_I, [_P, _I, _I, _I, _P, _P, _I, _P, _P, _P]),
+    "pm_moe_align": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _Z, _P]),
+    "pm_moe_quant_fp8": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
     "pm_moe_gemm1_fp8": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "pm_moe_gemm2_fp8": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
     "pm_moe_combine": (_I, [_P, _I, _I, _I, _P, _P]),

@@ -69,6 +69,6 @@ extern "C" int pm_moe_align_noalloc(const int32_t* topk_ids, int T, int k, int E
     const int st = noalloc_counts(&counts);
     if (st != PM_OK) return st;
     const cudaError_t e = launch_align(topk_ids, T * k, E, counts, sorted_ids, expert_ids, num_post_pad, expert_off,
-                                       (cudaStream_t)stream);
+                                       nullptr, (cudaStream_t)stream);
     return e == cudaSuccess ? PM_OK : PM_ERR_CUDA;
 }

@@ -16,8 +16,8 @@ namespace pm {
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 static std::once_flag g_encode_once;
 
-bool encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
-                       uint32_t box_inner, uint32_t box_outer) {
+bool encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t inner,
+                    uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
     std::call_once(g_encode_once, [] {
         cudaDriverEntryPointQueryResult q;
         void* fn = nullptr;
@@ -31,7 +31,8 @@ bool encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint6
     cuuint64_t strides[1] = {row_bytes};
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+    (void)elem_bytes;
+    CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
@@ -64,9 +65,11 @@ static int current_device_info(DeviceInfo* out) {
 }
 
 // ------------------------------------------------------------------------------------------- workspace
+constexpr int kRegions = PM_WS_SLOT_OF + 1;
+
 struct Layout {
-    size_t off[14];
-    size_t len[14];
+    size_t off[kRegions];
+    size_t len[kRegions];
     size_t total;
     int max_slots;
 };
@@ -98,8 +101,9 @@ static Layout layout_of(int T, int H, int I, int E, int k, int fmt) {
     L.len[PM_WS_A2] = (size_t)ms * (fp4 ? I / 2 : I);
     L.len[PM_WS_A2_SCALE] = (size_t)ms * (fp4 ? I / 16 : (I / 128) * 4);
     L.len[PM_WS_C3] = (size_t)n * H * 2;
+    L.len[PM_WS_SLOT_OF] = (size_t)n * 4;
     size_t o = 0;
-    for (int r = 0; r < 14; ++r) {
+    for (int r = 0; r < kRegions; ++r) {
         L.off[r] = o;
         o = align256(o + L.len[r]);
     }
@@ -170,7 +174,7 @@ size_t pm_moe_workspace_bytes(int T, int H, int I, int E, int k, int fmt) {
 int pm_moe_workspace_region(int T, int H, int I, int E, int k, int fmt, int region, size_t* offset, size_t* bytes) {
     const int st = check_dims(T, H, I, E, k);
     if (st != PM_OK) return st;
-    if (region < 0 || region > PM_WS_C3 || offset == nullptr || bytes == nullptr) return PM_ERR_INVALID;
+    if (region < 0 || region >= kRegions || offset == nullptr || bytes == nullptr) return PM_ERR_INVALID;
     const Layout L = layout_of(T, H, I, E, k, fmt);
     *offset = L.off[region];
     *bytes = L.len[region];
@@ -187,7 +191,8 @@ int pm_moe_router_topk(const void* x, const void* router_w, int T, int H, int E,
     DeviceInfo d;
     const int st = current_device_info(&d);
     if (st != PM_OK) return st;
-    return cuda_status(launch_router_topk(x, router_w, T, H, E, k, logits, topk_w, topk_ids, (cudaStream_t)stream));
+    return cuda_status(
+        launch_router_topk(x, router_w, T, H, E, k, logits, topk_w, topk_ids, nullptr, (cudaStream_t)stream));
 }
 
 int pm_moe_topk(const void* logits, int T, int E, int k, float* topk_w, int32_t* topk_ids, pm_stream_t stream) {
@@ -202,8 +207,8 @@ int pm_moe_topk(const void* logits, int T, int E, int k, float* topk_w, int32_t*
 }
 
 int pm_moe_align(const int32_t* topk_ids, int T, int k, int E, int32_t* sorted_ids, int32_t* expert_ids,
-                 int32_t* num_post_pad, int32_t* expert_off, void* workspace, size_t workspace_bytes,
-                 pm_stream_t stream) {
+                 int32_t* num_post_pad, int32_t* expert_off, int32_t* slot_of, void* workspace,
+                 size_t workspace_bytes, pm_stream_t stream) {
     if (T < 0 || k <= 0 || E <= 0 || E > 1024) return PM_ERR_INVALID;
     if (!sorted_ids || !expert_ids || !num_post_pad || !workspace || (T > 0 && !topk_ids)) return PM_ERR_INVALID;
     const long n = (long)T * k;
@@ -213,22 +218,20 @@ int pm_moe_align(const int32_t* topk_ids, int T, int k, int E, int32_t* sorted_i
     const int st = current_device_info(&d);
     if (st != PM_OK) return st;
     return cuda_status(launch_align(topk_ids, (int)n, E, static_cast<int32_t*>(workspace), sorted_ids, expert_ids,
-                                    num_post_pad, expert_off, (cudaStream_t)stream));
+                                    num_post_pad, expert_off, slot_of, (cudaStream_t)stream));
 }
 
-int pm_moe_permute_quant_fp8(const void* x, int T, int H, int k, const int32_t* sorted_ids,
-                             const int32_t* num_post_pad, int max_slots, uint8_t* a_q, float* a_s,
-                             pm_stream_t stream) {
-    if (T < 0 || H <= 0 || k <= 0 || max_slots < 0) return PM_ERR_INVALID;
+int pm_moe_quant_fp8(const void* x, int T, int H, int k, const int32_t* slot_of, uint8_t* a_q, float* a_s,
+                     pm_stream_t stream) {
+    if (T < 0 || H <= 0 || (slot_of != nullptr && k <= 0)) return PM_ERR_INVALID;
     if (H % 128 != 0) return PM_ERR_SHAPE;
-    if (max_slots == 0) return PM_OK;
-    if (!sorted_ids || !num_post_pad || !a_q || !a_s || (T > 0 && !x)) return PM_ERR_INVALID;
-    if ((T > 0 && !a16(x)) || !a16(a_q)) return PM_ERR_ALIGN;
+    if (T == 0) return PM_OK;
+    if (!x || !a_q || !a_s) return PM_ERR_INVALID;
+    if (!a16(x) || !a16(a_q)) return PM_ERR_ALIGN;
     DeviceInfo d;
     const int st = current_device_info(&d);
     if (st != PM_OK) return st;
-    return cuda_status(launch_permute_quant_fp8(x, H, k, T * k, sorted_ids, num_post_pad, max_slots, a_q, a_s,
-                                                (cudaStream_t)stream));
+    return cuda_status(launch_quant_fp8(x, T, H, k, slot_of, a_q, a_s, (cudaStream_t)stream));
 }
 
 int pm_moe_gemm1_fp8(const uint8_t* a_q, const float* a_s, const uint8_t* w1, const float* w1_s,
@@ -325,12 +328,13 @@ int pm_moe_forward_fp8(const void* x, const void* router_w, const void* logits, 
     if (logits != nullptr)
         e = launch_topk(logits, T, E, k, topk_w, topk_ids, s);
     else
-        e = launch_router_topk(x, router_w, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, s);
+        e = launch_router_topk(x, router_w, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s);
     if (e != cudaSuccess) return PM_ERR_CUDA;
+    int32_t* slot_of = reinterpret_cast<int32_t*>(R(PM_WS_SLOT_OF));
     e = launch_align(topk_ids, T * k, E, reinterpret_cast<int32_t*>(R(PM_WS_COUNTS)), sorted, expert_ids, npp,
-                     reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_OFF)), s);
+                     reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_OFF)), slot_of, s);
     if (e != cudaSuccess) return PM_ERR_CUDA;
-    e = launch_permute_quant_fp8(x, H, k, T * k, sorted, npp, L.max_slots, a1, a1s, s);
+    e = launch_quant_fp8(x, T, H, k, slot_of, a1, a1s, s);
     if (e != cudaSuccess) return PM_ERR_CUDA;
     st = pm_moe_gemm1_fp8(a1, a1s, w1, w1_s, expert_ids, npp, L.max_slots, H, I, E, a2, a2s, status, stream);
     if (st != PM_OK) return st;

@@ -8,7 +8,8 @@
 // block kb is being promoted.
 //
 // Tiles: 128 rows (one alignment block, one expert) x 256 columns x 128 K per pipeline stage.
-//   mode 0 (gate_up, K = H): the 256 columns are 128 gate rows n0.. and the matching 128 up rows I+n0..,
+//   mode 0 (gate_up, K = H): A is the expert-ordered FP8 copy of x written by the quantisation kernel.  The 256
+//           columns are 128 gate rows n0.. and the matching 128 up rows I+n0..,
 //           the epilogue applies bf16 -> silu(gate)*up -> bf16 and re-quantises to e4m3 with one scale per
 //           128 output columns (exactly one tile), writing the down GEMM's A operand in slot order.
 //   mode 1 (down, K = I): the 256 columns are hidden columns n0..n0+255; the epilogue multiplies by the routing
@@ -126,34 +127,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
       if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer
-        if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                const int mb = tile / args.n_tiles, nt = tile % args.n_tiles;
-                const int e = args.expert_ids[mb];
-                const int row0 = e * args.n_total + (MODE == 0 ? nt * 128 : nt * kBN);
-                const int row1 = (MODE == 0) ? e * args.n_total + args.inter + nt * 128 : row0 + 128;
-                for (int kb = 0; kb < KB; ++kb) {
-                    if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, abort)) { ok = false; break; }
-                    const uint32_t a_dst = sbase + stage * kStageBytes;
-                    const uint32_t b_dst = a_dst + kABytes;
-                    const uint32_t fb = bar_full + 8 * stage;
-                    mbar_arrive_expect_tx(fb, kStageBytes);
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+            const int mb = tile / args.n_tiles, nt = tile % args.n_tiles;
+            const int e = args.expert_ids[mb];
+            const int row0 = e * args.n_total + (MODE == 0 ? nt * 128 : nt * kBN);
+            const int row1 = (MODE == 0) ? e * args.n_total + args.inter + nt * 128 : row0 + 128;
+            for (int kb = 0; kb < KB; ++kb) {
+                int go = 1;
+                if (lane == 0) go = mbar_wait(bar_empty + 8 * stage, phase ^ 1u, abort) ? 1 : 0;
+                go = __shfl_sync(0xffffffffu, go, 0);
+                if (!go) { ok = false; break; }
+                const uint32_t a_dst = sbase + stage * kStageBytes;
+                const uint32_t b_dst = a_dst + kABytes;
+                const uint32_t fb = bar_full + 8 * stage;
+                if (lane == 0) mbar_arrive_expect_tx(fb, kStageBytes);
+                __syncwarp();
+                if (lane == 0) {
                     tma_load_2d(a_dst, &tm_a, fb, kb * kBK, mb * kBM);
                     tma_load_2d(b_dst, &tm_b, fb, kb * kBK, row0);
                     tma_load_2d(b_dst + kBBytes / 2, &tm_b, fb, kb * kBK, row1);
-                    if (++stage == kStages) { stage = 0; phase ^= 1u; }
                 }
+                if (++stage == kStages) { stage = 0; phase ^= 1u; }
             }
-            if (!ok) {
-                // Unwind: let every load this thread issued land before the CTA exits (bounded).
-                for (int s = 0; s < kStages; ++s) {
-                    const uint64_t t0 = globaltimer();
-                    while (!mbar_try_wait(bar_full + 8 * s, phase ^ (s < stage ? 0u : 1u)) &&
-                           globaltimer() - t0 < PM_WAIT_TIMEOUT_NS) {
-                    }
+        }
+        if (!ok && lane == 0) {
+            // Unwind: let every load this warp issued land before the CTA exits (bounded).
+            for (int s = 0; s < kStages; ++s) {
+                const uint64_t t0 = globaltimer();
+                while (!mbar_try_wait(bar_full + 8 * s, phase ^ (s < stage ? 0u : 1u)) &&
+                       globaltimer() - t0 < PM_WAIT_TIMEOUT_NS) {
                 }
             }
         }

@@ -18,16 +18,17 @@ inline int cdiv(long a, long b) { return static_cast<int>((a + b - 1) / b); }
 
 // Router projection (bf16, fp32 accumulation in a fixed order per row) fused with softmax / top-k.
 cudaError_t launch_router_topk(const void* x, const void* w, int T, int H, int E, int k, void* logits, float* topk_w,
-                               int32_t* topk_ids, cudaStream_t s);
+                               int32_t* topk_ids, int32_t* err, cudaStream_t s);
 // Softmax / top-k / renormalise from given bf16 logits.
 cudaError_t launch_topk(const void* logits, int T, int E, int k, float* topk_w, int32_t* topk_ids, cudaStream_t s);
 // Stable counting sort of the flat (token, slot) indices by expert, padded per expert to kBlockM.
+// slot_of (may be null) receives the inverse permutation: slot_of[flat index] = its slot.
 cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int32_t* sorted, int32_t* expert_ids,
-                         int32_t* num_post_pad, int32_t* expert_off, cudaStream_t s);
-// Gather x rows into expert order and quantise them to e4m3 with one fp32 scale per 128 columns.
-cudaError_t launch_permute_quant_fp8(const void* x, int H, int k, int n_valid, const int32_t* sorted,
-                                     const int32_t* num_post_pad, int max_slots, uint8_t* a_q, float* a_s,
-                                     cudaStream_t s);
+                         int32_t* num_post_pad, int32_t* expert_off, int32_t* slot_of, cudaStream_t s);
+// Quantise every token row of x to e4m3 with one fp32 scale per 128 columns.  With slot_of, each quantised row
+// is written to the k slots of its token (a_q [slots, H], a_s [slots, H/128]) instead of to row t.
+cudaError_t launch_quant_fp8(const void* x, int T, int H, int k, const int32_t* slot_of, uint8_t* x_q, float* x_s,
+                             cudaStream_t s);
 // out[t] = bf16(sum_j c3[t*k + j]) in fp32, j ascending.
 cudaError_t launch_combine(const void* c3, int T, int k, int H, void* out, cudaStream_t s);
 
@@ -55,8 +56,13 @@ struct GemmArgs {
 cudaError_t launch_gemm_fp8(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, const GemmArgs& args,
                             int num_sms, cudaStream_t s);
 
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
-bool encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
-                       uint32_t box_inner, uint32_t box_outer);
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda): a 2-D row-major
+// tensor of `outer` rows x `inner` elements, rows `row_bytes` apart, 128-byte swizzled boxes.
+bool encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t inner,
+                    uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
+inline bool encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                              uint32_t box_inner, uint32_t box_outer) {
+    return encode_tmap_2d(map, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, inner, outer, row_bytes, box_inner, box_outer);
+}
 
 }  // namespace pm

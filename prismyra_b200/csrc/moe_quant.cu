@@ -1,35 +1,31 @@
-// Data movement around the grouped GEMMs: the expert-ordered FP8 copy of the activations (with the
-// per-128-column quantisation of vLLM's per_token_group_quant_fp8, fp8_utils.py:137-147) and the final
-// top-k sum (vLLM moe_sum, fused_moe.py:1864).
+// Element-wise stages around the grouped GEMMs: the per-128-column FP8 quantisation of the token activations
+// (vLLM per_token_group_quant_fp8, fp8_utils.py:137-147) and the final top-k sum (vLLM moe_sum,
+// fused_moe.py:1864).
 #include "moe_internal.h"
 #include "ptx.cuh"
 
 namespace pm {
 namespace {
 
-// One warp per slot.  Lane L of an iteration holds 64 consecutive columns; lanes 2g and 2g+1 share one
-// 128-column group.  s = max(amax, 1e-10) * (1/448); q = e4m3(clamp(x / s, -448, 448)).  Padding slots
-// (flat index == n_valid) are written as zero codes with a zero scale.
-__global__ void __launch_bounds__(256) permute_quant_fp8_kernel(const __nv_bfloat16* __restrict__ x, int H, int k,
-                                                                int n_valid, const int32_t* __restrict__ sorted,
-                                                                const int32_t* __restrict__ num_post_pad,
-                                                                uint8_t* __restrict__ a_q,
-                                                                float* __restrict__ a_s) {
+// One warp per token row.  Lane L of an iteration holds 64 consecutive columns; lanes 2g and 2g+1 share one
+// 128-column group.  s = max(amax, 1e-10) * (1/448); q = e4m3(clamp(x / s, -448, 448)) with an IEEE division,
+// exactly as the reference's Triton kernel states it.  With slot_of the row is written to the token's k slots
+// (its expert-ordered copies for the gate_up GEMM; vLLM reads the same rows through sorted_ids // top_k); the
+// padding slots are left unwritten -- their GEMM rows are computed and discarded, never stored.
+__global__ void __launch_bounds__(256) quant_fp8_kernel(const __nv_bfloat16* __restrict__ x, int T, int H, int k,
+                                                        const int32_t* __restrict__ slot_of,
+                                                        uint8_t* __restrict__ x_q, float* __restrict__ x_s) {
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x >> 5);
-    const int npp = *num_post_pad;
-    for (int slot = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; slot < npp; slot += warps) {
-        const int flat = sorted[slot];
-        const bool real = flat < n_valid;
-        const __nv_bfloat16* src = x + (size_t)(real ? flat / k : 0) * H;
-        uint8_t* dq = a_q + (size_t)slot * H;
-        float* ds = a_s + (size_t)slot * (H / 128);
+    for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < T; row += warps) {
+        const __nv_bfloat16* src = x + (size_t)row * H;
+        const int ncopies = slot_of != nullptr ? k : 1;
         for (int c0 = 0; c0 < H; c0 += 32 * 64) {
             const int col = c0 + lane * 64;
             const bool act = col < H;
             float v[64];
             float amax = 0.0f;
-            if (act && real) {
+            if (act) {
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
                     const uint4 w = *reinterpret_cast<const uint4*>(src + col + u * 8);
@@ -40,9 +36,6 @@ __global__ void __launch_bounds__(256) permute_quant_fp8_kernel(const __nv_bfloa
                         amax = fmaxf(amax, fabsf(v[u * 8 + i]));
                     }
                 }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 64; ++i) v[i] = 0.0f;
             }
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
             const float sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
@@ -56,11 +49,14 @@ __global__ void __launch_bounds__(256) permute_quant_fp8_kernel(const __nv_bfloa
                     const float q3 = fminf(fmaxf(__fdiv_rn(v[4 * i + 3], sc), -448.0f), 448.0f);
                     packed[i] = (uint32_t)e4m3x2(q0, q1) | ((uint32_t)e4m3x2(q2, q3) << 16);
                 }
-                uint4* d = reinterpret_cast<uint4*>(dq + col);
+                for (int c = 0; c < ncopies; ++c) {
+                    const size_t dst = slot_of != nullptr ? (size_t)slot_of[(size_t)row * k + c] : (size_t)row;
+                    uint4* d = reinterpret_cast<uint4*>(x_q + dst * H + col);
 #pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    d[u] = make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
-                if ((lane & 1) == 0) ds[col / 128] = real ? sc : 0.0f;
+                    for (int u = 0; u < 4; ++u)
+                        d[u] = make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
+                    if ((lane & 1) == 0) x_s[dst * (H / 128) + col / 128] = sc;
+                }
             }
         }
     }
@@ -92,16 +88,14 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
 
 }  // namespace
 
-cudaError_t launch_permute_quant_fp8(const void* x, int H, int k, int n_valid, const int32_t* sorted,
-                                     const int32_t* num_post_pad, int max_slots, uint8_t* a_q, float* a_s,
-                                     cudaStream_t s) {
-    if (max_slots == 0) return cudaSuccess;
+cudaError_t launch_quant_fp8(const void* x, int T, int H, int k, const int32_t* slot_of, uint8_t* x_q, float* x_s,
+                             cudaStream_t s) {
+    if (T == 0) return cudaSuccess;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int blocks = min(cdiv(max_slots, 8), sms * 8);
-    permute_quant_fp8_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), H, k, n_valid, sorted,
-                                                     num_post_pad, a_q, a_s);
+    const int blocks = min(cdiv(T, 8), sms * 8);
+    quant_fp8_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), T, H, k, slot_of, x_q, x_s);
     return cudaGetLastError();
 }
 

@@ -1,5 +1,5 @@
-// Routing stage of the routed-expert layer: router projection, softmax / top-k / renormalise, and the stable
-// expert alignment of the flat (token, slot) indices.
+// Routing stage of the routed-expert layer: softmax / top-k / renormalise from given logits, and the stable
+// expert alignment of the flat (token, slot) indices (the router projection itself is moe_router_tc.cu).
 //
 // Reference behaviour (restated here, see the oracle for the executable statement):
 //   router  prismyra/kernels/qwen3_moe.py:169-171 (_route: bf16 x . W^T, fp32 accumulation, bf16 logits)
@@ -26,14 +26,16 @@ __device__ __forceinline__ void warp_topk(const float (&v)[kMaxEPT], int E, int 
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float ex[kMaxEPT];
+#pragma unroll
+    for (int i = 0; i < kMaxEPT; ++i) ex[i] = (lane + 32 * i < E) ? expf(v[i] - mx) : 0.0f;
+    // The exponent sum in ascending expert order, the same order as the router kernel's epilogue, so both
+    // entry points give bit-identical weights for the same logits.
     float sum = 0.0f;
 #pragma unroll
     for (int i = 0; i < kMaxEPT; ++i) {
-        ex[i] = (lane + 32 * i < E) ? expf(v[i] - mx) : 0.0f;
-        sum += ex[i];
+        if (32 * i >= E) break;
+        for (int l = 0; l < 32; ++l) sum += __shfl_sync(0xffffffffu, ex[i], l);
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
 
     uint32_t used = 0;
     float sel = 0.0f, my_p = 0.0f;
@@ -91,100 +93,6 @@ __global__ void __launch_bounds__(256) topk_kernel(const __nv_bfloat16* __restri
         v[i] = e < E ? __bfloat162float(logits[(size_t)warp * E + e]) : -INFINITY;
     }
     warp_topk(v, E, k, topk_w + (size_t)warp * k, topk_ids + (size_t)warp * k);
-}
-
-// Router projection on CUDA cores: a CTA computes 32 tokens x all experts with every output reduced over H in
-// ascending order (a row's logits never depend on which other rows share the call), rounds to bf16, then ranks
-// its 32 tokens with one warp per token.
-constexpr int kRTM = 32;   // tokens per CTA
-constexpr int kRKC = 64;   // H chunk
-constexpr int kRPad = 4;
-
-__global__ void __launch_bounds__(256) router_topk_kernel(const __nv_bfloat16* __restrict__ x,
-                                                          const __nv_bfloat16* __restrict__ w, int T, int H, int E,
-                                                          int k, __nv_bfloat16* __restrict__ logits,
-                                                          float* __restrict__ topk_w,
-                                                          int32_t* __restrict__ topk_ids) {
-    extern __shared__ float rsm[];
-    float* xs = rsm;                              // [kRTM][kRKC + kRPad]
-    float* ws = rsm + kRTM * (kRKC + kRPad);      // [E][kRKC + kRPad]
-    const int tid = threadIdx.x, ty = tid >> 5, tx = tid & 31;
-    const int t0 = blockIdx.x * kRTM;
-    float acc[4][kMaxEPT];
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int j = 0; j < kMaxEPT; ++j) acc[r][j] = 0.0f;
-
-    for (int h0 = 0; h0 < H; h0 += kRKC) {
-        {   // 32 x 64 activations: one 16-byte load per thread
-            const int r = tid >> 3, c = (tid & 7) * 8;
-            uint4 u = make_uint4(0, 0, 0, 0);
-            if (t0 + r < T) u = *reinterpret_cast<const uint4*>(x + (size_t)(t0 + r) * H + h0 + c);
-            const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
-            float* d = xs + r * (kRKC + kRPad) + c;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) d[i] = __bfloat162float(b[i]);
-        }
-        for (int q = tid; q < E * 8; q += 256) {
-            const int r = q >> 3, c = (q & 7) * 8;
-            const uint4 u = *reinterpret_cast<const uint4*>(w + (size_t)r * H + h0 + c);
-            const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
-            float* d = ws + r * (kRKC + kRPad) + c;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) d[i] = __bfloat162float(b[i]);
-        }
-        __syncthreads();
-#pragma unroll 4
-        for (int kk = 0; kk < kRKC; kk += 4) {
-            float4 xv[4];
-#pragma unroll
-            for (int r = 0; r < 4; ++r)
-                xv[r] = *reinterpret_cast<const float4*>(xs + (ty * 4 + r) * (kRKC + kRPad) + kk);
-#pragma unroll
-            for (int j = 0; j < kMaxEPT; ++j) {
-                const int e = tx + 32 * j;
-                if (e < E) {
-                    const float4 wv = *reinterpret_cast<const float4*>(ws + e * (kRKC + kRPad) + kk);
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        float a = acc[r][j];
-                        a = fmaf(xv[r].x, wv.x, a);
-                        a = fmaf(xv[r].y, wv.y, a);
-                        a = fmaf(xv[r].z, wv.z, a);
-                        a = fmaf(xv[r].w, wv.w, a);
-                        acc[r][j] = a;
-                    }
-                }
-            }
-        }
-        __syncthreads();
-    }
-    // bf16 logits into shared memory (and global when asked), then rank.
-    float* lg = rsm;  // [kRTM][E]
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int j = 0; j < kMaxEPT; ++j) {
-            const int e = tx + 32 * j, t = ty * 4 + r;
-            if (e < E) {
-                const __nv_bfloat16 b = __float2bfloat16_rn(acc[r][j]);
-                lg[t * E + e] = __bfloat162float(b);
-                if (logits != nullptr && t0 + t < T) logits[(size_t)(t0 + t) * E + e] = b;
-            }
-        }
-    __syncthreads();
-    for (int r = 0; r < 4; ++r) {
-        const int t = ty * 4 + r;
-        if (t0 + t >= T) break;
-        float v[kMaxEPT];
-#pragma unroll
-        for (int i = 0; i < kMaxEPT; ++i) {
-            const int e = tx + 32 * i;
-            v[i] = e < E ? lg[t * E + e] : -INFINITY;
-        }
-        warp_topk(v, E, k, topk_w + (size_t)(t0 + t) * k, topk_ids + (size_t)(t0 + t) * k);
-    }
 }
 
 // ------------------------------------------------------------------------------------------- alignment
@@ -245,7 +153,8 @@ __global__ void __launch_bounds__(1024) align_scan_kernel(int32_t* __restrict__ 
 // equal experts are ordered by warp (via per-warp counts) and by lane (via the match mask).
 __global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __restrict__ ids, int n, int E,
                                                             const int32_t* __restrict__ bases,
-                                                            int32_t* __restrict__ sorted) {
+                                                            int32_t* __restrict__ sorted,
+                                                            int32_t* __restrict__ slot_of) {
     extern __shared__ int32_t sm[];
     int32_t* base = sm;            // [E]
     int32_t* wcnt = sm + E;        // [8][E]
@@ -266,6 +175,7 @@ __global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __res
             int pos = base[e] + rank;
             for (int w = 0; w < warp; ++w) pos += wcnt[w * E + e];
             sorted[pos] = i;
+            if (slot_of != nullptr) slot_of[i] = pos;
         }
         __syncthreads();
         for (int q = tid; q < E; q += 256) {
@@ -286,29 +196,8 @@ cudaError_t launch_topk(const void* logits, int T, int E, int k, float* topk_w, 
     return cudaGetLastError();
 }
 
-cudaError_t launch_router_topk(const void* x, const void* w, int T, int H, int E, int k, void* logits, float* topk_w,
-                               int32_t* topk_ids, cudaStream_t s) {
-    if (T == 0) return cudaSuccess;
-    size_t smem = sizeof(float) * (size_t)(kRTM + E) * (kRKC + kRPad);
-    const size_t need_lg = sizeof(float) * (size_t)kRTM * E;
-    if (need_lg > smem) smem = need_lg;
-    static bool configured[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(router_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)(sizeof(float) * (kRTM + kMaxExperts) * (kRKC + kRPad)));
-        if (e != cudaSuccess) return e;
-        configured[dev] = true;
-    }
-    router_topk_kernel<<<cdiv(T, kRTM), 256, smem, s>>>(
-        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), T, H, E, k,
-        static_cast<__nv_bfloat16*>(logits), topk_w, topk_ids);
-    return cudaGetLastError();
-}
-
 cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int32_t* sorted, int32_t* expert_ids,
-                         int32_t* num_post_pad, int32_t* expert_off, cudaStream_t s) {
+                         int32_t* num_post_pad, int32_t* expert_off, int32_t* slot_of, cudaStream_t s) {
     const int nchunks = n > 0 ? cdiv(n, kAlignChunk) : 0;
     if (nchunks > 0) {
         align_count_kernel<<<nchunks, 256, sizeof(int32_t) * E, s>>>(ids, n, E, counts);
@@ -318,7 +207,7 @@ cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int3
     align_scan_kernel<<<1, 1024, 0, s>>>(counts, nchunks, n, E, sorted, expert_ids, num_post_pad, expert_off);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || nchunks == 0) return e;
-    align_scatter_kernel<<<nchunks, 256, sizeof(int32_t) * 9 * E, s>>>(ids, n, E, counts, sorted);
+    align_scatter_kernel<<<nchunks, 256, sizeof(int32_t) * 9 * E, s>>>(ids, n, E, counts, sorted, slot_of);
     return cudaGetLastError();
 }
 

@@ -156,8 +156,8 @@ def topk(logits: torch.Tensor, k: int):
 
 
 def align(ids: torch.Tensor, E: int, out=None):
-    """-> sorted_ids [max_slots], expert_ids [max_slots/128], num_post_pad [1], expert_off [E+1] (and the
-    per-chunk count scratch when ``out`` is given as a 5-tuple)."""
+    """-> sorted_ids [max_slots], expert_ids [max_slots/128], num_post_pad [1], expert_off [E+1],
+    slot_of [T*k] and the per-chunk count scratch."""
     _cuda(ids, "ids", torch.int32)
     T, k = ids.shape
     ms = _lib.max_slots(T, E, k)
@@ -166,26 +166,30 @@ def align(ids: torch.Tensor, E: int, out=None):
         out = (torch.full((ms,), -1, dtype=torch.int32, device=dev),
                torch.full((ms // 128,), -1, dtype=torch.int32, device=dev),
                torch.zeros(1, dtype=torch.int32, device=dev), torch.zeros(E + 1, dtype=torch.int32, device=dev),
+               torch.zeros(T * k, dtype=torch.int32, device=dev),
                torch.zeros(max(1, -(-T * k // 4096)) * E, dtype=torch.int32, device=dev))
-    sorted_ids, expert_ids, npp, off, scratch = out
-    _lib.call("pm_moe_align", _p(ids), T, k, E, _p(sorted_ids), _p(expert_ids), _p(npp), _p(off), _p(scratch),
-              scratch.numel() * 4, _stream(dev))
-    return sorted_ids, expert_ids, npp, off, scratch
+    sorted_ids, expert_ids, npp, off, slot_of, scratch = out
+    _lib.call("pm_moe_align", _p(ids), T, k, E, _p(sorted_ids), _p(expert_ids), _p(npp), _p(off), _p(slot_of),
+              _p(scratch), scratch.numel() * 4, _stream(dev))
+    return sorted_ids, expert_ids, npp, off, slot_of, scratch
 
 
-def permute_quant_fp8(x: torch.Tensor, sorted_ids: torch.Tensor, npp: torch.Tensor, k: int, out=None):
+def quant_fp8(x: torch.Tensor, slot_of: torch.Tensor | None = None, k: int = 1, max_slots: int = 0, out=None):
+    """Per-token, per-128-column e4m3 quantisation of x [T, H] bf16.  Without ``slot_of``: (x_q [T, H] u8,
+    x_s [T, H/128] f32).  With it: the rows land in the k slots of each token (a_q [max_slots, H], a_s)."""
     T, H = x.shape
-    ms = sorted_ids.numel()
+    _cuda(x, "x", torch.bfloat16)
+    rows = T if slot_of is None else max_slots
     if out is None:
-        out = (torch.zeros(ms, H, dtype=torch.uint8, device=x.device),
-               torch.zeros(ms, H // 128, dtype=torch.float32, device=x.device))
-    a_q, a_s = out
-    _lib.call("pm_moe_permute_quant_fp8", _p(x), T, H, k, _p(sorted_ids), _p(npp), ms, _p(a_q), _p(a_s),
-              _stream(x.device))
-    return a_q, a_s
+        out = (torch.zeros(rows, H, dtype=torch.uint8, device=x.device),
+               torch.zeros(rows, H // 128, dtype=torch.float32, device=x.device))
+    x_q, x_s = out
+    _lib.call("pm_moe_quant_fp8", _p(x), T, H, k, _p(slot_of), _p(x_q), _p(x_s), _stream(x.device))
+    return x_q, x_s
 
 
 def gemm1_fp8(a_q, a_s, w1, w1_s, expert_ids, npp, out=None):
+    """gate_up GEMM over expert-ordered slots (a_q [max_slots, H], a_s [max_slots, H/128])."""
     ms, H = a_q.shape
     E, I2, _ = w1.shape
     I = I2 // 2

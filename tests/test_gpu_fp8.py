@@ -114,7 +114,7 @@ def test_align_matches_oracle(T, E_, k_):
     ids = torch.stack([torch.randperm(E_, generator=g)[:k_] for _ in range(T)]).to(torch.int32)
     if T >= 7:
         ids[:, 0] = 0  # a hot expert
-    s, eids, npp, off, _ = ops.align(ids.to(DEV), E_)
+    s, eids, npp, off, slot_of, _ = ops.align(ids.to(DEV), E_)
     rs, re, rn = O.align(bits(ids), E_, 128)
     n = int(npp.item())
     assert n == rn
@@ -122,6 +122,8 @@ def test_align_matches_oracle(T, E_, k_):
     assert np.array_equal(bits(eids)[: n // 128], re)
     offs = bits(off)
     assert offs[E_] == n
+    inv = bits(slot_of)  # the inverse permutation: slot_of[flat] = slot
+    assert np.array_equal(bits(s)[inv], np.arange(T * k_))
     for e in range(E_):
         blk = re == e
         if blk.any():
@@ -130,7 +132,7 @@ def test_align_matches_oracle(T, E_, k_):
 
 def test_align_docstring_example(golden):
     kat = golden("align_kat")
-    s, eids, npp, _, _ = ops.align(torch.from_numpy(kat["ids"]).to(DEV), int(kat["num_experts"]))
+    s, eids, npp, _, _, _ = ops.align(torch.from_numpy(kat["ids"]).to(DEV), int(kat["num_experts"]))
     # block 128 instead of the docstring's 4: same grouping and order, wider padding
     rs, re, rn = O.align(kat["ids"], int(kat["num_experts"]), 128)
     n = int(npp.item())
@@ -140,20 +142,19 @@ def test_align_docstring_example(golden):
     assert np.array_equal(bits(eids)[:4], [1, 2, 3, 4])
 
 
-def test_permute_quant_matches_oracle(layer):
+def test_quant_matches_oracle(layer):
     L, gpu = layer
-    T = 512
-    logits, w, ids = ops.router_topk(gpu["x"], gpu["router_w"], K)
-    s, eids, npp, _, _ = ops.align(ids, E)
-    a_q, a_s = ops.permute_quant_fp8(gpu["x"], s, npp, K)
-    n = int(npp.item())
+    x_q, x_s = ops.quant_fp8(gpu["x"])
     xq, xs = O.quant_fp8_groups(bits(L["x"]))
-    sv = bits(s)[:n]
-    real = sv < T * K
-    tok = sv[real] // K
-    assert np.array_equal(bits(a_q)[:n][real], xq[tok])
-    assert np.array_equal(bits(a_s)[:n][real], xs[tok])
-    assert np.all(bits(a_q)[:n][~real] == 0) and np.all(bits(a_s)[:n][~real] == 0)
+    assert np.array_equal(bits(x_q), xq)
+    assert np.array_equal(bits(x_s), xs)
+
+
+def test_quant_edge_rows_match_vllm_golden(golden):
+    g = golden("act_quant")
+    x_q, x_s = ops.quant_fp8(from_bits_bf16(g["x"]).to(DEV))
+    assert np.array_equal(bits(x_q), g["q"])
+    assert np.array_equal(bits(x_s), g["s"])
 
 
 # ------------------------------------------------------------------------------------------- GEMMs
@@ -161,8 +162,8 @@ def test_gemm1_matches_oracle(layer):
     L, gpu = layer
     T = 512
     _, w, ids = ops.router_topk(gpu["x"], gpu["router_w"], K)
-    s, eids, npp, _, _ = ops.align(ids, E)
-    a_q, a_s = ops.permute_quant_fp8(gpu["x"], s, npp, K)
+    s, eids, npp, _, slot_of, _ = ops.align(ids, E)
+    a_q, a_s = ops.quant_fp8(gpu["x"], slot_of, K, s.numel())
     out_q, out_s, err = ops.gemm1_fp8(a_q, a_s, gpu["w1"], gpu["w1_s"], eids, npp)
     torch.cuda.synchronize()
     assert int(err.item()) == 0
@@ -171,6 +172,9 @@ def test_gemm1_matches_oracle(layer):
     real = np.nonzero(sv < T * K)[0]
     rows = real[:: max(1, len(real) // 600)]  # a spread sample of slots across experts
     row_e = bits(eids)[rows // 128]
+    xq, xs = O.quant_fp8_groups(bits(L["x"]))
+    tok = sv[rows] // K
+    assert np.array_equal(bits(a_q)[rows], xq[tok]) and np.array_equal(bits(a_s)[rows], xs[tok])
     c1 = O.gemm_fp8_rows(bits(a_q)[rows], bits(a_s)[rows], row_e, bits(L["w1"]), bits(L["w1_s"]))
     c1b = O.f32_to_bf16(c1)
     c2 = O.silu_mul(c1b[:, :I], c1b[:, I:])
@@ -187,8 +191,8 @@ def test_gemm2_matches_oracle(layer):
     L, gpu = layer
     T = 512
     _, w, ids = ops.router_topk(gpu["x"], gpu["router_w"], K)
-    s, eids, npp, _, _ = ops.align(ids, E)
-    a_q, a_s = ops.permute_quant_fp8(gpu["x"], s, npp, K)
+    s, eids, npp, _, slot_of, _ = ops.align(ids, E)
+    a_q, a_s = ops.quant_fp8(gpu["x"], slot_of, K, s.numel())
     out_q, out_s, _ = ops.gemm1_fp8(a_q, a_s, gpu["w1"], gpu["w1_s"], eids, npp)
     c3, err = ops.gemm2_fp8(out_q, out_s, gpu["w2"], gpu["w2_s"], eids, npp, s, w.reshape(-1), T, K)
     torch.cuda.synchronize()

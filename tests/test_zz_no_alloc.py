@@ -51,7 +51,7 @@ def test_noalloc_matches_the_workspace_entry_point_twice_in_a_row(T, E, k):
         ids = _ids(T, E, k, seed + T)
         st, s, eids, npp, off = _noalloc(ids, E)
         assert st == 0, _lib.load().pm_moe_status_string(st)
-        rs, reids, rnpp, roff, _ = ops.align(ids, E)
+        rs, reids, rnpp, roff, _, _ = ops.align(ids, E)
         torch.cuda.synchronize()
         n = int(rnpp.item())
         assert int(npp.item()) == n, f"call {call}"
