@@ -132,6 +132,44 @@ int pm_moe_forward_fp8(const void *x, const void *router_w, const void *logits, 
                        const float *w1_s, const uint8_t *w2, const float *w2_s, int T, int H, int I, int E, int k,
                        void *out, void *workspace, size_t workspace_bytes, pm_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------------------------
+ * NVFP4 (e2m1 values, one e4m3 scale per 16 elements, one fp32 global scale per tensor): the routed path of
+ * prismyra/kernels/nvfp4.py:112-312 (FusedExpertsFp4, which calls FlashInfer's cutlass_fused_moe).
+ * Packed e2m1: two values per byte, the even column in the low nibble (prismyra/kernels/nvfp4.py:50).
+ * Scale layout ("blocked"): a matrix of R rows and K/16 scales per row is [R/128][K/64][512 bytes]; in a block,
+ * row r (0..127) stores its four scales of the 64-column chunk as one 32-bit word at byte (r%32)*16 + (r/32)*4.
+ * Weights: w1 u8 [E, 2I, H/2] (gate rows then up rows, as in prepare_layer), w1_sf blocked [E][2I/128][H/64][512];
+ * w2 u8 [E, H, I/2], w2_sf blocked [E][H/128][I/64][512]; alpha1/alpha2 f32 [E] = 1/(g_w[e] * a_gs)
+ * (prismyra/kernels/nvfp4.py:141-142).  Extra shape limit: I % 256 == 0.
+ * --------------------------------------------------------------------------------------------------------------- */
+
+/* NVFP4 quantisation of token rows with global scale gs (vllm/model_executor/layers/quantization/utils/
+ * nvfp4_emulation_utils.py:172-216; the reference's ops.scaled_fp4_quant call at prismyra/kernels/nvfp4.py:260).
+ * slot_of == NULL: row t of a_q [T, H/2] / blocked a_sf; otherwise the token's k slots. */
+int pm_moe_quant_nvfp4(const void *x, int T, int H, int k, const int32_t *slot_of, float gs, uint8_t *a_q,
+                       uint8_t *a_sf, pm_stream_t stream);
+
+/* NVFP4 grouped gate_up GEMM: alpha1[e] * (A . W1^T) -> bf16 -> silu*mul -> bf16 -> NVFP4 with a2_gs
+ * (FlashInfer FC1 + activation + requantisation inside cutlass_fused_moe, prismyra/kernels/nvfp4.py:262-287). */
+int pm_moe_gemm1_nvfp4(const uint8_t *a_q, const uint8_t *a_sf, const uint8_t *w1, const uint8_t *w1_sf,
+                       const float *alpha1, float a2_gs, const int32_t *expert_ids, const int32_t *num_post_pad,
+                       int max_slots, int H, int I, int E, uint8_t *out_q, uint8_t *out_sf, int32_t *err,
+                       pm_stream_t stream);
+
+/* NVFP4 grouped down GEMM: bf16(alpha2[e] * (A . W2^T) * routing weight) scattered to c3[t*k + j]
+ * (FlashInfer FC2 + finalize, prismyra/kernels/nvfp4.py:262-287). */
+int pm_moe_gemm2_nvfp4(const uint8_t *a_q, const uint8_t *a_sf, const uint8_t *w2, const uint8_t *w2_sf,
+                       const float *alpha2, const int32_t *expert_ids, const int32_t *num_post_pad,
+                       const int32_t *sorted_ids, const float *topk_w, int max_slots, int T, int k, int H, int I,
+                       int E, void *c3, int32_t *err, pm_stream_t stream);
+
+/* The whole routed NVFP4 layer: prismyra/kernels/nvfp4.py:147-170 (FusedExpertsFp4.forward) minus the shared
+ * expert.  a1_gs / a2_gs are the activation global scales (nvfp4.py:125-126). */
+int pm_moe_forward_nvfp4(const void *x, const void *router_w, const void *logits, const uint8_t *w1,
+                         const uint8_t *w1_sf, const float *alpha1, float a1_gs, const uint8_t *w2,
+                         const uint8_t *w2_sf, const float *alpha2, float a2_gs, int T, int H, int I, int E, int k,
+                         void *out, void *workspace, size_t workspace_bytes, pm_stream_t stream);
+
 /* Expert alignment that allocates nothing -- no counterpart in the reference.  Same results as pm_moe_align,
  * for callers that cannot hand the library scratch memory on demand: hosts that route every device byte through
  * their own pool and forbid library allocations, and latency-critical loops that cannot afford the implicit

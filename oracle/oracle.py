@@ -222,3 +222,25 @@ def moe_forward_nvfp4(x_bits, logits_bits, w1, s1, w2, s2, alpha1, alpha2, a1_gs
         ctypes.c_float(a2_gs), T, H, I, E, k, _p(out), _p(c3),
     )
     return {"out": out, "c3": c3}
+
+
+def gemm_nvfp4_rows(a, a_sf, row_expert, w, w_sf, alpha) -> np.ndarray:
+    a = _c(a, np.uint8)
+    a_sf = _c(a_sf, np.uint8)
+    re = _c(row_expert, np.int32)
+    w = _c(w, np.uint8)
+    w_sf = _c(w_sf, np.uint8)
+    al = _c(alpha, np.float32)
+    rows, K2 = a.shape
+    E, N, _ = w.shape
+    out = np.empty((rows, N), np.float32)
+    lib().or_gemm_nvfp4_rows(_p(a), _p(a_sf), _p(re), rows, _p(w), _p(w_sf), _p(al), N, K2 * 2, _p(out))
+    return out
+
+
+def nvfp4_dequant(packed, sf, gs: float) -> np.ndarray:
+    """Values of an NVFP4 tensor (unblocked scales [R, K/16]) divided by its global scale."""
+    v = e2m1_unpack(packed)
+    R, K = v.shape
+    s = e4m3_to_f32(sf).reshape(R, K // 16, 1) / np.float32(gs)
+    return (v.reshape(R, K // 16, 16) * s).reshape(R, K).astype(np.float32)

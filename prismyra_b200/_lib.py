@@ -46,6 +46,11 @@ SIGNATURES: dict[str, tuple] = {
     "pm_moe_forward_fp8": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _Z, _P]),
     "pm_moe_read_status": (_I, [_P, _P]),
     "pm_moe_align_noalloc": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P]),
+    "pm_moe_quant_nvfp4": (_I, [_P, _I, _I, _I, _P, ctypes.c_float, _P, _P, _P]),
+    "pm_moe_gemm1_nvfp4": (_I, [_P, _P, _P, _P, _P, ctypes.c_float, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "pm_moe_gemm2_nvfp4": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
+    "pm_moe_forward_nvfp4": (_I, [_P, _P, _P, _P, _P, _P, ctypes.c_float, _P, _P, _P, ctypes.c_float, _I, _I, _I,
+                                  _I, _I, _P, _P, _Z, _P]),
 }
 
 

@@ -344,6 +344,146 @@ int pm_moe_forward_fp8(const void* x, const void* router_w, const void* logits, 
     return cuda_status(launch_combine(c3, T, k, H, out, s));
 }
 
+int pm_moe_quant_nvfp4(const void* x, int T, int H, int k, const int32_t* slot_of, float gs, uint8_t* a_q,
+                       uint8_t* a_sf, pm_stream_t stream) {
+    if (T < 0 || H <= 0 || (slot_of != nullptr && k <= 0) || !(gs > 0.0f)) return PM_ERR_INVALID;
+    if (H % 64 != 0) return PM_ERR_SHAPE;
+    if (T == 0) return PM_OK;
+    if (!x || !a_q || !a_sf) return PM_ERR_INVALID;
+    if (!a16(x) || !a16(a_q) || !a16(a_sf)) return PM_ERR_ALIGN;
+    DeviceInfo d;
+    const int st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    return cuda_status(launch_quant_nvfp4(x, T, H, k, slot_of, gs, a_q, a_sf, (cudaStream_t)stream));
+}
+
+static int check_nvfp4_dims(int T, int H, int I, int E, int k) {
+    const int st = check_dims(T, H, I, E, k);
+    if (st != PM_OK) return st;
+    return (I % 256 == 0) ? PM_OK : PM_ERR_SHAPE;
+}
+
+int pm_moe_gemm1_nvfp4(const uint8_t* a_q, const uint8_t* a_sf, const uint8_t* w1, const uint8_t* w1_sf,
+                       const float* alpha1, float a2_gs, const int32_t* expert_ids, const int32_t* num_post_pad,
+                       int max_slots, int H, int I, int E, uint8_t* out_q, uint8_t* out_sf, int32_t* err,
+                       pm_stream_t stream) {
+    int st = check_nvfp4_dims(0, H, I, E, 1);
+    if (st != PM_OK) return st;
+    if (max_slots < 0 || max_slots % kBlockM != 0 || !(a2_gs > 0.0f)) return PM_ERR_SHAPE;
+    if (max_slots == 0) return PM_OK;
+    if (!a_q || !a_sf || !w1 || !w1_sf || !alpha1 || !expert_ids || !num_post_pad || !out_q || !out_sf)
+        return PM_ERR_INVALID;
+    if (!a16(a_q) || !a16(a_sf) || !a16(w1) || !a16(w1_sf) || !a16(out_q) || !a16(out_sf)) return PM_ERR_ALIGN;
+    DeviceInfo d;
+    st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    CUtensorMap ta, tb;
+    if (!encode_tmap_2d_u8(&ta, a_q, (uint64_t)H / 2, (uint64_t)max_slots, (uint64_t)H / 2, 128, 128) ||
+        !encode_tmap_2d_u8(&tb, w1, (uint64_t)H / 2, (uint64_t)E * 2 * I, (uint64_t)H / 2, 128, 128))
+        return PM_ERR_CUDA;
+    NvGemmArgs g;
+    memset(&g, 0, sizeof(g));
+    g.a_sf = a_sf;
+    g.b_sf = w1_sf;
+    g.alpha = alpha1;
+    g.expert_ids = expert_ids;
+    g.num_post_pad = num_post_pad;
+    g.n_total = 2 * I;
+    g.K = H;
+    g.n_tiles = I / 128;
+    g.max_tiles = (max_slots / kBlockM) * g.n_tiles;
+    g.inter = I;
+    g.gs_out = a2_gs;
+    g.out_q = out_q;
+    g.out_sf = out_sf;
+    g.err = err;
+    return cuda_status(launch_gemm_nvfp4(0, ta, tb, g, d.sms, (cudaStream_t)stream));
+}
+
+int pm_moe_gemm2_nvfp4(const uint8_t* a_q, const uint8_t* a_sf, const uint8_t* w2, const uint8_t* w2_sf,
+                       const float* alpha2, const int32_t* expert_ids, const int32_t* num_post_pad,
+                       const int32_t* sorted_ids, const float* topk_w, int max_slots, int T, int k, int H, int I,
+                       int E, void* c3, int32_t* err, pm_stream_t stream) {
+    int st = check_nvfp4_dims(T, H, I, E, k);
+    if (st != PM_OK) return st;
+    if (max_slots < 0 || max_slots % kBlockM != 0) return PM_ERR_SHAPE;
+    if (max_slots == 0 || T == 0) return PM_OK;
+    if (!a_q || !a_sf || !w2 || !w2_sf || !alpha2 || !expert_ids || !num_post_pad || !sorted_ids || !topk_w || !c3)
+        return PM_ERR_INVALID;
+    if (!a16(a_q) || !a16(a_sf) || !a16(w2) || !a16(w2_sf) || !a16(c3)) return PM_ERR_ALIGN;
+    DeviceInfo d;
+    st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    CUtensorMap ta, tb;
+    if (!encode_tmap_2d_u8(&ta, a_q, (uint64_t)I / 2, (uint64_t)max_slots, (uint64_t)I / 2, 128, 128) ||
+        !encode_tmap_2d_u8(&tb, w2, (uint64_t)I / 2, (uint64_t)E * H, (uint64_t)I / 2, 128, 128))
+        return PM_ERR_CUDA;
+    NvGemmArgs g;
+    memset(&g, 0, sizeof(g));
+    g.a_sf = a_sf;
+    g.b_sf = w2_sf;
+    g.alpha = alpha2;
+    g.expert_ids = expert_ids;
+    g.num_post_pad = num_post_pad;
+    g.n_total = H;
+    g.K = I;
+    g.n_tiles = H / 256;
+    g.max_tiles = (max_slots / kBlockM) * g.n_tiles;
+    g.inter = I;
+    g.sorted_ids = sorted_ids;
+    g.topk_w = topk_w;
+    g.c3 = static_cast<__nv_bfloat16*>(c3);
+    g.n_valid = T * k;
+    g.err = err;
+    return cuda_status(launch_gemm_nvfp4(1, ta, tb, g, d.sms, (cudaStream_t)stream));
+}
+
+int pm_moe_forward_nvfp4(const void* x, const void* router_w, const void* logits, const uint8_t* w1,
+                         const uint8_t* w1_sf, const float* alpha1, float a1_gs, const uint8_t* w2,
+                         const uint8_t* w2_sf, const float* alpha2, float a2_gs, int T, int H, int I, int E, int k,
+                         void* out, void* workspace, size_t workspace_bytes, pm_stream_t stream) {
+    int st = check_nvfp4_dims(T, H, I, E, k);
+    if (st != PM_OK) return st;
+    if (T == 0) return PM_OK;
+    if (!x || !w1 || !w1_sf || !alpha1 || !w2 || !w2_sf || !alpha2 || !out || !workspace || (!router_w && !logits))
+        return PM_ERR_INVALID;
+    if (!(a1_gs > 0.0f) || !(a2_gs > 0.0f)) return PM_ERR_INVALID;
+    if (!a16(x) || !a16(w1) || !a16(w2) || !a16(out) || !a16(workspace) || (router_w && !logits && !a16(router_w)))
+        return PM_ERR_ALIGN;
+    const Layout L = layout_of(T, H, I, E, k, PM_FMT_NVFP4);
+    if (workspace_bytes < L.total) return PM_ERR_WORKSPACE;
+    DeviceInfo d;
+    st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    auto R = [&](int r) { return ws + L.off[r]; };
+    int32_t* status = reinterpret_cast<int32_t*>(R(PM_WS_STATUS));
+    float* topk_w = reinterpret_cast<float*>(R(PM_WS_TOPK_W));
+    int32_t* topk_ids = reinterpret_cast<int32_t*>(R(PM_WS_TOPK_IDS));
+    int32_t* sorted = reinterpret_cast<int32_t*>(R(PM_WS_SORTED));
+    int32_t* expert_ids = reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_IDS));
+    int32_t* npp = reinterpret_cast<int32_t*>(R(PM_WS_NUM_POST_PAD));
+    int32_t* slot_of = reinterpret_cast<int32_t*>(R(PM_WS_SLOT_OF));
+    if (cudaMemsetAsync(status, 0, L.len[PM_WS_STATUS], s) != cudaSuccess) return PM_ERR_CUDA;
+    cudaError_t e = logits != nullptr
+                        ? launch_topk(logits, T, E, k, topk_w, topk_ids, s)
+                        : launch_router_topk(x, router_w, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s);
+    if (e != cudaSuccess) return PM_ERR_CUDA;
+    e = launch_align(topk_ids, T * k, E, reinterpret_cast<int32_t*>(R(PM_WS_COUNTS)), sorted, expert_ids, npp,
+                     reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_OFF)), slot_of, s);
+    if (e != cudaSuccess) return PM_ERR_CUDA;
+    e = launch_quant_nvfp4(x, T, H, k, slot_of, a1_gs, R(PM_WS_A1), R(PM_WS_A1_SCALE), s);
+    if (e != cudaSuccess) return PM_ERR_CUDA;
+    st = pm_moe_gemm1_nvfp4(R(PM_WS_A1), R(PM_WS_A1_SCALE), w1, w1_sf, alpha1, a2_gs, expert_ids, npp, L.max_slots,
+                            H, I, E, R(PM_WS_A2), R(PM_WS_A2_SCALE), status, stream);
+    if (st != PM_OK) return st;
+    st = pm_moe_gemm2_nvfp4(R(PM_WS_A2), R(PM_WS_A2_SCALE), w2, w2_sf, alpha2, expert_ids, npp, sorted, topk_w,
+                            L.max_slots, T, k, H, I, E, R(PM_WS_C3), status, stream);
+    if (st != PM_OK) return st;
+    return cuda_status(launch_combine(R(PM_WS_C3), T, k, H, out, s));
+}
+
 int pm_moe_read_status(const void* workspace, pm_stream_t stream) {
     if (!workspace) return PM_ERR_INVALID;
     int32_t flag = 0;

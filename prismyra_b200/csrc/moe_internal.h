@@ -56,6 +56,31 @@ struct GemmArgs {
 cudaError_t launch_gemm_fp8(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, const GemmArgs& args,
                             int num_sms, cudaStream_t s);
 
+struct NvGemmArgs {
+    const uint8_t* a_sf;          // blocked e4m3 scales of A: [rows/128][K/64][512]
+    const uint8_t* b_sf;          // blocked e4m3 scales of B: [E][n_total/128][K/64][512]
+    const float* alpha;           // [E] 1 / (weight global scale * activation global scale)
+    const int32_t* expert_ids;
+    const int32_t* num_post_pad;
+    int n_total, K, n_tiles, max_tiles, inter;
+    // gate_up epilogue: NVFP4 re-quantisation of silu(gate)*up with the layer's second activation scale
+    float gs_out;
+    uint8_t* out_q;               // packed e2m1 [rows, I/2]
+    uint8_t* out_sf;              // blocked [rows/128][I/64][512]
+    // down epilogue
+    const int32_t* sorted_ids;
+    const float* topk_w;
+    __nv_bfloat16* c3;
+    int n_valid;
+    int* err;
+};
+
+// NVFP4 quantisation of token rows (global scale gs), written to each token's k slots when slot_of is given.
+cudaError_t launch_quant_nvfp4(const void* x, int T, int H, int k, const int32_t* slot_of, float gs, uint8_t* a_q,
+                               uint8_t* a_sf, cudaStream_t s);
+cudaError_t launch_gemm_nvfp4(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, const NvGemmArgs& args,
+                              int num_sms, cudaStream_t s);
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda): a 2-D row-major
 // tensor of `outer` rows x `inner` elements, rows `row_bytes` apart, 128-byte swizzled boxes.
 bool encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t inner,

@@ -221,3 +221,87 @@ def combine(c3: torch.Tensor, T: int, k: int, out=None):
         out = torch.empty(T, H, dtype=torch.bfloat16, device=c3.device)
     _lib.call("pm_moe_combine", _p(c3), T, k, H, _p(out), _stream(c3.device))
     return out
+
+
+# ------------------------------------------------------------------------------------------- NVFP4
+def forward_nvfp4(x: torch.Tensor, w1: torch.Tensor, w1_sf: torch.Tensor, alpha1: torch.Tensor, a1_gs: float,
+                  w2: torch.Tensor, w2_sf: torch.Tensor, alpha2: torch.Tensor, a2_gs: float, top_k: int,
+                  router_w: torch.Tensor | None = None, logits: torch.Tensor | None = None,
+                  out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed NVFP4 experts for x [T, H] bf16.  w1 u8 [E, 2I, H/2], w1_sf blocked [E, 2I/128, H/64, 512],
+    w2 u8 [E, H, I/2], w2_sf blocked [E, H/128, I/64, 512], alphas f32 [E]."""
+    _need(x.dim() == 2, "x must be [T, H]")
+    T, H = x.shape
+    E, I2, _ = w1.shape
+    I = I2 // 2
+    _cuda(x, "x", torch.bfloat16)
+    _cuda(w1, "w1", torch.uint8, (E, 2 * I, H // 2))
+    _cuda(w2, "w2", torch.uint8, (E, H, I // 2))
+    _cuda(w1_sf, "w1_sf", torch.uint8, (E, 2 * I // 128, H // 64, 512))
+    _cuda(w2_sf, "w2_sf", torch.uint8, (E, H // 128, I // 64, 512))
+    _cuda(alpha1, "alpha1", torch.float32, (E,))
+    _cuda(alpha2, "alpha2", torch.float32, (E,))
+    _need(router_w is not None or logits is not None, "give router_w or logits")
+    if logits is not None:
+        _cuda(logits, "logits", torch.bfloat16, (T, E))
+    else:
+        _cuda(router_w, "router_w", torch.bfloat16, (E, H))
+    if out is None:
+        out = torch.empty_like(x)
+    if T == 0:
+        return out
+    if workspace is None:
+        workspace, nbytes = workspace_for(x, T, H, I, E, top_k, _lib.FMT_NVFP4)
+    else:
+        nbytes = workspace.numel()
+    _lib.call(
+        "pm_moe_forward_nvfp4", _p(x), _p(router_w), _p(logits), _p(w1), _p(w1_sf), _p(alpha1),
+        ctypes.c_float(a1_gs), _p(w2), _p(w2_sf), _p(alpha2), ctypes.c_float(a2_gs), T, H, I, E, top_k, _p(out),
+        _p(workspace), nbytes, _stream(x.device),
+    )
+    return out
+
+
+def quant_nvfp4(x: torch.Tensor, gs: float, slot_of: torch.Tensor | None = None, k: int = 1, max_slots: int = 0,
+                out=None):
+    """NVFP4 quantisation of x [T, H] bf16 -> (packed [rows, H/2] u8, blocked scales [rows/128, H/64, 512] u8);
+    rows = T (slot_of None, T padded up to 128 for the scale blocks) or max_slots."""
+    T, H = x.shape
+    _cuda(x, "x", torch.bfloat16)
+    rows = T if slot_of is None else max_slots
+    rb = -(-rows // 128)
+    if out is None:
+        out = (torch.zeros(rows, H // 2, dtype=torch.uint8, device=x.device),
+               torch.zeros(rb, H // 64, 512, dtype=torch.uint8, device=x.device))
+    q, sf = out
+    _lib.call("pm_moe_quant_nvfp4", _p(x), T, H, k, _p(slot_of), ctypes.c_float(gs), _p(q), _p(sf),
+              _stream(x.device))
+    return q, sf
+
+
+def gemm1_nvfp4(a_q, a_sf, w1, w1_sf, alpha1, a2_gs: float, expert_ids, npp, out=None):
+    ms, H2 = a_q.shape
+    H = 2 * H2
+    E, I2, _ = w1.shape
+    I = I2 // 2
+    if out is None:
+        out = (torch.zeros(ms, I // 2, dtype=torch.uint8, device=a_q.device),
+               torch.zeros(ms // 128, I // 64, 512, dtype=torch.uint8, device=a_q.device),
+               torch.zeros(1, dtype=torch.int32, device=a_q.device))
+    oq, osf, err = out
+    _lib.call("pm_moe_gemm1_nvfp4", _p(a_q), _p(a_sf), _p(w1), _p(w1_sf), _p(alpha1), ctypes.c_float(a2_gs),
+              _p(expert_ids), _p(npp), ms, H, I, E, _p(oq), _p(osf), _p(err), _stream(a_q.device))
+    return oq, osf, err
+
+
+def gemm2_nvfp4(a_q, a_sf, w2, w2_sf, alpha2, expert_ids, npp, sorted_ids, topk_w, T: int, k: int, out=None):
+    ms, I2 = a_q.shape
+    I = 2 * I2
+    E, H, _ = w2.shape
+    if out is None:
+        out = (torch.zeros(T * k, H, dtype=torch.bfloat16, device=a_q.device),
+               torch.zeros(1, dtype=torch.int32, device=a_q.device))
+    c3, err = out
+    _lib.call("pm_moe_gemm2_nvfp4", _p(a_q), _p(a_sf), _p(w2), _p(w2_sf), _p(alpha2), _p(expert_ids), _p(npp),
+              _p(sorted_ids), _p(topk_w), ms, T, k, H, I, E, _p(c3), _p(err), _stream(a_q.device))
+    return c3, err

@@ -80,3 +80,27 @@ def layer_bytes(T: int, experts_hit: int, H: int = 2048, I: int = 768, E: int = 
 def expected_experts_hit(T: int, E: int = 128, k: int = 8) -> float:
     """Expected number of experts with >= 1 token under uniform routing of T tokens, k distinct experts each."""
     return E * (1.0 - math.pow(1.0 - k / E, T))
+
+
+def make_nvfp4_layer(fp8: dict, calib_tokens: int = 256, top_k: int = 8) -> dict:
+    """NVFP4 weights from an FP8 synthetic layer (the reference's prepare_layer recipe) plus a synthetic activation
+    calibration: w13_in_amax = max|x|, w2_in_amax = max|silu(gate)*up| over the first ``calib_tokens`` tokens routed
+    by the layer's own router, computed in fp32 from the dequantised FP8 weights (no calibration file exists for
+    synthetic data)."""
+    from .kernels import nvfp4
+
+    dev = fp8["w1"].device
+    prep = nvfp4.prepare_layer(fp8["w1"], fp8["w1_s"], fp8["w2"], fp8["w2_s"], dev)
+    x = fp8["x"][:calib_tokens].float()
+    logits = (x @ fp8["router_w"].float().t()).to(torch.bfloat16).float()
+    ids = torch.topk(torch.softmax(logits, -1), top_k, dim=-1).indices
+    amax2 = 0.0
+    I = fp8["w1"].shape[1] // 2
+    for e in ids.unique().tolist():
+        rows = (ids == e).any(-1)
+        w = dequantize_fp8_blocks(fp8["w1"][e], fp8["w1_s"][e])
+        h = x[rows] @ w.t()
+        a = torch.nn.functional.silu(h[:, :I]) * h[:, I:]
+        amax2 = max(amax2, float(a.abs().max()))
+    act = {"w13_in_amax": float(fp8["x"].float().abs().max()), "w2_in_amax": [amax2]}
+    return {"prepared": prep, "act": act}
