@@ -30,7 +30,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "MoE-layer tokens/s and % FP8/FP4 tensor peak at T=5120; HBM GB/s at T=128"
 H, I, E, K = 2048, 768, 128, 8
 T_CTX, T_BRANCH, T_CPU_SAMPLE = 5120, 128, 512
-KERNELS_PER_STEP = 8  # router+top-k, 3 alignment passes, activation quant, gate_up GEMM, down GEMM, combine
+KERNELS_PER_STEP = 9  # router GEMM, top-k, 3 alignment passes, activation quant, gate_up, down, combine
 
 
 def peaks() -> dict:
@@ -297,6 +297,29 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
     b_bytes = synth.layer_bytes(T_BRANCH, b_st["experts_hit"], H, I, E)
     b_gbs = b_bytes / (b_ms * 1e-3) / 1e9
 
+    # NVFP4 variant at T=5120: weights from the same FP8 layer via the reference's
+    # prepare_layer recipe, synthetic activation calibration
+    from prismyra_b200.kernels import nvfp4
+
+    nv = synth.make_nvfp4_layer(layer)
+    prep, act = nv["prepared"], nv["act"]
+    a1 = float(448.0 * 6.0 / (1.25 * act["w13_in_amax"]))
+    a2 = float(448.0 * 6.0 / (1.25 * max(act["w2_in_amax"])))
+    nw = {"w1": prep["w1"].to(dev), "w2": prep["w2"].to(dev), "w1_sf": nvfp4.block_scales(prep["s1"]).to(dev),
+          "w2_sf": nvfp4.block_scales(prep["s2"]).to(dev), "al1": (1.0 / (prep["g1"] * a1)).float().to(dev),
+          "al2": (1.0 / (prep["g2"] * a2)).float().to(dev)}
+    del nv, prep
+
+    def nv_step():
+        return ops.forward_nvfp4(x, nw["w1"], nw["w1_sf"], nw["al1"], a1, nw["w2"], nw["w2_sf"], nw["al2"], a2, K,
+                                 router_w=layer["router_w"])
+
+    for _ in range(5):
+        nv_step()
+    nv_ms = time_region(nv_step, max(20, args.steps), stream)
+    nv_tflops = fl["total"] / (nv_ms * 1e-3) / 1e12
+    fp4_peak = 4.0 * pk["bf16_tflops"]  # B200 FP4 dense rate is four times its BF16 dense rate
+
     if rank != 0:
         return
     cb = None
@@ -324,6 +347,9 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
                         "stages_ms": {k: round(v, 4) for k, v in b_st.items() if isinstance(v, float)}},
         "e2e": {"value": world * T_CTX / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": T_CTX * H * 2, "d2h_bytes_per_step": T_CTX * H * 2},
+        "nvfp4_t5120": {"ms": nv_ms, "tokens_per_s": T_CTX / (nv_ms * 1e-3), "tflops": nv_tflops,
+                        "frac_fp4_peak": nv_tflops / fp4_peak, "fp4_peak": fp4_peak,
+                        "weights": "NVFP4 from the FP8 layer (reference prepare_layer recipe), synthetic calibration"},
         "gpu_launches": KERNELS_PER_STEP * args.steps,
         "clocks": clk.summary(),
     }

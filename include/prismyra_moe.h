@@ -82,7 +82,7 @@ int pm_moe_workspace_region(int T, int H, int I, int E, int k, int fmt, int regi
 /* Router projection + softmax + top-k + renormalise, row-count invariant.  Replaces
  * prismyra/kernels/qwen3_moe.py:169-171 (FusedExperts._route) followed by :196 (vllm fused_topk,
  * renormalize=True; vllm/model_executor/layers/fused_moe/router/fused_topk_router.py:69-113).
- * logits may be NULL when the caller does not want them. */
+ * logits (bf16 [T, E], 16-byte aligned) receives the router's output and is read back by the ranking. */
 int pm_moe_router_topk(const void *x, const void *router_w, int T, int H, int E, int k, void *logits,
                        float *topk_w, int32_t *topk_ids, pm_stream_t stream);
 

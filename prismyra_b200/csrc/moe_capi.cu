@@ -186,8 +186,8 @@ int pm_moe_router_topk(const void* x, const void* router_w, int T, int H, int E,
     if (T < 0 || H <= 0 || E <= 0 || k <= 0) return PM_ERR_INVALID;
     if (H % 128 != 0 || E > kMaxExperts || k > kMaxTopK || k > E) return PM_ERR_SHAPE;
     if (T == 0) return PM_OK;
-    if (!x || !router_w || !topk_w || !topk_ids) return PM_ERR_INVALID;
-    if (!a16(x) || !a16(router_w)) return PM_ERR_ALIGN;
+    if (!x || !router_w || !topk_w || !topk_ids || !logits) return PM_ERR_INVALID;
+    if (!a16(x) || !a16(router_w) || !a16(logits)) return PM_ERR_ALIGN;
     DeviceInfo d;
     const int st = current_device_info(&d);
     if (st != PM_OK) return st;

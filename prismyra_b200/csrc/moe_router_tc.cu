@@ -5,13 +5,11 @@
 // (router/fused_topk_router.py:69-113): p = softmax(logits) in fp32, the k largest (equal values: lower expert
 // index first), weights = p / sum of the selected p.
 //
-// One CTA = 128 tokens x all experts: tcgen05 kind::f16 MMAs (M=128, N=E rounded up to 16, K=16 per instruction)
-// accumulate the whole H reduction in TMEM, fed by a 4-stage TMA pipeline of 64-column slices.  Every token's
-// logits are reduced in the same fixed order whatever the token count, so a row's result never depends on which
-// rows share the call.  The epilogue (4 warps, one token per thread) stages the bf16 logits in shared memory and
-// ranks each token sequentially.
-#include <math.h>
-
+// One CTA = 128 tokens x 32 experts: tcgen05 kind::f16 MMAs (M=128, N=32, K=16 per instruction) accumulate the
+// whole H reduction in TMEM, fed by a 4-stage TMA pipeline of 64-column slices; the grid covers the experts in
+// 32-wide slices, so even a 128-token call spreads over E/32 SMs.  Every token's logits are reduced in the same
+// fixed order whatever the token count, so a row's result never depends on which rows share the call.  The
+// epilogue writes bf16 logits; the ranking (softmax / top-k / renormalise) is the warp-per-token top-k kernel.
 #include "moe_internal.h"
 #include "ptx.cuh"
 
@@ -19,9 +17,12 @@ namespace pm {
 namespace {
 
 constexpr int kTM = 128;       // tokens per CTA
+constexpr int kTN = 32;        // experts per CTA
 constexpr int kTK = 64;        // bf16 columns of H per stage (128-byte rows)
 constexpr int kTStages = 4;
 constexpr int kTXBytes = kTM * kTK * 2;  // 16 KB
+constexpr int kTWBytes = kTN * kTK * 2;  // 4 KB
+constexpr int kTStageBytes = kTXBytes + kTWBytes;
 
 struct RouterTail {
     uint64_t full[kTStages];
@@ -31,23 +32,19 @@ struct RouterTail {
     int abort;
 };
 
-__host__ __device__ constexpr size_t router_smem(int N) {
-    return 1024 + (size_t)kTStages * (kTXBytes + (size_t)N * 128) + sizeof(RouterTail);
-}
+constexpr size_t kRouterSmem = 1024 + (size_t)kTStages * kTStageBytes + sizeof(RouterTail);
 
 __global__ void __launch_bounds__(128, 1)
     router_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w, int T, int H,
-                     int E, int N, uint32_t tmem_cols, int k, __nv_bfloat16* __restrict__ logits,
-                     float* __restrict__ topk_w, int32_t* __restrict__ topk_ids, int* err) {
+                     int E, __nv_bfloat16* __restrict__ logits, int* err) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(smem);
-    const int stage_bytes = kTXBytes + N * 128;
-    RouterTail* tail = reinterpret_cast<RouterTail*>(smem + (size_t)kTStages * stage_bytes);
+    RouterTail* tail = reinterpret_cast<RouterTail*>(smem + (size_t)kTStages * kTStageBytes);
     volatile int* abort = &tail->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t0 = blockIdx.x * kTM;
+    const int t0 = blockIdx.x * kTM, e0 = blockIdx.y * kTN;
     const int KB = H / kTK;
 
     if (threadIdx.x == 0) {
@@ -63,7 +60,7 @@ __global__ void __launch_bounds__(128, 1)
         prefetch_tensormap(&tm_w);
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(&tail->tmem_base), tmem_cols);
+        tmem_alloc(smem_u32(&tail->tmem_base), 32);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -76,21 +73,21 @@ __global__ void __launch_bounds__(128, 1)
         uint32_t phase = 0;
         for (int kb = 0; kb < KB; ++kb) {
             if (!mbar_wait(smem_u32(&tail->empty[stage]), phase ^ 1u, abort)) break;
-            const uint32_t xd = sbase + stage * stage_bytes;
+            const uint32_t xd = sbase + stage * kTStageBytes;
             const uint32_t fb = smem_u32(&tail->full[stage]);
-            mbar_arrive_expect_tx(fb, stage_bytes);
+            mbar_arrive_expect_tx(fb, kTStageBytes);
             tma_load_2d(xd, &tm_x, fb, kb * kTK, t0);
-            tma_load_2d(xd + kTXBytes, &tm_w, fb, kb * kTK, 0);
+            tma_load_2d(xd + kTXBytes, &tm_w, fb, kb * kTK, e0);
             if (++stage == kTStages) { stage = 0; phase ^= 1u; }
         }
     } else if (warp == 1 && lane == 0) {
-        const uint32_t idesc = idesc_f32acc(1 /*bf16*/, 1 /*bf16*/, kTM, (uint32_t)N);
+        constexpr uint32_t idesc = idesc_f32acc(1 /*bf16*/, 1 /*bf16*/, kTM, kTN);
         int stage = 0;
         uint32_t phase = 0;
         for (int kb = 0; kb < KB; ++kb) {
             if (!mbar_wait(smem_u32(&tail->full[stage]), phase, abort)) break;
             tc_fence_after();
-            const uint32_t xa = sbase + stage * stage_bytes;
+            const uint32_t xa = sbase + stage * kTStageBytes;
             const uint64_t da = desc_kmajor_sw128(xa), db = desc_kmajor_sw128(xa + kTXBytes);
 #pragma unroll
             for (int j = 0; j < kTK / 16; ++j)  // 16 bf16 (32 bytes) of K per instruction
@@ -102,60 +99,31 @@ __global__ void __launch_bounds__(128, 1)
     }
     __syncwarp();
 
-    // Epilogue: every thread owns token t0 + threadIdx.x (TMEM lane threadIdx.x).
+    // Epilogue: thread i owns token t0 + i (TMEM lane i) and writes its 32 bf16 logits.
     const bool ok = mbar_wait(smem_u32(&tail->done), 0, abort);
     tc_fence_after();
-    float* lg = reinterpret_cast<float*>(smem);  // [128][E + 1] floats, reusing the drained pipeline buffers
-    const int LS = E + 1;
-    const int row = threadIdx.x;
-    const int t = t0 + row;
+    const int t = t0 + threadIdx.x;
     if (ok) {
-        for (int c0 = 0; c0 < N; c0 += 32) {
-            uint32_t r[32];
-            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c0, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const int e = c0 + i;
-                if (e < E) {
-                    const __nv_bfloat16 b = __float2bfloat16_rn(__uint_as_float(r[i]));
-                    lg[row * LS + e] = __bfloat162float(b);
-                    if (logits != nullptr && t < T) logits[(size_t)t * E + e] = b;
-                }
-            }
-        }
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16), r);
+        tmem_ld_wait();
         if (t < T) {
-            float* v = lg + row * LS;
-            float mx = -INFINITY;
-            for (int e = 0; e < E; ++e) mx = fmaxf(mx, v[e]);
-            float sum = 0.0f;
-            for (int e = 0; e < E; ++e) sum += expf(v[e] - mx);
-            float sel = 0.0f;
-            float pj[kMaxTopK];
-            int ij[kMaxTopK];
-            for (int j = 0; j < k; ++j) {
-                // the largest untaken logit; a strict '>' keeps the lower index among equal values.  Taken
-                // entries are marked NaN, which no comparison selects.
-                int best = -1;
-                float bv = 0.0f;
-                for (int e = 0; e < E; ++e) {
-                    const float x = v[e];
-                    if (isnan(x)) continue;
-                    if (best < 0 || x > bv) {
-                        bv = x;
-                        best = e;
-                    }
+            if (e0 + kTN <= E) {
+                uint4* dst = reinterpret_cast<uint4*>(logits + (size_t)t * E + e0);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    uint4 o;
+                    __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        ob[i] = __floats2bfloat162_rn(__uint_as_float(r[8 * u + 2 * i]),
+                                                      __uint_as_float(r[8 * u + 2 * i + 1]));
+                    dst[u] = o;
                 }
-                if (best < 0) best = 0;  // fewer than k finite logits (non-finite input): keep the output defined
-                const float p = expf(bv - mx) / sum;
-                pj[j] = p;
-                ij[j] = best;
-                sel += p;
-                v[best] = __int_as_float(0x7fc00000);
-            }
-            for (int j = 0; j < k; ++j) {
-                topk_w[(size_t)t * k + j] = pj[j] / sel;
-                topk_ids[(size_t)t * k + j] = ij[j];
+            } else {
+#pragma unroll
+                for (int i = 0; i < kTN; ++i)
+                    if (e0 + i < E) logits[(size_t)t * E + e0 + i] = __float2bfloat16_rn(__uint_as_float(r[i]));
             }
         }
     }
@@ -163,7 +131,7 @@ __global__ void __launch_bounds__(128, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, tmem_cols);
+        tmem_dealloc(tmem, 32);
     }
     if (threadIdx.x == 0 && tail->abort && err != nullptr) atomicExch(err, 1);
 }
@@ -173,28 +141,27 @@ __global__ void __launch_bounds__(128, 1)
 cudaError_t launch_router_topk(const void* x, const void* w, int T, int H, int E, int k, void* logits, float* topk_w,
                                int32_t* topk_ids, int32_t* err, cudaStream_t s) {
     if (T == 0) return cudaSuccess;
-    const int N = (E + 15) / 16 * 16;
-    uint32_t cols = 32;
-    while (cols < (uint32_t)N) cols <<= 1;
+    if (logits == nullptr) return cudaErrorInvalidValue;  // the ranking reads the logits back
     CUtensorMap tx, tw;
     if (!encode_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H, (uint64_t)T, (uint64_t)H * 2,
                         kTK, kTM) ||
         !encode_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H, (uint64_t)E, (uint64_t)H * 2, kTK,
-                        (uint32_t)N))
+                        kTN))
         return cudaErrorInvalidValue;
-    const size_t smem = router_smem(N);
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !configured[dev]) {
         cudaError_t e = cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)router_smem(kMaxExperts));
+                                             (int)kRouterSmem);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
-    router_tc_kernel<<<cdiv(T, kTM), 128, smem, s>>>(tx, tw, T, H, E, N, cols, k,
-                                                    static_cast<__nv_bfloat16*>(logits), topk_w, topk_ids, err);
-    return cudaGetLastError();
+    const dim3 grid(cdiv(T, kTM), cdiv(E, kTN));
+    router_tc_kernel<<<grid, 128, kRouterSmem, s>>>(tx, tw, T, H, E, static_cast<__nv_bfloat16*>(logits), err);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    return launch_topk(logits, T, E, k, topk_w, topk_ids, s);
 }
 
 }  // namespace pm
