@@ -7,7 +7,8 @@ One step = one call of the routed FP8 layer (router projection, softmax/top-k, e
 quantisation, gate_up GEMM + silu*mul + requantisation, down GEMM + routing weight, top-k sum) on T=5120 tokens
 of H=2048 with E=128 experts, top-8, I=768, synthetic seeded data, expert weights 128x128
 block-FP8.  The weights (604 MB) exceed the 126 MB L2, so every step streams them from HBM; no L2 flush is added.
-Under torchrun each rank runs its own replica (weak scaling) and the step time is the max over ranks.
+Under torchrun (N GPUs) the step is the expert-parallel layer: every rank owns E/N experts and its own 5120
+tokens (weak scaling), NCCL all-to-all dispatch and combine; the step time is the max over ranks.
 
 ``--impl reference`` times the reference's own CPU implementation of the same layer (transformers' fallback
 block, float32, all host threads) on a bounded sample of the workload and prints the same JSON line with
@@ -217,6 +218,50 @@ def stage_times(layer: dict, T: int, reps: int = 20) -> dict:
     return out
 
 
+def ep_stack(dev, rank: int, world: int, layers: int, tokens: int, steps: int):
+    """a stack of `layers` expert-parallel FP8 MoE layers (per-layer weights from seed =
+    layer index, experts sharded over the ranks), `tokens` tokens per rank, router logits skewed by a Zipf(1.1)
+    expert bias.  Returns ms per stack pass (max over ranks) and the peak expert load share."""
+    import torch
+
+    from prismyra_b200 import ep, synth
+
+    epr = E // world
+    lo, hi = rank * epr, (rank + 1) * epr
+    bias = synth.zipf_bias(E).to(dev)
+    stack = []
+    for li in range(layers):
+        L = synth.make_fp8_layer(8, H, I, E, seed=li, device=dev, gen_device="cuda")
+        b = ep.CudaBackend(L["w1"][lo:hi].contiguous(), L["w1_s"][lo:hi].contiguous(), L["w2"][lo:hi].contiguous(),
+                           L["w2_s"][lo:hi].contiguous(), L["router_w"], K, bias=bias)
+        stack.append(ep.ExpertParallelLayer(b, E, K, rank, world))
+        del L
+    g = torch.Generator("cuda").manual_seed(1000 + rank)
+    x = torch.randn(tokens, H, generator=g, device=dev).to(torch.bfloat16)
+
+    def run():
+        h = x
+        for layer in stack:
+            h = layer.forward(h)
+        return h
+
+    for _ in range(2):
+        run()
+    if world > 1:
+        torch.distributed.barrier()
+    ms = time_region(run, steps, torch.cuda.current_stream())
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    from prismyra_b200 import ops
+
+    _, _, ids = ops.router_topk(x, stack[0].b.router_w, K, bias=bias)
+    load = torch.bincount(ids.reshape(-1).long(), minlength=E).float()
+    del stack
+    return ms, float(load.max() / load.sum())
+
+
 def run_b200(args, rank: int, world: int, local: int) -> None:
     import torch
 
@@ -229,9 +274,25 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
     layer = synth.make_fp8_layer(T_CTX, H, I, E, seed=0, device=dev, gen_device="cuda")
     x = layer["x"]
     stream = torch.cuda.current_stream()
+    if world > 1:
+        # every rank owns E/world experts and its own T_CTX tokens (weak scaling); NCCL all-to-all dispatch/combine
+        from prismyra_b200 import ep
 
-    def step():
-        return ops.forward_fp8(x, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K, router_w=layer["router_w"])
+        gx = torch.Generator("cuda").manual_seed(1000 + rank)
+        x = torch.randn(T_CTX, H, generator=gx, device=dev).to(torch.bfloat16)
+        epr = E // world
+        lo, hi = rank * epr, (rank + 1) * epr
+        ep_layer = ep.ExpertParallelLayer(
+            ep.CudaBackend(layer["w1"][lo:hi].contiguous(), layer["w1_s"][lo:hi].contiguous(),
+                           layer["w2"][lo:hi].contiguous(), layer["w2_s"][lo:hi].contiguous(), layer["router_w"], K),
+            E, K, rank, world)
+
+        def step():
+            return ep_layer.forward(x)
+    else:
+        def step():
+            return ops.forward_fp8(x, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K,
+                                   router_w=layer["router_w"])
 
     clk = Clocks(local).start()
     for _ in range(max(3, args.warmup)):
@@ -265,8 +326,11 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
 
     def e2e_step():
         x_dev.copy_(x_host, non_blocking=True)
-        o = ops.forward_fp8(x_dev, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K,
-                            router_w=layer["router_w"])
+        if world > 1:
+            o = ep_layer.forward(x_dev)
+        else:
+            o = ops.forward_fp8(x_dev, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K,
+                                router_w=layer["router_w"])
         out_host.copy_(o, non_blocking=True)
 
     for _ in range(3):
@@ -320,6 +384,8 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
     nv_tflops = fl["total"] / (nv_ms * 1e-3) / 1e12
     fp4_peak = 4.0 * pk["bf16_tflops"]  # B200 FP4 dense rate is four times its BF16 dense rate
 
+    stack_ms, stack_peak = ep_stack(dev, rank, world, args.stack_layers, 4096, max(2, args.steps // 20))
+
     if rank != 0:
         return
     cb = None
@@ -332,7 +398,7 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
         "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
         "config": {"workload": f"FP8 block-scaled routed-expert layer, T={T_CTX} tokens per GPU (BASELINE configs[1])",
                    "tokens": T_CTX, "hidden": H, "intermediate": I, "experts": E, "top_k": K,
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "parallelism": f"expert parallel x{world} (NCCL all-to-all)" if world > 1 else "single GPU",
                    "l2": "no flush: 604 MB of expert weights (> 126 MB L2) stream from HBM every step"},
         "tflops": layer_tflops,
         "frac_fp8_peak": layer_tflops / fp8_peak,
@@ -350,6 +416,10 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
         "nvfp4_t5120": {"ms": nv_ms, "tokens_per_s": T_CTX / (nv_ms * 1e-3), "tflops": nv_tflops,
                         "frac_fp4_peak": nv_tflops / fp4_peak, "fp4_peak": fp4_peak,
                         "weights": "NVFP4 from the FP8 layer (reference prepare_layer recipe), synthetic calibration"},
+        "ep_stack": {"layers": args.stack_layers, "tokens_per_gpu": 4096, "ms": stack_ms,
+                     "tokens_per_s": world * 4096 / (stack_ms * 1e-3), "zipf_peak_expert_share": stack_peak,
+                     "config": "BASELINE configs[4]: FP8 layers, per-layer weights from seed = layer, Zipf(1.1) "
+                               "expert bias, experts sharded over the ranks"},
         "gpu_launches": KERNELS_PER_STEP * args.steps,
         "clocks": clk.summary(),
     }
@@ -365,6 +435,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--stack-layers", type=int, default=36)
     args = ap.parse_args()
     if args.impl == "reference":
         # the CPU reference runs on rank 0 only; other ranks exit without work or a process group

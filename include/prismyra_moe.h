@@ -82,12 +82,16 @@ int pm_moe_workspace_region(int T, int H, int I, int E, int k, int fmt, int regi
 /* Router projection + softmax + top-k + renormalise, row-count invariant.  Replaces
  * prismyra/kernels/qwen3_moe.py:169-171 (FusedExperts._route) followed by :196 (vllm fused_topk,
  * renormalize=True; vllm/model_executor/layers/fused_moe/router/fused_topk_router.py:69-113).
- * logits (bf16 [T, E], 16-byte aligned) receives the router's output and is read back by the ranking. */
-int pm_moe_router_topk(const void *x, const void *router_w, int T, int H, int E, int k, void *logits,
-                       float *topk_w, int32_t *topk_ids, pm_stream_t stream);
+ * logits (bf16 [T, E], 16-byte aligned) receives the router's output and is read back by the ranking.  bias
+ * (fp32 [E], may be NULL) is added to every logit before the ranking; it has no counterpart in the reference and
+ * exists to skew the expert load in benchmarks (a Zipf-shaped bias). */
+int pm_moe_router_topk(const void *x, const void *router_w, const float *bias, int T, int H, int E, int k,
+                       void *logits, float *topk_w, int32_t *topk_ids, pm_stream_t stream);
 
-/* Softmax + top-k + renormalise from given bf16 logits: prismyra/kernels/qwen3_moe.py:196 (fused_topk). */
-int pm_moe_topk(const void *logits, int T, int E, int k, float *topk_w, int32_t *topk_ids, pm_stream_t stream);
+/* Softmax + top-k + renormalise from given bf16 logits: prismyra/kernels/qwen3_moe.py:196 (fused_topk); bias as
+ * for pm_moe_router_topk. */
+int pm_moe_topk(const void *logits, const float *bias, int T, int E, int k, float *topk_w, int32_t *topk_ids,
+                pm_stream_t stream);
 
 /* Expert alignment: vllm/model_executor/layers/fused_moe/moe_align_block_size.py:11-99 with block 128, the
  * reference's call at vllm/model_executor/layers/fused_moe/fused_moe.py:1536-1585.  Flat indices grouped by
@@ -121,9 +125,15 @@ int pm_moe_gemm2_fp8(const uint8_t *a_q, const float *a_s, const uint8_t *w2, co
                      const float *topk_w, int max_slots, int T, int k, int H, int I, int E, void *c3, int32_t *err,
                      pm_stream_t stream);
 
-/* out[t] = bf16(sum_j c3[t*k + j]) accumulated in fp32: vllm/model_executor/layers/fused_moe/fused_moe.py:1864
- * (ops.moe_sum). */
-int pm_moe_combine(const void *c3, int T, int k, int H, void *out, pm_stream_t stream);
+/* out[t] = bf16(sum_j c3[row(t*k + j)]) accumulated in fp32, j ascending: vllm/model_executor/layers/fused_moe/
+ * fused_moe.py:1864 (ops.moe_sum).  row_of (i32 [T*k], may be NULL = identity) lets rows come back from
+ * expert-parallel ranks in their send order. */
+int pm_moe_combine(const void *c3, const int32_t *row_of, int T, int k, int H, void *out, pm_stream_t stream);
+
+/* Row scatter for expert parallelism (no counterpart in the reference, which runs on one device):
+ * dst + dst_index[i]*dst_stride <- src + i*src_stride, row_bytes bytes per row (multiples of 16). */
+int pm_moe_scatter_rows(const void *src, int rows, int row_bytes, int src_stride, const int32_t *dst_index,
+                        void *dst, int dst_stride, pm_stream_t stream);
 
 /* The whole routed FP8 layer: prismyra/kernels/qwen3_moe.py:184-199 (FusedExperts.forward) minus the shared
  * expert, i.e. logits -> fused_topk -> fused_experts (vllm/model_executor/layers/fused_moe/fused_moe.py:

@@ -101,6 +101,15 @@ def route_topk(logits_bits, k: int):
     return w, ids
 
 
+def route_topk_f32(scores, k: int):
+    sc = _c(scores, np.float32)
+    T, E = sc.shape
+    w = np.empty((T, k), np.float32)
+    ids = np.empty((T, k), np.int32)
+    lib().or_route_topk_f32(_p(sc), T, E, k, _p(w), _p(ids))
+    return w, ids
+
+
 def align(ids, num_experts: int, block_m: int):
     flat = _c(ids, np.int32).reshape(-1)
     n = flat.size

@@ -36,13 +36,14 @@ SIGNATURES: dict[str, tuple] = {
     "pm_moe_max_slots": (_I, [_I, _I, _I]),
     "pm_moe_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I]),
     "pm_moe_workspace_region": (_I, [_I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_Z), ctypes.POINTER(_Z)]),
-    "pm_moe_router_topk": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
-    "pm_moe_topk": (_I, [_P, _I, _I, _I, _P, _P, _P]),
+    "pm_moe_router_topk": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "pm_moe_topk": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
     "pm_moe_align": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _Z, _P]),
     "pm_moe_quant_fp8": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
     "pm_moe_gemm1_fp8": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "pm_moe_gemm2_fp8": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
-    "pm_moe_combine": (_I, [_P, _I, _I, _I, _P, _P]),
+    "pm_moe_combine": (_I, [_P, _P, _I, _I, _I, _P, _P]),
+    "pm_moe_scatter_rows": (_I, [_P, _I, _I, _I, _P, _P, _I, _P]),
     "pm_moe_forward_fp8": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _Z, _P]),
     "pm_moe_read_status": (_I, [_P, _P]),
     "pm_moe_align_noalloc": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P]),

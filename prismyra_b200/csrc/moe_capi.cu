@@ -181,8 +181,8 @@ int pm_moe_workspace_region(int T, int H, int I, int E, int k, int fmt, int regi
     return PM_OK;
 }
 
-int pm_moe_router_topk(const void* x, const void* router_w, int T, int H, int E, int k, void* logits,
-                       float* topk_w, int32_t* topk_ids, pm_stream_t stream) {
+int pm_moe_router_topk(const void* x, const void* router_w, const float* bias, int T, int H, int E, int k,
+                       void* logits, float* topk_w, int32_t* topk_ids, pm_stream_t stream) {
     if (T < 0 || H <= 0 || E <= 0 || k <= 0) return PM_ERR_INVALID;
     if (H % 128 != 0 || E > kMaxExperts || k > kMaxTopK || k > E) return PM_ERR_SHAPE;
     if (T == 0) return PM_OK;
@@ -192,10 +192,11 @@ int pm_moe_router_topk(const void* x, const void* router_w, int T, int H, int E,
     const int st = current_device_info(&d);
     if (st != PM_OK) return st;
     return cuda_status(
-        launch_router_topk(x, router_w, T, H, E, k, logits, topk_w, topk_ids, nullptr, (cudaStream_t)stream));
+        launch_router_topk(x, router_w, bias, T, H, E, k, logits, topk_w, topk_ids, nullptr, (cudaStream_t)stream));
 }
 
-int pm_moe_topk(const void* logits, int T, int E, int k, float* topk_w, int32_t* topk_ids, pm_stream_t stream) {
+int pm_moe_topk(const void* logits, const float* bias, int T, int E, int k, float* topk_w, int32_t* topk_ids,
+                pm_stream_t stream) {
     if (T < 0 || E <= 0 || k <= 0) return PM_ERR_INVALID;
     if (E > kMaxExperts || k > kMaxTopK || k > E) return PM_ERR_SHAPE;
     if (T == 0) return PM_OK;
@@ -203,7 +204,7 @@ int pm_moe_topk(const void* logits, int T, int E, int k, float* topk_w, int32_t*
     DeviceInfo d;
     const int st = current_device_info(&d);
     if (st != PM_OK) return st;
-    return cuda_status(launch_topk(logits, T, E, k, topk_w, topk_ids, (cudaStream_t)stream));
+    return cuda_status(launch_topk(logits, bias, T, E, k, topk_w, topk_ids, (cudaStream_t)stream));
 }
 
 int pm_moe_align(const int32_t* topk_ids, int T, int k, int E, int32_t* sorted_ids, int32_t* expert_ids,
@@ -282,7 +283,21 @@ int pm_moe_gemm2_fp8(const uint8_t* a_q, const float* a_s, const uint8_t* w2, co
     return cuda_status(launch_gemm_fp8(1, ta, tb, g, d.sms, (cudaStream_t)stream));
 }
 
-int pm_moe_combine(const void* c3, int T, int k, int H, void* out, pm_stream_t stream) {
+int pm_moe_scatter_rows(const void* src, int rows, int row_bytes, int src_stride, const int32_t* dst_index,
+                        void* dst, int dst_stride, pm_stream_t stream) {
+    if (rows < 0 || row_bytes <= 0 || src_stride < row_bytes || dst_stride < row_bytes) return PM_ERR_INVALID;
+    if (row_bytes % 16 || src_stride % 16 || dst_stride % 16) return PM_ERR_ALIGN;
+    if (rows == 0) return PM_OK;
+    if (!src || !dst_index || !dst) return PM_ERR_INVALID;
+    if (!a16(src) || !a16(dst)) return PM_ERR_ALIGN;
+    DeviceInfo d;
+    const int st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    return cuda_status(
+        launch_scatter_rows(src, rows, row_bytes, src_stride, dst_index, dst, dst_stride, (cudaStream_t)stream));
+}
+
+int pm_moe_combine(const void* c3, const int32_t* row_of, int T, int k, int H, void* out, pm_stream_t stream) {
     if (T < 0 || k <= 0 || H <= 0) return PM_ERR_INVALID;
     if (H % 8 != 0) return PM_ERR_SHAPE;
     if (T == 0) return PM_OK;
@@ -291,7 +306,7 @@ int pm_moe_combine(const void* c3, int T, int k, int H, void* out, pm_stream_t s
     DeviceInfo d;
     const int st = current_device_info(&d);
     if (st != PM_OK) return st;
-    return cuda_status(launch_combine(c3, T, k, H, out, (cudaStream_t)stream));
+    return cuda_status(launch_combine(c3, row_of, T, k, H, out, (cudaStream_t)stream));
 }
 
 int pm_moe_forward_fp8(const void* x, const void* router_w, const void* logits, const uint8_t* w1,
@@ -326,9 +341,9 @@ int pm_moe_forward_fp8(const void* x, const void* router_w, const void* logits, 
     if (cudaMemsetAsync(status, 0, L.len[PM_WS_STATUS], s) != cudaSuccess) return PM_ERR_CUDA;
     cudaError_t e;
     if (logits != nullptr)
-        e = launch_topk(logits, T, E, k, topk_w, topk_ids, s);
+        e = launch_topk(logits, nullptr, T, E, k, topk_w, topk_ids, s);
     else
-        e = launch_router_topk(x, router_w, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s);
+        e = launch_router_topk(x, router_w, nullptr, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s);
     if (e != cudaSuccess) return PM_ERR_CUDA;
     int32_t* slot_of = reinterpret_cast<int32_t*>(R(PM_WS_SLOT_OF));
     e = launch_align(topk_ids, T * k, E, reinterpret_cast<int32_t*>(R(PM_WS_COUNTS)), sorted, expert_ids, npp,
@@ -341,7 +356,7 @@ int pm_moe_forward_fp8(const void* x, const void* router_w, const void* logits, 
     st = pm_moe_gemm2_fp8(a2, a2s, w2, w2_s, expert_ids, npp, sorted, topk_w, L.max_slots, T, k, H, I, E, c3,
                           status, stream);
     if (st != PM_OK) return st;
-    return cuda_status(launch_combine(c3, T, k, H, out, s));
+    return cuda_status(launch_combine(c3, nullptr, T, k, H, out, s));
 }
 
 int pm_moe_quant_nvfp4(const void* x, int T, int H, int k, const int32_t* slot_of, float gs, uint8_t* a_q,
@@ -466,9 +481,10 @@ int pm_moe_forward_nvfp4(const void* x, const void* router_w, const void* logits
     int32_t* npp = reinterpret_cast<int32_t*>(R(PM_WS_NUM_POST_PAD));
     int32_t* slot_of = reinterpret_cast<int32_t*>(R(PM_WS_SLOT_OF));
     if (cudaMemsetAsync(status, 0, L.len[PM_WS_STATUS], s) != cudaSuccess) return PM_ERR_CUDA;
-    cudaError_t e = logits != nullptr
-                        ? launch_topk(logits, T, E, k, topk_w, topk_ids, s)
-                        : launch_router_topk(x, router_w, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s);
+    cudaError_t e =
+        logits != nullptr
+            ? launch_topk(logits, nullptr, T, E, k, topk_w, topk_ids, s)
+            : launch_router_topk(x, router_w, nullptr, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s);
     if (e != cudaSuccess) return PM_ERR_CUDA;
     e = launch_align(topk_ids, T * k, E, reinterpret_cast<int32_t*>(R(PM_WS_COUNTS)), sorted, expert_ids, npp,
                      reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_OFF)), slot_of, s);
@@ -481,7 +497,7 @@ int pm_moe_forward_nvfp4(const void* x, const void* router_w, const void* logits
     st = pm_moe_gemm2_nvfp4(R(PM_WS_A2), R(PM_WS_A2_SCALE), w2, w2_sf, alpha2, expert_ids, npp, sorted, topk_w,
                             L.max_slots, T, k, H, I, E, R(PM_WS_C3), status, stream);
     if (st != PM_OK) return st;
-    return cuda_status(launch_combine(R(PM_WS_C3), T, k, H, out, s));
+    return cuda_status(launch_combine(R(PM_WS_C3), nullptr, T, k, H, out, s));
 }
 
 int pm_moe_read_status(const void* workspace, pm_stream_t stream) {

@@ -17,10 +17,12 @@ constexpr int kAlignChunk = 4096;  // flat (token, slot) indices handled by one 
 inline int cdiv(long a, long b) { return static_cast<int>((a + b - 1) / b); }
 
 // Router projection (bf16, fp32 accumulation in a fixed order per row) fused with softmax / top-k.
-cudaError_t launch_router_topk(const void* x, const void* w, int T, int H, int E, int k, void* logits, float* topk_w,
-                               int32_t* topk_ids, int32_t* err, cudaStream_t s);
-// Softmax / top-k / renormalise from given bf16 logits.
-cudaError_t launch_topk(const void* logits, int T, int E, int k, float* topk_w, int32_t* topk_ids, cudaStream_t s);
+// bias (may be null): fp32 [E] added to each logit before the ranking.
+cudaError_t launch_router_topk(const void* x, const void* w, const float* bias, int T, int H, int E, int k,
+                               void* logits, float* topk_w, int32_t* topk_ids, int32_t* err, cudaStream_t s);
+// Softmax / top-k / renormalise from given bf16 logits (+ optional fp32 bias per expert).
+cudaError_t launch_topk(const void* logits, const float* bias, int T, int E, int k, float* topk_w, int32_t* topk_ids,
+                        cudaStream_t s);
 // Stable counting sort of the flat (token, slot) indices by expert, padded per expert to kBlockM.
 // slot_of (may be null) receives the inverse permutation: slot_of[flat index] = its slot.
 cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int32_t* sorted, int32_t* expert_ids,
@@ -29,8 +31,11 @@ cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int3
 // is written to the k slots of its token (a_q [slots, H], a_s [slots, H/128]) instead of to row t.
 cudaError_t launch_quant_fp8(const void* x, int T, int H, int k, const int32_t* slot_of, uint8_t* x_q, float* x_s,
                              cudaStream_t s);
-// out[t] = bf16(sum_j c3[t*k + j]) in fp32, j ascending.
-cudaError_t launch_combine(const void* c3, int T, int k, int H, void* out, cudaStream_t s);
+// out[t] = bf16(sum_j c3[row(t*k + j)]) in fp32, j ascending; row = identity or row_of.
+cudaError_t launch_combine(const void* c3, const int32_t* row_of, int T, int k, int H, void* out, cudaStream_t s);
+// dst[dst_index[i]] = src[i] for rows of row_bytes (multiple of 16) with the given byte strides.
+cudaError_t launch_scatter_rows(const void* src, int rows, int row_bytes, int src_stride, const int32_t* dst_index,
+                                void* dst, int dst_stride, cudaStream_t s);
 
 struct GemmArgs {
     const float* a_scale;     // [rows, K/128]

@@ -62,8 +62,10 @@ __global__ void __launch_bounds__(256) quant_fp8_kernel(const __nv_bfloat16* __r
     }
 }
 
-// out[t, c..c+7] = bf16(sum_j c3[t*k + j, c..c+7]) with an fp32 running sum, j ascending.
-__global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ c3, int T, int k, int H,
+// out[t, c..c+7] = bf16(sum_j c3[row(t*k + j), c..c+7]) with an fp32 running sum, j ascending; row() is the
+// identity or the row_of map (rows returned by expert-parallel ranks arrive in their send order).
+__global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ c3,
+                                                      const int32_t* __restrict__ row_of, int T, int k, int H,
                                                       __nv_bfloat16* __restrict__ out) {
     const long total = (long)T * (H / 8);
     for (long q = (long)blockIdx.x * blockDim.x + threadIdx.x; q < total; q += (long)gridDim.x * blockDim.x) {
@@ -73,7 +75,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
 #pragma unroll
         for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
         for (int j = 0; j < k; ++j) {
-            const uint4 u = *reinterpret_cast<const uint4*>(c3 + ((size_t)t * k + j) * H + c);
+            const size_t rrow = row_of != nullptr ? (size_t)row_of[(size_t)t * k + j] : (size_t)t * k + j;
+            const uint4 u = *reinterpret_cast<const uint4*>(c3 + rrow * H + c);
             const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
             for (int i = 0; i < 8; ++i) acc[i] += __bfloat162float(b[i]);
@@ -99,7 +102,35 @@ cudaError_t launch_quant_fp8(const void* x, int T, int H, int k, const int32_t* 
     return cudaGetLastError();
 }
 
-cudaError_t launch_combine(const void* c3, int T, int k, int H, void* out, cudaStream_t s) {
+// dst row dst_index[i] (dst_stride bytes apart) = src row i (src_stride bytes apart), row_bytes bytes each.
+__global__ void __launch_bounds__(256) scatter_rows_kernel(const uint8_t* __restrict__ src, int rows, int row_bytes,
+                                                           int src_stride, const int32_t* __restrict__ dst_index,
+                                                           uint8_t* __restrict__ dst, int dst_stride) {
+    const int per_row = row_bytes / 16;
+    const long total = (long)rows * per_row;
+    for (long q = (long)blockIdx.x * blockDim.x + threadIdx.x; q < total; q += (long)gridDim.x * blockDim.x) {
+        const long r = q / per_row;
+        const int c = (int)(q % per_row) * 16;
+        const uint4 v = *reinterpret_cast<const uint4*>(src + r * src_stride + c);
+        *reinterpret_cast<uint4*>(dst + (size_t)dst_index[r] * dst_stride + c) = v;
+    }
+}
+
+cudaError_t launch_scatter_rows(const void* src, int rows, int row_bytes, int src_stride, const int32_t* dst_index,
+                                void* dst, int dst_stride, cudaStream_t s) {
+    if (rows == 0) return cudaSuccess;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long total = (long)rows * (row_bytes / 16);
+    const long want = (total + 255) / 256;
+    const int blocks = (int)(want < (long)sms * 16 ? want : (long)sms * 16);
+    scatter_rows_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint8_t*>(src), rows, row_bytes, src_stride,
+                                               dst_index, static_cast<uint8_t*>(dst), dst_stride);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const void* c3, const int32_t* row_of, int T, int k, int H, void* out, cudaStream_t s) {
     if (T == 0) return cudaSuccess;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
@@ -107,7 +138,7 @@ cudaError_t launch_combine(const void* c3, int T, int k, int H, void* out, cudaS
     const long total = (long)T * (H / 8);
     const long want = (total + 255) / 256;
     const int blocks = (int)(want < (long)sms * 16 ? want : (long)sms * 16);
-    combine_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(c3), T, k, H,
+    combine_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(c3), row_of, T, k, H,
                                           static_cast<__nv_bfloat16*>(out));
     return cudaGetLastError();
 }

@@ -81,7 +81,8 @@ __device__ __forceinline__ void warp_topk(const float (&v)[kMaxEPT], int E, int 
     }
 }
 
-__global__ void __launch_bounds__(256) topk_kernel(const __nv_bfloat16* __restrict__ logits, int T, int E, int k,
+__global__ void __launch_bounds__(256) topk_kernel(const __nv_bfloat16* __restrict__ logits,
+                                                   const float* __restrict__ bias, int T, int E, int k,
                                                    float* __restrict__ topk_w, int32_t* __restrict__ topk_ids) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -90,7 +91,8 @@ __global__ void __launch_bounds__(256) topk_kernel(const __nv_bfloat16* __restri
 #pragma unroll
     for (int i = 0; i < kMaxEPT; ++i) {
         const int e = lane + 32 * i;
-        v[i] = e < E ? __bfloat162float(logits[(size_t)warp * E + e]) : -INFINITY;
+        v[i] = e < E ? __bfloat162float(logits[(size_t)warp * E + e]) + (bias != nullptr ? bias[e] : 0.0f)
+                     : -INFINITY;
     }
     warp_topk(v, E, k, topk_w + (size_t)warp * k, topk_ids + (size_t)warp * k);
 }
@@ -189,10 +191,11 @@ __global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __res
 
 }  // namespace
 
-cudaError_t launch_topk(const void* logits, int T, int E, int k, float* topk_w, int32_t* topk_ids, cudaStream_t s) {
+cudaError_t launch_topk(const void* logits, const float* bias, int T, int E, int k, float* topk_w, int32_t* topk_ids,
+                        cudaStream_t s) {
     if (T == 0) return cudaSuccess;
     const int blocks = cdiv((long)T * 32, 256);
-    topk_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(logits), T, E, k, topk_w, topk_ids);
+    topk_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(logits), bias, T, E, k, topk_w, topk_ids);
     return cudaGetLastError();
 }
 

@@ -138,8 +138,8 @@ __global__ void __launch_bounds__(128, 1)
 
 }  // namespace
 
-cudaError_t launch_router_topk(const void* x, const void* w, int T, int H, int E, int k, void* logits, float* topk_w,
-                               int32_t* topk_ids, int32_t* err, cudaStream_t s) {
+cudaError_t launch_router_topk(const void* x, const void* w, const float* bias, int T, int H, int E, int k,
+                               void* logits, float* topk_w, int32_t* topk_ids, int32_t* err, cudaStream_t s) {
     if (T == 0) return cudaSuccess;
     if (logits == nullptr) return cudaErrorInvalidValue;  // the ranking reads the logits back
     CUtensorMap tx, tw;
@@ -161,7 +161,7 @@ cudaError_t launch_router_topk(const void* x, const void* w, int T, int H, int E
     router_tc_kernel<<<grid, 128, kRouterSmem, s>>>(tx, tw, T, H, E, static_cast<__nv_bfloat16*>(logits), err);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    return launch_topk(logits, T, E, k, topk_w, topk_ids, s);
+    return launch_topk(logits, bias, T, E, k, topk_w, topk_ids, s);
 }
 
 }  // namespace pm

@@ -131,7 +131,7 @@ def read_status(workspace: torch.Tensor) -> None:
 
 
 # ------------------------------------------------------------------------------------------- stages
-def router_topk(x: torch.Tensor, router_w: torch.Tensor, k: int, out=None):
+def router_topk(x: torch.Tensor, router_w: torch.Tensor, k: int, out=None, bias: torch.Tensor | None = None):
     T, H = x.shape
     E = router_w.shape[0]
     _cuda(x, "x", torch.bfloat16)
@@ -141,17 +141,21 @@ def router_topk(x: torch.Tensor, router_w: torch.Tensor, k: int, out=None):
                torch.empty(T, k, dtype=torch.float32, device=x.device),
                torch.empty(T, k, dtype=torch.int32, device=x.device))
     logits, w, ids = out
-    _lib.call("pm_moe_router_topk", _p(x), _p(router_w), T, H, E, k, _p(logits), _p(w), _p(ids),
+    if bias is not None:
+        _cuda(bias, "bias", torch.float32, (E,))
+    _lib.call("pm_moe_router_topk", _p(x), _p(router_w), _p(bias), T, H, E, k, _p(logits), _p(w), _p(ids),
               _stream(x.device))
     return logits, w, ids
 
 
-def topk(logits: torch.Tensor, k: int):
+def topk(logits: torch.Tensor, k: int, bias: torch.Tensor | None = None):
     T, E = logits.shape
     _cuda(logits, "logits", torch.bfloat16)
+    if bias is not None:
+        _cuda(bias, "bias", torch.float32, (E,))
     w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
     ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
-    _lib.call("pm_moe_topk", _p(logits), T, E, k, _p(w), _p(ids), _stream(logits.device))
+    _lib.call("pm_moe_topk", _p(logits), _p(bias), T, E, k, _p(w), _p(ids), _stream(logits.device))
     return w, ids
 
 
@@ -172,6 +176,18 @@ def align(ids: torch.Tensor, E: int, out=None):
     _lib.call("pm_moe_align", _p(ids), T, k, E, _p(sorted_ids), _p(expert_ids), _p(npp), _p(off), _p(slot_of),
               _p(scratch), scratch.numel() * 4, _stream(dev))
     return sorted_ids, expert_ids, npp, off, slot_of, scratch
+
+
+def scatter_rows(src: torch.Tensor, dst_index: torch.Tensor, dst: torch.Tensor) -> torch.Tensor:
+    """dst[dst_index[i]] = src[i] for 2-D tensors whose rows are multiples of 16 bytes (strided views allowed)."""
+    _cuda(dst_index, "dst_index", torch.int32)
+    rows = src.shape[0]
+    rb = src.shape[1] * src.element_size()
+    _need(dst.shape[1] * dst.element_size() == rb, "row sizes differ")
+    _need(src.stride(1) == 1 and dst.stride(1) == 1, "rows must be contiguous")
+    _lib.call("pm_moe_scatter_rows", _p(src), rows, rb, src.stride(0) * src.element_size(), _p(dst_index), _p(dst),
+              dst.stride(0) * dst.element_size(), _stream(src.device))
+    return dst
 
 
 def quant_fp8(x: torch.Tensor, slot_of: torch.Tensor | None = None, k: int = 1, max_slots: int = 0, out=None):
@@ -215,11 +231,11 @@ def gemm2_fp8(a_q, a_s, w2, w2_s, expert_ids, npp, sorted_ids, topk_w, T: int, k
     return c3, err
 
 
-def combine(c3: torch.Tensor, T: int, k: int, out=None):
+def combine(c3: torch.Tensor, T: int, k: int, out=None, row_of: torch.Tensor | None = None):
     H = c3.shape[1]
     if out is None:
         out = torch.empty(T, H, dtype=torch.bfloat16, device=c3.device)
-    _lib.call("pm_moe_combine", _p(c3), T, k, H, _p(out), _stream(c3.device))
+    _lib.call("pm_moe_combine", _p(c3), _p(row_of), T, k, H, _p(out), _stream(c3.device))
     return out
 
 

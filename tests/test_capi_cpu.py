@@ -68,8 +68,8 @@ def test_null_pointers_are_rejected_without_a_device():
     lib = _lib.load()
     st = lib.pm_moe_forward_fp8(None, None, None, None, None, None, None, 16, 2048, 768, 128, 8, None, None, 0, None)
     assert st == 1
-    assert lib.pm_moe_topk(None, 4, 128, 8, None, None, None) == 1
-    assert lib.pm_moe_combine(None, 4, 8, 2048, None, None) == 1
+    assert lib.pm_moe_topk(None, None, 4, 128, 8, None, None, None) == 1
+    assert lib.pm_moe_combine(None, None, 4, 8, 2048, None, None) == 1
     assert lib.pm_moe_read_status(None, None) == 1
 
 
