@@ -53,6 +53,7 @@ def dist_init():
     import torch.distributed as dist
 
     rank, local = int(os.environ["RANK"]), int(os.environ.get("LOCAL_RANK", "0"))
+    os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep NCCL's banner off stdout: the JSON line is the output
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     return rank, ws, local
@@ -363,16 +364,8 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
 
     # NVFP4 variant at T=5120: weights from the same FP8 layer via the reference's
     # prepare_layer recipe, synthetic activation calibration
-    from prismyra_b200.kernels import nvfp4
-
-    nv = synth.make_nvfp4_layer(layer)
-    prep, act = nv["prepared"], nv["act"]
-    a1 = float(448.0 * 6.0 / (1.25 * act["w13_in_amax"]))
-    a2 = float(448.0 * 6.0 / (1.25 * max(act["w2_in_amax"])))
-    nw = {"w1": prep["w1"].to(dev), "w2": prep["w2"].to(dev), "w1_sf": nvfp4.block_scales(prep["s1"]).to(dev),
-          "w2_sf": nvfp4.block_scales(prep["s2"]).to(dev), "al1": (1.0 / (prep["g1"] * a1)).float().to(dev),
-          "al2": (1.0 / (prep["g2"] * a2)).float().to(dev)}
-    del nv, prep
+    nw = synth.nvfp4_device_layer(layer, dev)
+    a1, a2 = nw["a1"], nw["a2"]
 
     def nv_step():
         return ops.forward_nvfp4(x, nw["w1"], nw["w1_sf"], nw["al1"], a1, nw["w2"], nw["w2_sf"], nw["al2"], a2, K,

@@ -59,21 +59,30 @@ constexpr size_t smem_bytes() {
            sizeof(SmemTail);
 }
 
-// silu(g) * u on bf16 values with bf16 rounding after each step (vLLM silu_and_mul semantics).  The sigmoid uses
-// the fast exponential and division: the result is rounded to bf16 (8 significant bits) right after, so their
-// last-bit fp32 error changes an output only when it straddles a bf16 rounding boundary.
-__device__ __forceinline__ float silu_mul(float g, float u) {
-    const float s = bf16_round(__fdividef(g, 1.0f + __expf(-g)));
-    return bf16_round(s * u);
-}
+// silu(g) * u on bf16 values with bf16 rounding after each step (vLLM silu_and_mul semantics) is computed pairwise
+// in the gate_up epilogue.  The sigmoid uses the fast exponential and division: the result is rounded to bf16
+// (8 significant bits) right after, so their last-bit fp32 error changes an output only when it straddles a bf16
+// rounding boundary.
 
-// acc[c] += scale * TMEM[lane, col + c] for 32 consecutive columns.
+// acc[c] += scale * TMEM[lane, col + c] for 32 consecutive columns, as packed fp32x2 FMAs when PACKED.
+template <bool PACKED>
 __device__ __forceinline__ void promote32(uint32_t taddr, float scale, float* acc) {
     uint32_t r[32];
     tmem_ld32(taddr, r);
     tmem_ld_wait();
+    if (PACKED) {
+        const float2 s2 = make_float2(scale, scale);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) acc[i] = fmaf(__uint_as_float(r[i]), scale, acc[i]);
+        for (int i = 0; i < 32; i += 2) {
+            const float2 v = __ffma2_rn(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), s2,
+                                        make_float2(acc[i], acc[i + 1]));
+            acc[i] = v.x;
+            acc[i + 1] = v.y;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = fmaf(__uint_as_float(r[i]), scale, acc[i]);
+    }
 }
 
 template <int MODE>
@@ -202,6 +211,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row = q * 32 + lane;
         const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
         const int nb_total = args.n_total / 128;
+        // Packed FMAs halve the promotion's issue slots; in the down GEMM they cost spills, so it stays scalar.
+        constexpr bool kPackedPromote = MODE == 0;
         uint32_t it = 0;
         int local = 0;
         float acc[128];
@@ -231,15 +242,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t tb = t_lane + buf * kBN;
                 if (MODE == 0) {
                     // gate columns [64*half, 64*half+64) and up columns [128+64*half, ...+64) of the tile
-                    promote32(tb + 64 * half, s0, acc);
-                    promote32(tb + 64 * half + 32, s0, acc + 32);
-                    promote32(tb + 128 + 64 * half, s1, acc + 64);
-                    promote32(tb + 128 + 64 * half + 32, s1, acc + 96);
+                    promote32<kPackedPromote>(tb + 64 * half, s0, acc);
+                    promote32<kPackedPromote>(tb + 64 * half + 32, s0, acc + 32);
+                    promote32<kPackedPromote>(tb + 128 + 64 * half, s1, acc + 64);
+                    promote32<kPackedPromote>(tb + 128 + 64 * half + 32, s1, acc + 96);
                 } else {
-                    promote32(tb + 128 * half, s0, acc);
-                    promote32(tb + 128 * half + 32, s0, acc + 32);
-                    promote32(tb + 128 * half + 64, s0, acc + 64);
-                    promote32(tb + 128 * half + 96, s0, acc + 96);
+                    promote32<kPackedPromote>(tb + 128 * half, s0, acc);
+                    promote32<kPackedPromote>(tb + 128 * half + 32, s0, acc + 32);
+                    promote32<kPackedPromote>(tb + 128 * half + 64, s0, acc + 64);
+                    promote32<kPackedPromote>(tb + 128 * half + 96, s0, acc + 96);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -249,12 +260,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             if (MODE == 0) {
                 // bf16(gate), bf16(up) -> silu(gate) * up in bf16 -> e4m3 with one scale per 128 columns.
+                // Pairs share each rounding instruction (the conversion pipe, not the FMA pipe, bounds this loop).
                 float amax = 0.0f;
 #pragma unroll
-                for (int c = 0; c < 64; ++c) {
-                    const float y = silu_mul(bf16_round(acc[c]), bf16_round(acc[64 + c]));
-                    acc[c] = y;
-                    amax = fmaxf(amax, fabsf(y));
+                for (int c = 0; c < 64; c += 2) {
+                    const float2 g = bf16x2_round(acc[c], acc[c + 1]);
+                    const float2 u = bf16x2_round(acc[64 + c], acc[64 + c + 1]);
+                    const float2 s2 = silu2(g);
+                    const float2 sg = bf16x2_round(s2.x, s2.y);
+                    const float2 p2 = __fmul2_rn(sg, u);
+                    const float2 y = bf16x2_round(p2.x, p2.y);
+                    acc[c] = y.x;
+                    acc[c + 1] = y.y;
+                    amax = fmaxf(amax, fmaxf(fabsf(y.x), fabsf(y.y)));
                 }
                 // The other column half of this row lives in another warp: exchange the half maxima through
                 // shared memory, synchronised by an mbarrier (a bounded wait, unlike a named barrier).
@@ -266,15 +284,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
                 // y * (1/s) instead of y / s: the e4m3 code keeps 3 significand bits, so the quotient's last-bit
                 // difference moves a code only when it lies on an e4m3 rounding midpoint.
+                // The saturating conversion clamps to +-448 exactly as clamp-then-round does.
                 const float inv = __frcp_rn(sc);
+                const float2 inv2 = make_float2(inv, inv);
                 uint32_t packed[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float q0 = fminf(fmaxf(acc[4 * i + 0] * inv, -448.0f), 448.0f);
-                    const float q1 = fminf(fmaxf(acc[4 * i + 1] * inv, -448.0f), 448.0f);
-                    const float q2 = fminf(fmaxf(acc[4 * i + 2] * inv, -448.0f), 448.0f);
-                    const float q3 = fminf(fmaxf(acc[4 * i + 3] * inv, -448.0f), 448.0f);
-                    packed[i] = (uint32_t)e4m3x2(q0, q1) | ((uint32_t)e4m3x2(q2, q3) << 16);
+                    const float2 q01 = __fmul2_rn(make_float2(acc[4 * i + 0], acc[4 * i + 1]), inv2);
+                    const float2 q23 = __fmul2_rn(make_float2(acc[4 * i + 2], acc[4 * i + 3]), inv2);
+                    packed[i] = (uint32_t)e4m3x2(q01.x, q01.y) | ((uint32_t)e4m3x2(q23.x, q23.y) << 16);
                 }
                 uint4* dst = reinterpret_cast<uint4*>(args.out_q + (size_t)grow * args.inter + nt * 128 + 64 * half);
 #pragma unroll

@@ -151,11 +151,6 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                  : "memory");
 }
 
-__device__ __forceinline__ float silu_mul_bf16(float g, float u) {
-    const float s = bf16_round(__fdividef(g, 1.0f + __expf(-g)));
-    return bf16_round(s * u);
-}
-
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
@@ -303,7 +298,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // bf16(alpha*gate), bf16(alpha*up) -> silu(gate)*up in bf16 -> NVFP4 with the layer's a2 scale.
                 float y[64];
 #pragma unroll
-                for (int c = 0; c < 64; ++c) y[c] = silu_mul_bf16(bf16_round(acc[c]), bf16_round(acc[64 + c]));
+                for (int c = 0; c < 64; c += 2) {
+                    const float2 g = bf16x2_round(acc[c], acc[c + 1]);
+                    const float2 u = bf16x2_round(acc[64 + c], acc[64 + c + 1]);
+                    const float2 s2 = silu2(g);
+                    const float2 sg = bf16x2_round(s2.x, s2.y);
+                    const float2 p2 = __fmul2_rn(sg, u);
+                    const float2 yy = bf16x2_round(p2.x, p2.y);
+                    y[c] = yy.x;
+                    y[c + 1] = yy.y;
+                }
                 uint32_t codes[8];
                 uint32_t sfw = 0;
 #pragma unroll

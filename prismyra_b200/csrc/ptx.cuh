@@ -178,6 +178,18 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
 // ------------------------------------------------------------------------------------------- numerics
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// silu of a pair: g / (1 + exp(-g)) with the fast exponential and division intrinsics; the 1 + e is one packed
+// fp32x2 add.
+__device__ __forceinline__ float2 silu2(float2 g) {
+    const float2 den = __fadd2_rn(make_float2(__expf(-g.x), __expf(-g.y)), make_float2(1.0f, 1.0f));
+    return make_float2(__fdividef(g.x, den.x), __fdividef(g.y, den.y));
+}
+
+// Two values rounded to bf16 with one packed conversion (cvt.rn.bf16x2.f32) and widened back.
+__device__ __forceinline__ float2 bf16x2_round(float a, float b) {
+    return __bfloat1622float2(__floats2bfloat162_rn(a, b));
+}
+
 // Two fp32 -> two e4m3 bytes (low byte = a), round to nearest even, saturating.
 __device__ __forceinline__ uint16_t e4m3x2(float a, float b) {
     return static_cast<uint16_t>(__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3));

@@ -1,9 +1,10 @@
 """Run the routed-expert layer on synthetic data a fixed number of times (for profilers and quick checks).
 
-    python -m prismyra_b200.run --tokens 5120 --iters 3 [--format fp8]
+    python -m prismyra_b200.run --tokens 5120 --iters 3 [--format fp8|nvfp4]
 
-Builds the seeded synthetic layer (H=2048, I=768, E=128, top-8 by default) on the current GPU, runs the forward
-``--iters`` times on the current stream and prints the output checksum and the device status.
+Builds the seeded synthetic layer (H=2048, I=768, E=128, top-8 by default; NVFP4 weights derived from the FP8
+ones) on the current GPU, runs the forward ``--iters`` times on the current stream and prints the output checksum
+and the device status.
 """
 
 from __future__ import annotations
@@ -24,16 +25,26 @@ def main() -> None:
     ap.add_argument("--experts", type=int, default=128)
     ap.add_argument("--top-k", type=int, default=8)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--format", choices=["fp8", "nvfp4"], default="fp8")
     a = ap.parse_args()
     dev = torch.device("cuda", torch.cuda.current_device())
     L = synth.make_fp8_layer(a.tokens, a.hidden, a.inter, a.experts, seed=a.seed, device=dev, gen_device="cuda")
+    if a.format == "nvfp4":
+        nw = synth.nvfp4_device_layer(L, dev)
+
+        def step():
+            return ops.forward_nvfp4(L["x"], nw["w1"], nw["w1_sf"], nw["al1"], nw["a1"], nw["w2"], nw["w2_sf"],
+                                     nw["al2"], nw["a2"], a.top_k, router_w=L["router_w"])
+    else:
+        def step():
+            return ops.forward_fp8(L["x"], L["w1"], L["w1_s"], L["w2"], L["w2_s"], a.top_k, router_w=L["router_w"])
     torch.cuda.synchronize()
     out = None
     for _ in range(a.iters):
-        out = ops.forward_fp8(L["x"], L["w1"], L["w1_s"], L["w2"], L["w2_s"], a.top_k, router_w=L["router_w"])
-    ws, _ = ops.workspace_for(L["x"], a.tokens, a.hidden, a.inter, a.experts, a.top_k)
+        out = step()
+    ws, _ = ops.workspace_for(L["x"], a.tokens, a.hidden, a.inter, a.experts, a.top_k, int(a.format == "nvfp4"))
     ops.read_status(ws)
-    print(f"tokens={a.tokens} iters={a.iters} checksum={out.float().abs().sum().item():.6e} status=ok")
+    print(f"format={a.format} tokens={a.tokens} iters={a.iters} checksum={out.float().abs().sum().item():.6e} status=ok")
 
 
 if __name__ == "__main__":

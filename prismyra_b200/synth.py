@@ -104,3 +104,17 @@ def make_nvfp4_layer(fp8: dict, calib_tokens: int = 256, top_k: int = 8) -> dict
         amax2 = max(amax2, float(a.abs().max()))
     act = {"w13_in_amax": float(fp8["x"].float().abs().max()), "w2_in_amax": [amax2]}
     return {"prepared": prep, "act": act}
+
+
+def nvfp4_device_layer(fp8: dict, dev) -> dict:
+    """The NVFP4 operands of :func:`make_nvfp4_layer` on ``dev`` in the kernels' layouts: FP4 weights, blocked
+    e4m3 scale tiles, per-expert alphas 1/(g_w * g_a) and the two activation global scales 448*6/(1.25*amax)."""
+    from .kernels import nvfp4
+
+    nv = make_nvfp4_layer(fp8)
+    prep, act = nv["prepared"], nv["act"]
+    a1 = float(448.0 * 6.0 / (1.25 * act["w13_in_amax"]))
+    a2 = float(448.0 * 6.0 / (1.25 * max(act["w2_in_amax"])))
+    return {"w1": prep["w1"].to(dev), "w2": prep["w2"].to(dev), "w1_sf": nvfp4.block_scales(prep["s1"]).to(dev),
+            "w2_sf": nvfp4.block_scales(prep["s2"]).to(dev), "al1": (1.0 / (prep["g1"] * a1)).float().to(dev),
+            "al2": (1.0 / (prep["g2"] * a2)).float().to(dev), "a1": a1, "a2": a2}
