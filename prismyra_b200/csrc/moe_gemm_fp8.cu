@@ -16,8 +16,8 @@
 //           weight in fp32, rounds to bf16 and scatters the row to c3[flat index].
 // Warp roles (384 threads, three warpgroups): warp 0 issues TMA loads, warp 1 owns TMEM and issues the MMAs
 // (warps 2-3 idle); warpgroups 1 and 2 (warps 4-11) promote and run the epilogue.  Epilogue warp w reads TMEM
-// lanes 32*(w%4).. and one half of the tile's columns.  Registers are rebalanced with setmaxnreg: 56 for
-// warpgroup 0 and 224 for the epilogue warpgroups (56*128 + 224*256 = 64512 = 168 * 384, the launch's total).
+// lanes 32*(w%4).. and one half of the tile's columns.  Registers are rebalanced with setmaxnreg: 40 for
+// warpgroup 0 and 232 for the epilogue warpgroups (40*128 + 232*256 = 64512 = 168 * 384, the launch's total).
 #include "moe_internal.h"
 #include "ptx.cuh"
 
@@ -38,7 +38,8 @@ constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kThreads = 384;
 constexpr int kEpiWarp0 = 4;          // first epilogue warp
 constexpr int kEpiWarps = 8;
-constexpr uint32_t kTmemCols = 512;         // two 256-column fp32 accumulators
+constexpr uint32_t kTmemCols = 512;
+constexpr int kEidCache = 512;              // tiles per CTA whose expert ids are staged in shared memory         // two 256-column fp32 accumulators
 constexpr uint32_t kIdesc = idesc_f32acc(0 /*e4m3*/, 0 /*e4m3*/, kBM, kBN);
 
 struct SmemTail {
@@ -50,6 +51,7 @@ struct SmemTail {
     uint64_t xbar[2];         // epilogue amax exchange, one per tile parity
     uint32_t tmem_base;
     int abort;
+    int eid[kEidCache];  // expert of this CTA's j-th tile, j < kEidCache
     float amax_x[2][2][kBM];  // [tile parity][column half][row]
 };
 
@@ -133,7 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int num_tiles = (*args.num_post_pad / kBM) * args.n_tiles;
 
     if (warp < kEpiWarp0) {
-      asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 40;" ::: "memory");
       if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer
         int stage = 0;
@@ -204,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     } else {
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 232;" ::: "memory");
         // ------------------------------------------------------------------ promotion + epilogue
         const int q = warp & 3;                    // TMEM lane quarter
         const int half = (warp - kEpiWarp0) >> 2;  // column half
@@ -216,19 +218,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t it = 0;
         int local = 0;
         float acc[128];
+        // Per-tile inputs are fetched ahead so that no tile starts on a dependent chain of global loads: the
+        // experts of this CTA's tiles are staged in shared memory once, the next tile's first K block scales are
+        // loaded during the last K block, and (down) the row's flat index at the start of the tile and its routing
+        // weight during the second K block.  Later tiles than the staged ones read their expert from global memory.
+        const int ptid = threadIdx.x - kEpiWarp0 * 32;
+        for (int j = ptid; j < kEidCache; j += kEpiWarps * 32) {
+            const long long t = blockIdx.x + (long long)j * gridDim.x;
+            tail->eid[j] = t < num_tiles ? args.expert_ids[t / args.n_tiles] : 0;
+        }
+        named_bar_sync(1, kEpiWarps * 32);
+        float sa_n = 0.0f, b0_n = 0.0f, b1_n = 0.0f;  // scales of the next K block to promote
+        if (blockIdx.x < num_tiles) {
+            const int e = tail->eid[0], nt = blockIdx.x % args.n_tiles;
+            const float* bs = args.b_scale + (size_t)e * nb_total * KB;
+            sa_n = args.a_scale[(size_t)((blockIdx.x / args.n_tiles) * kBM + row) * KB];
+            b0_n = bs[(size_t)(MODE == 0 ? nt : nt * 2 + half) * KB];
+            b1_n = bs[(size_t)(MODE == 0 ? args.inter / 128 + nt : nt * 2 + half) * KB];
+        }
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
             const int mb = tile / args.n_tiles, nt = tile % args.n_tiles;
-            const int e = args.expert_ids[mb];
+            const int e = local < kEidCache ? tail->eid[local] : args.expert_ids[mb];
             const int grow = mb * kBM + row;
             const float* bs = args.b_scale + (size_t)e * nb_total * KB;
             const float* as = args.a_scale + (size_t)grow * KB;
             // the two block-scale rows this thread multiplies by (gate/up halves, or its column half)
             const float* bs0 = bs + (size_t)(MODE == 0 ? nt : nt * 2 + half) * KB;
             const float* bs1 = bs + (size_t)(MODE == 0 ? args.inter / 128 + nt : nt * 2 + half) * KB;
+            const int flat = MODE == 1 ? args.sorted_ids[grow] : 0;
+            float w = 0.0f;
 #pragma unroll
             for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
             bool ok = true;
-            float sa_n = as[0], b0_n = bs0[0], b1_n = bs1[0];  // scales of the next K block, loaded ahead
             for (int kb = 0; kb < KB; ++kb, ++it) {
                 const uint32_t buf = it & 1u, use = it >> 1;
                 const float s0 = sa_n * b0_n, s1 = sa_n * b1_n;
@@ -236,7 +257,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     sa_n = as[kb + 1];
                     b0_n = bs0[kb + 1];
                     b1_n = bs1[kb + 1];
+                } else if (tile + (int)gridDim.x < num_tiles) {
+                    const int t2 = tile + gridDim.x, j2 = local + 1;
+                    const int m2 = t2 / args.n_tiles, n2 = t2 % args.n_tiles;
+                    const int e2 = j2 < kEidCache ? tail->eid[j2] : args.expert_ids[m2];
+                    const float* bs2 = args.b_scale + (size_t)e2 * nb_total * KB;
+                    sa_n = args.a_scale[(size_t)(m2 * kBM + row) * KB];
+                    b0_n = bs2[(size_t)(MODE == 0 ? n2 : n2 * 2 + half) * KB];
+                    b1_n = bs2[(size_t)(MODE == 0 ? args.inter / 128 + n2 : n2 * 2 + half) * KB];
                 }
+                if (MODE == 1 && kb == (KB > 1 ? 1 : 0)) w = flat < args.n_valid ? args.topk_w[flat] : 0.0f;
                 if (!mbar_wait(bar_tfull + 8 * buf, use & 1u, abort)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t tb = t_lane + buf * kBN;
@@ -302,8 +332,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
                 // Weight, round, and stage this warp's 32 rows x 128 columns in shared memory (one row per
                 // thread), then write the rows out as coalesced 256-byte segments, two rows per instruction.
-                const int flat = args.sorted_ids[grow];
-                const float w = flat < args.n_valid ? args.topk_w[flat] : 0.0f;
                 constexpr int RB = Cfg<MODE>::kStageRowBytes;
                 uint8_t* wst = staging + (size_t)(warp - kEpiWarp0) * 32 * RB;
 #pragma unroll
