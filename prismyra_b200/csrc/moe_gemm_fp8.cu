@@ -62,9 +62,9 @@ constexpr size_t smem_bytes() {
 }
 
 // silu(g) * u on bf16 values with bf16 rounding after each step (vLLM silu_and_mul semantics) is computed pairwise
-// in the gate_up epilogue.  The sigmoid uses the fast exponential and division: the result is rounded to bf16
-// (8 significant bits) right after, so their last-bit fp32 error changes an output only when it straddles a bf16
-// rounding boundary.
+// in the gate_up epilogue.  The sigmoid comes from the hardware tanh (relative error below 2^-11): the result is
+// rounded to bf16 (8 significant bits) right after, so the error changes an output only when it straddles a bf16
+// rounding boundary, and then by one bf16 unit before the e4m3 requantisation.
 
 // acc[c] += scale * TMEM[lane, col + c] for 32 consecutive columns, as packed fp32x2 FMAs when PACKED.
 template <bool PACKED>
