@@ -93,10 +93,15 @@ int pm_moe_router_topk(const void *x, const void *router_w, const float *bias, i
 int pm_moe_topk(const void *logits, const float *bias, int T, int E, int k, float *topk_w, int32_t *topk_ids,
                 pm_stream_t stream);
 
+/* Bytes of device scratch pm_moe_align needs (its per-chunk expert counts); 0 for invalid arguments.  No
+ * counterpart in the reference (vLLM allocates this scratch inside moe_align_block_size). */
+size_t pm_moe_align_workspace_bytes(int T, int k, int E);
+
 /* Expert alignment: vllm/model_executor/layers/fused_moe/moe_align_block_size.py:11-99 with block 128, the
  * reference's call at vllm/model_executor/layers/fused_moe/fused_moe.py:1536-1585.  Flat indices grouped by
- * expert in ascending order, padded with T*k.  Needs the workspace for its per-chunk counts.  expert_off and
- * slot_of (the inverse permutation, slot_of[t*k + j] = slot) may be NULL. */
+ * expert in ascending order, padded with T*k.  Needs pm_moe_align_workspace_bytes(T, k, E) bytes of workspace
+ * for its per-chunk counts.  expert_off and slot_of (the inverse permutation, slot_of[t*k + j] = slot) may be
+ * NULL. */
 int pm_moe_align(const int32_t *topk_ids, int T, int k, int E, int32_t *sorted_ids, int32_t *expert_ids,
                  int32_t *num_post_pad, int32_t *expert_off, int32_t *slot_of, void *workspace,
                  size_t workspace_bytes, pm_stream_t stream);

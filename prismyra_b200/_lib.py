@@ -34,6 +34,7 @@ SIGNATURES: dict[str, tuple] = {
     "pm_moe_abi_version": (_I, []),
     "pm_moe_status_string": (ctypes.c_char_p, [_I]),
     "pm_moe_max_slots": (_I, [_I, _I, _I]),
+    "pm_moe_align_workspace_bytes": (ctypes.c_size_t, [_I, _I, _I]),
     "pm_moe_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I]),
     "pm_moe_workspace_region": (_I, [_I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_Z), ctypes.POINTER(_Z)]),
     "pm_moe_router_topk": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
@@ -107,3 +108,8 @@ def workspace_region(T: int, H: int, I: int, E: int, k: int, fmt: int, region: s
 
 def max_slots(T: int, E: int, k: int) -> int:
     return int(load().pm_moe_max_slots(T, E, k))
+
+
+def align_workspace_bytes(T: int, k: int, E: int) -> int:
+    """Scratch bytes pm_moe_align needs for T tokens, top-k and E experts."""
+    return int(load().pm_moe_align_workspace_bytes(T, k, E))

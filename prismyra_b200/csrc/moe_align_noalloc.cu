@@ -25,7 +25,7 @@ namespace {
 
 constexpr long kNoallocMaxFlat = 1L << 20;
 constexpr int kNoallocMaxExperts = 256;
-constexpr int kNoallocChunks = (int)(kNoallocMaxFlat / kAlignChunk);
+constexpr int kNoallocChunks = kAlignMaxChunks;
 constexpr size_t kNoallocCountBytes = sizeof(int32_t) * (size_t)kNoallocChunks * kNoallocMaxExperts;
 
 static __device__ __align__(256) int32_t g_noalloc_counts[kNoallocChunks * kNoallocMaxExperts];

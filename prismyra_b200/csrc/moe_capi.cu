@@ -85,7 +85,7 @@ static Layout layout_of(int T, int H, int I, int E, int k, int fmt) {
     Layout L;
     const long n = (long)T * k;
     const int ms = max_slots_of(T, E, k);
-    const int chunks = n > 0 ? cdiv(n, kAlignChunk) : 1;
+    const int chunks = n > 0 ? align_chunks(n) : 1;
     const bool fp4 = fmt == PM_FMT_NVFP4;
     L.len[PM_WS_STATUS] = 4 * sizeof(int32_t);
     L.len[PM_WS_LOGITS] = (size_t)T * E * 2;
@@ -207,14 +207,19 @@ int pm_moe_topk(const void* logits, const float* bias, int T, int E, int k, floa
     return cuda_status(launch_topk(logits, bias, T, E, k, topk_w, topk_ids, (cudaStream_t)stream));
 }
 
+size_t pm_moe_align_workspace_bytes(int T, int k, int E) {
+    if (T < 0 || k <= 0 || E <= 0 || E > 1024) return 0;
+    const long n = (long)T * k;
+    return (size_t)(n > 0 ? align_chunks(n) : 1) * E * 4;
+}
+
 int pm_moe_align(const int32_t* topk_ids, int T, int k, int E, int32_t* sorted_ids, int32_t* expert_ids,
                  int32_t* num_post_pad, int32_t* expert_off, int32_t* slot_of, void* workspace,
                  size_t workspace_bytes, pm_stream_t stream) {
     if (T < 0 || k <= 0 || E <= 0 || E > 1024) return PM_ERR_INVALID;
     if (!sorted_ids || !expert_ids || !num_post_pad || !workspace || (T > 0 && !topk_ids)) return PM_ERR_INVALID;
     const long n = (long)T * k;
-    const int chunks = n > 0 ? cdiv(n, kAlignChunk) : 1;
-    if (workspace_bytes < (size_t)chunks * E * 4) return PM_ERR_WORKSPACE;
+    if (workspace_bytes < pm_moe_align_workspace_bytes(T, k, E)) return PM_ERR_WORKSPACE;
     DeviceInfo d;
     const int st = current_device_info(&d);
     if (st != PM_OK) return st;

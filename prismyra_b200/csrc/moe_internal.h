@@ -12,7 +12,15 @@ namespace pm {
 constexpr int kBlockM = 128;  // rows of one GEMM tile == the alignment block of the expert permutation
 constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 16;
-constexpr int kAlignChunk = 4096;  // flat (token, slot) indices handled by one CTA of the alignment kernels
+// The alignment kernels split the n flat (token, slot) indices into at most kAlignMaxChunks chunks of
+// align_chunk(n) indices (at least 1024, a multiple of 256); the per-chunk count table has align_chunks(n) rows.
+constexpr int kAlignMaxChunks = 256;
+inline int align_chunk(long n) {
+    long c = (n + kAlignMaxChunks - 1) / kAlignMaxChunks;
+    if (c < 1024) c = 1024;
+    return (int)((c + 255) / 256 * 256);
+}
+inline int align_chunks(long n) { return n > 0 ? (int)((n + align_chunk(n) - 1) / align_chunk(n)) : 0; }
 
 inline int cdiv(long a, long b) { return static_cast<int>((a + b - 1) / b); }
 

@@ -98,13 +98,17 @@ __global__ void __launch_bounds__(256) topk_kernel(const __nv_bfloat16* __restri
 }
 
 // ------------------------------------------------------------------------------------------- alignment
+// Two launches over chunks of align_chunk(n) flat indices (at most kAlignMaxChunks chunks, so that every CTA of
+// the second pass can afford to read the whole count table).
+//
 // Pass 1: per-chunk expert histogram.
-__global__ void __launch_bounds__(256) align_count_kernel(const int32_t* __restrict__ ids, int n, int E,
+__global__ void __launch_bounds__(256) align_count_kernel(const int32_t* __restrict__ ids, int n, int E, int chunk,
                                                           int32_t* __restrict__ counts) {
     extern __shared__ int32_t cnt[];
     for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
-    const int lo = blockIdx.x * kAlignChunk, hi = min(n, lo + kAlignChunk);
+    const int lo = blockIdx.x * chunk, hi = min(n, lo + chunk);
+#pragma unroll 4
     for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         const int e = ids[i];
         if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
@@ -113,56 +117,89 @@ __global__ void __launch_bounds__(256) align_count_kernel(const int32_t* __restr
     for (int e = threadIdx.x; e < E; e += blockDim.x) counts[(size_t)blockIdx.x * E + e] = cnt[e];
 }
 
-// Pass 2 (one CTA, one thread per expert): expert totals, padded offsets, per-chunk bases, block -> expert
-// table, padding slots and the padded total.
-__global__ void __launch_bounds__(1024) align_scan_kernel(int32_t* __restrict__ counts, int nchunks, int n, int E,
-                                                          int32_t* __restrict__ sorted,
-                                                          int32_t* __restrict__ expert_ids,
-                                                          int32_t* __restrict__ num_post_pad,
-                                                          int32_t* __restrict__ expert_off) {
-    __shared__ int32_t scan[1024];
-    const int e = threadIdx.x;
-    int total = 0;
-    if (e < E)
-        for (int c = 0; c < nchunks; ++c) {
-            const int v = counts[(size_t)c * E + e];
-            counts[(size_t)c * E + e] = total;  // exclusive prefix over chunks, relative to the expert's start
-            total += v;
-        }
-    const int padded = (total + kBlockM - 1) / kBlockM * kBlockM;
-    scan[e] = (e < E) ? padded : 0;
-    __syncthreads();
-    for (int o = 1; o < 1024; o <<= 1) {  // inclusive Hillis-Steele scan
-        const int v = (e >= o) ? scan[e - o] : 0;
-        __syncthreads();
-        scan[e] += v;
-        __syncthreads();
-    }
-    const int off = scan[e] - ((e < E) ? padded : 0);
-    if (e < E) {
-        for (int c = 0; c < nchunks; ++c) counts[(size_t)c * E + e] += off;
-        for (int b = off / kBlockM; b < (off + padded) / kBlockM; ++b) expert_ids[b] = e;
-        for (int i = off + total; i < off + padded; ++i) sorted[i] = n;
-        if (expert_off != nullptr) {
-            expert_off[e] = off;
-            if (e == E - 1) expert_off[E] = off + padded;
-        }
-    }
-    if (e == 1023) *num_post_pad = scan[1023];
-}
+constexpr int kAlignEPT = 4;  // experts per thread in pass 2 (E <= 1024 with 256 threads)
 
-// Pass 3: scatter each chunk's indices to their slots.  Ranks are stable: within a round of 256 indices,
-// equal experts are ordered by warp (via per-warp counts) and by lane (via the match mask).
-__global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __restrict__ ids, int n, int E,
-                                                            const int32_t* __restrict__ bases,
+// Pass 2: every CTA derives, from the count table, each expert's padded offset (an exclusive scan of the padded
+// totals) and the number of its indices in earlier chunks, then scatters its chunk's indices with stable ranks:
+// within a round of 256 indices, equal experts are ordered by warp (per-warp counts) and by lane (match mask).
+// CTA 0 also writes the block -> expert table, the padding slots (value n), the expert offsets and the total.
+__global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __restrict__ ids, int n, int E, int chunk,
+                                                            int nchunks, const int32_t* __restrict__ counts,
                                                             int32_t* __restrict__ sorted,
+                                                            int32_t* __restrict__ expert_ids,
+                                                            int32_t* __restrict__ num_post_pad,
+                                                            int32_t* __restrict__ expert_off,
                                                             int32_t* __restrict__ slot_of) {
     extern __shared__ int32_t sm[];
-    int32_t* base = sm;            // [E]
-    int32_t* wcnt = sm + E;        // [8][E]
+    int32_t* base = sm;            // [E]  next slot of each expert for this chunk
+    int32_t* pad = sm + E;         // [E]  padded totals, then padded offsets
+    int32_t* wcnt = sm + 2 * E;    // [8][E]
+    __shared__ int32_t wsum[8];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int e = tid; e < E; e += 256) base[e] = bases[(size_t)blockIdx.x * E + e];
-    const int lo = blockIdx.x * kAlignChunk, hi = min(n, lo + kAlignChunk);
+
+    int tot[kAlignEPT], pre[kAlignEPT];
+#pragma unroll
+    for (int q = 0; q < kAlignEPT; ++q) {
+        const int e = tid + 256 * q;
+        tot[q] = pre[q] = 0;
+        if (e < E)
+            for (int c = 0; c < nchunks; ++c) {
+                const int v = counts[(size_t)c * E + e];
+                tot[q] += v;
+                if (c < (int)blockIdx.x) pre[q] += v;
+            }
+        if (e < E) pad[e] = (tot[q] + kBlockM - 1) / kBlockM * kBlockM;
+    }
+    __syncthreads();
+    // exclusive scan of pad[0..E): thread t owns entries [4t, 4t+4)
+    int loc[kAlignEPT], run = 0;
+#pragma unroll
+    for (int j = 0; j < kAlignEPT; ++j) {
+        const int e = kAlignEPT * tid + j;
+        loc[j] = run;
+        run += e < E ? pad[e] : 0;
+    }
+    int inc = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += v;
+    }
+    if (lane == 31) wsum[warp] = inc;
+    __syncthreads();
+    int wpre = 0, total = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        wpre += w < warp ? wsum[w] : 0;
+        total += wsum[w];
+    }
+    const int tpre = wpre + inc - run;  // exclusive prefix of this thread's four entries
+#pragma unroll
+    for (int j = 0; j < kAlignEPT; ++j) {
+        const int e = kAlignEPT * tid + j;
+        if (e < E) pad[e] = tpre + loc[j];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < kAlignEPT; ++q) {
+        const int e = tid + 256 * q;
+        if (e >= E) continue;
+        const int off = pad[e];
+        base[e] = off + pre[q];
+        if (blockIdx.x == 0) {
+            const int padded = (tot[q] + kBlockM - 1) / kBlockM * kBlockM;
+            for (int blk = off / kBlockM; blk < (off + padded) / kBlockM; ++blk) expert_ids[blk] = e;
+            for (int i = off + tot[q]; i < off + padded; ++i) sorted[i] = n;
+            if (expert_off != nullptr) expert_off[e] = off;
+        }
+    }
+    if (blockIdx.x == 0 && tid == 0) {
+        *num_post_pad = total;
+        if (expert_off != nullptr) expert_off[E] = total;
+    }
+    __syncthreads();
+
+    const int lo = blockIdx.x * chunk, hi = min(n, lo + chunk);
     for (int r0 = lo; r0 < hi; r0 += 256) {
         for (int q = tid; q < 8 * E; q += 256) wcnt[q] = 0;
         __syncthreads();
@@ -181,9 +218,9 @@ __global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __res
         }
         __syncthreads();
         for (int q = tid; q < E; q += 256) {
-            int s = 0;
-            for (int w = 0; w < 8; ++w) s += wcnt[w * E + q];
-            base[q] += s;
+            int s2 = 0;
+            for (int w = 0; w < 8; ++w) s2 += wcnt[w * E + q];
+            base[q] += s2;
         }
         __syncthreads();
     }
@@ -201,16 +238,16 @@ cudaError_t launch_topk(const void* logits, const float* bias, int T, int E, int
 
 cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int32_t* sorted, int32_t* expert_ids,
                          int32_t* num_post_pad, int32_t* expert_off, int32_t* slot_of, cudaStream_t s) {
-    const int nchunks = n > 0 ? cdiv(n, kAlignChunk) : 0;
+    if (E > kAlignEPT * 256) return cudaErrorInvalidValue;
+    const int chunk = align_chunk(n);
+    const int nchunks = align_chunks(n);
     if (nchunks > 0) {
-        align_count_kernel<<<nchunks, 256, sizeof(int32_t) * E, s>>>(ids, n, E, counts);
+        align_count_kernel<<<nchunks, 256, sizeof(int32_t) * E, s>>>(ids, n, E, chunk, counts);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
-    align_scan_kernel<<<1, 1024, 0, s>>>(counts, nchunks, n, E, sorted, expert_ids, num_post_pad, expert_off);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess || nchunks == 0) return e;
-    align_scatter_kernel<<<nchunks, 256, sizeof(int32_t) * 9 * E, s>>>(ids, n, E, counts, sorted, slot_of);
+    align_scatter_kernel<<<nchunks > 0 ? nchunks : 1, 256, sizeof(int32_t) * 10 * E, s>>>(
+        ids, n, E, chunk, nchunks, counts, sorted, expert_ids, num_post_pad, expert_off, slot_of);
     return cudaGetLastError();
 }
 

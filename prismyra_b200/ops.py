@@ -171,7 +171,7 @@ def align(ids: torch.Tensor, E: int, out=None):
                torch.full((ms // 128,), -1, dtype=torch.int32, device=dev),
                torch.zeros(1, dtype=torch.int32, device=dev), torch.zeros(E + 1, dtype=torch.int32, device=dev),
                torch.zeros(T * k, dtype=torch.int32, device=dev),
-               torch.zeros(max(1, -(-T * k // 4096)) * E, dtype=torch.int32, device=dev))
+               torch.zeros(_lib.align_workspace_bytes(T, k, E) // 4, dtype=torch.int32, device=dev))
     sorted_ids, expert_ids, npp, off, slot_of, scratch = out
     _lib.call("pm_moe_align", _p(ids), T, k, E, _p(sorted_ids), _p(expert_ids), _p(npp), _p(off), _p(slot_of),
               _p(scratch), scratch.numel() * 4, _stream(dev))

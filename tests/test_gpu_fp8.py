@@ -108,10 +108,12 @@ def test_router_is_row_count_invariant(layer):
 
 
 @pytest.mark.parametrize("T,E_,k_", [(1, 128, 8), (7, 8, 4), (128, 128, 8), (513, 128, 8), (5120, 128, 8),
-                                     (40000 // 8, 128, 8), (1000, 256, 16)])
+                                     (40000 // 8, 128, 8), (1000, 256, 16), (300, 1024, 16), (1 << 17, 128, 8)])
 def test_align_matches_oracle(T, E_, k_):
+    # (1 << 17) x 8 = 2^20 indices: the largest chunks (4096) and the most chunks (256); E = 1024: four experts
+    # per thread in the scan
     g = torch.Generator().manual_seed(T + E_)
-    ids = torch.stack([torch.randperm(E_, generator=g)[:k_] for _ in range(T)]).to(torch.int32)
+    ids = torch.rand(T, E_, generator=g).argsort(dim=1)[:, :k_].contiguous().to(torch.int32)
     if T >= 7:
         ids[:, 0] = 0  # a hot expert
     s, eids, npp, off, slot_of, _ = ops.align(ids.to(DEV), E_)
