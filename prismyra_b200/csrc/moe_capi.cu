@@ -65,7 +65,7 @@ static int current_device_info(DeviceInfo* out) {
 }
 
 // ------------------------------------------------------------------------------------------- workspace
-constexpr int kRegions = PM_WS_SLOT_OF + 1;
+constexpr int kRegions = PM_WS_ROUTER_PART + 1;
 
 struct Layout {
     size_t off[kRegions];
@@ -102,6 +102,7 @@ static Layout layout_of(int T, int H, int I, int E, int k, int fmt) {
     L.len[PM_WS_A2_SCALE] = (size_t)ms * (fp4 ? I / 16 : (I / 128) * 4);
     L.len[PM_WS_C3] = (size_t)n * H * 2;
     L.len[PM_WS_SLOT_OF] = (size_t)n * 4;
+    L.len[PM_WS_ROUTER_PART] = router_split_bytes(T, H, E);
     size_t o = 0;
     for (int r = 0; r < kRegions; ++r) {
         L.off[r] = o;
@@ -331,6 +332,7 @@ int pm_moe_forward_fp8(const void* x, const void* router_w, const void* logits, 
     cudaStream_t s = (cudaStream_t)stream;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     auto R = [&](int r) { return ws + L.off[r]; };
+    float* router_part = L.len[PM_WS_ROUTER_PART] > 0 ? reinterpret_cast<float*>(R(PM_WS_ROUTER_PART)) : nullptr;
     int32_t* status = reinterpret_cast<int32_t*>(R(PM_WS_STATUS));
     float* topk_w = reinterpret_cast<float*>(R(PM_WS_TOPK_W));
     int32_t* topk_ids = reinterpret_cast<int32_t*>(R(PM_WS_TOPK_IDS));
@@ -348,7 +350,8 @@ int pm_moe_forward_fp8(const void* x, const void* router_w, const void* logits, 
     if (logits != nullptr)
         e = launch_topk(logits, nullptr, T, E, k, topk_w, topk_ids, s);
     else
-        e = launch_router_topk(x, router_w, nullptr, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s);
+        e = launch_router_topk(x, router_w, nullptr, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s,
+                               router_part);
     if (e != cudaSuccess) return PM_ERR_CUDA;
     int32_t* slot_of = reinterpret_cast<int32_t*>(R(PM_WS_SLOT_OF));
     e = launch_align(topk_ids, T * k, E, reinterpret_cast<int32_t*>(R(PM_WS_COUNTS)), sorted, expert_ids, npp,
@@ -478,6 +481,7 @@ int pm_moe_forward_nvfp4(const void* x, const void* router_w, const void* logits
     cudaStream_t s = (cudaStream_t)stream;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     auto R = [&](int r) { return ws + L.off[r]; };
+    float* router_part = L.len[PM_WS_ROUTER_PART] > 0 ? reinterpret_cast<float*>(R(PM_WS_ROUTER_PART)) : nullptr;
     int32_t* status = reinterpret_cast<int32_t*>(R(PM_WS_STATUS));
     float* topk_w = reinterpret_cast<float*>(R(PM_WS_TOPK_W));
     int32_t* topk_ids = reinterpret_cast<int32_t*>(R(PM_WS_TOPK_IDS));
@@ -489,7 +493,8 @@ int pm_moe_forward_nvfp4(const void* x, const void* router_w, const void* logits
     cudaError_t e =
         logits != nullptr
             ? launch_topk(logits, nullptr, T, E, k, topk_w, topk_ids, s)
-            : launch_router_topk(x, router_w, nullptr, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s);
+            : launch_router_topk(x, router_w, nullptr, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s,
+                               router_part);
     if (e != cudaSuccess) return PM_ERR_CUDA;
     e = launch_align(topk_ids, T * k, E, reinterpret_cast<int32_t*>(R(PM_WS_COUNTS)), sorted, expert_ids, npp,
                      reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_OFF)), slot_of, s);

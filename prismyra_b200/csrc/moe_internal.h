@@ -13,11 +13,13 @@ constexpr int kBlockM = 128;  // rows of one GEMM tile == the alignment block of
 constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 16;
 // The alignment kernels split the n flat (token, slot) indices into at most kAlignMaxChunks chunks of
-// align_chunk(n) indices (at least 1024, a multiple of 256); the per-chunk count table has align_chunks(n) rows.
+// align_chunk(n) indices (one chunk up to 1024 indices, else at least 512, a multiple of 256); the per-chunk count
+// table has align_chunks(n) rows.
 constexpr int kAlignMaxChunks = 256;
 inline int align_chunk(long n) {
+    if (n <= 1024) return 1024;
     long c = (n + kAlignMaxChunks - 1) / kAlignMaxChunks;
-    if (c < 1024) c = 1024;
+    if (c < 512) c = 512;
     return (int)((c + 255) / 256 * 256);
 }
 inline int align_chunks(long n) { return n > 0 ? (int)((n + align_chunk(n) - 1) / align_chunk(n)) : 0; }
@@ -26,11 +28,18 @@ inline int cdiv(long a, long b) { return static_cast<int>((a + b - 1) / b); }
 
 // Router projection (bf16, fp32 accumulation in a fixed order per row) fused with softmax / top-k.
 // bias (may be null): fp32 [E] added to each logit before the ranking.
+// part: fp32 scratch of router_split_bytes(T, H, E) bytes for the split launch shape, or nullptr (fused shape);
+// both give the same bits.
+size_t router_split_bytes(int T, int H, int E);
 cudaError_t launch_router_topk(const void* x, const void* w, const float* bias, int T, int H, int E, int k,
-                               void* logits, float* topk_w, int32_t* topk_ids, int32_t* err, cudaStream_t s);
+                               void* logits, float* topk_w, int32_t* topk_ids, int32_t* err, cudaStream_t s,
+                               float* part = nullptr);
 // Softmax / top-k / renormalise from given bf16 logits (+ optional fp32 bias per expert).
 cudaError_t launch_topk(const void* logits, const float* bias, int T, int E, int k, float* topk_w, int32_t* topk_ids,
                         cudaStream_t s);
+// Top-k from fp32 chunk partials part[c][t][e] (c < chunks, added in ascending order): also writes the bf16 logits.
+cudaError_t launch_topk_partials(const float* part, int chunks, void* logits, const float* bias, int T, int E, int k,
+                                 float* topk_w, int32_t* topk_ids, cudaStream_t s);
 // Stable counting sort of the flat (token, slot) indices by expert, padded per expert to kBlockM.
 // slot_of (may be null) receives the inverse permutation: slot_of[flat index] = its slot.
 cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int32_t* sorted, int32_t* expert_ids,

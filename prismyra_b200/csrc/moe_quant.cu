@@ -7,57 +7,55 @@
 namespace pm {
 namespace {
 
-// One warp per token row.  Lane L of an iteration holds 64 consecutive columns; lanes 2g and 2g+1 share one
-// 128-column group.  s = max(amax, 1e-10) * (1/448); q = e4m3(clamp(x / s, -448, 448)) with an IEEE division,
-// exactly as the reference's Triton kernel states it.  With slot_of the row is written to the token's k slots
-// (its expert-ordered copies for the gate_up GEMM; vLLM reads the same rows through sorted_ids // top_k); the
-// padding slots are left unwritten -- their GEMM rows are computed and discarded, never stored.
+// One half-warp per (token, 128-column group), two groups per warp: each lane converts 8 columns, the group's amax
+// is a half-warp reduction, and every copy of the group is one coalesced 128-byte segment (so small token counts
+// still spread over the whole GPU).  s = max(amax, 1e-10) * (1/448); q = e4m3(clamp(x / s, -448, 448)) with an
+// IEEE division, exactly as the reference's Triton kernel states it.  With slot_of the row is written to the
+// token's k slots (its expert-ordered copies for the gate_up GEMM; vLLM reads the same rows through
+// sorted_ids // top_k); the padding slots are left unwritten -- their GEMM rows are computed and discarded, never
+// stored.  Without slot_of the single copy goes to row t.
 __global__ void __launch_bounds__(256) quant_fp8_kernel(const __nv_bfloat16* __restrict__ x, int T, int H, int k,
                                                         const int32_t* __restrict__ slot_of,
                                                         uint8_t* __restrict__ x_q, float* __restrict__ x_s) {
-    const int lane = threadIdx.x & 31;
-    const int warps = gridDim.x * (blockDim.x >> 5);
-    for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < T; row += warps) {
-        const __nv_bfloat16* src = x + (size_t)row * H;
-        const int ncopies = slot_of != nullptr ? k : 1;
-        for (int c0 = 0; c0 < H; c0 += 32 * 64) {
-            const int col = c0 + lane * 64;
-            const bool act = col < H;
-            float v[64];
-            float amax = 0.0f;
-            if (act) {
+    const int lane = threadIdx.x & 31, sub = lane & 15;
+    const int G = H / 128;
+    const long items = (long)T * G;
+    const long pairs = (items + 1) / 2;
+    const long nwarps = ((long)gridDim.x * blockDim.x) >> 5;
+    const int ncopies = slot_of != nullptr ? k : 1;
+    for (long wp = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; wp < pairs; wp += nwarps) {
+        const long item = 2 * wp + (lane >> 4);
+        const bool valid = item < items;
+        const long row = valid ? item / G : 0;
+        const int col = valid ? (int)(item % G) * 128 + sub * 8 : 0;
+        float v[8];
+        float amax = 0.0f;
+        if (valid) {
+            const uint4 w = *reinterpret_cast<const uint4*>(x + row * H + col);
+            const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&w);
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const uint4 w = *reinterpret_cast<const uint4*>(src + col + u * 8);
-                    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&w);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        v[u * 8 + i] = __bfloat162float(b[i]);
-                        amax = fmaxf(amax, fabsf(v[u * 8 + i]));
-                    }
-                }
+            for (int i = 0; i < 8; ++i) {
+                v[i] = __bfloat162float(b[i]);
+                amax = fmaxf(amax, fabsf(v[i]));
             }
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-            const float sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
-            if (act) {
-                uint32_t packed[16];
+        }
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float q0 = fminf(fmaxf(__fdiv_rn(v[4 * i + 0], sc), -448.0f), 448.0f);
-                    const float q1 = fminf(fmaxf(__fdiv_rn(v[4 * i + 1], sc), -448.0f), 448.0f);
-                    const float q2 = fminf(fmaxf(__fdiv_rn(v[4 * i + 2], sc), -448.0f), 448.0f);
-                    const float q3 = fminf(fmaxf(__fdiv_rn(v[4 * i + 3], sc), -448.0f), 448.0f);
-                    packed[i] = (uint32_t)e4m3x2(q0, q1) | ((uint32_t)e4m3x2(q2, q3) << 16);
-                }
-                for (int c = 0; c < ncopies; ++c) {
-                    const size_t dst = slot_of != nullptr ? (size_t)slot_of[(size_t)row * k + c] : (size_t)row;
-                    uint4* d = reinterpret_cast<uint4*>(x_q + dst * H + col);
+        for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (!valid) continue;
+        const float sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
+        uint32_t packed[2];
 #pragma unroll
-                    for (int u = 0; u < 4; ++u)
-                        d[u] = make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
-                    if ((lane & 1) == 0) x_s[dst * (H / 128) + col / 128] = sc;
-                }
-            }
+        for (int i = 0; i < 2; ++i) {
+            const float q0 = fminf(fmaxf(__fdiv_rn(v[4 * i + 0], sc), -448.0f), 448.0f);
+            const float q1 = fminf(fmaxf(__fdiv_rn(v[4 * i + 1], sc), -448.0f), 448.0f);
+            const float q2 = fminf(fmaxf(__fdiv_rn(v[4 * i + 2], sc), -448.0f), 448.0f);
+            const float q3 = fminf(fmaxf(__fdiv_rn(v[4 * i + 3], sc), -448.0f), 448.0f);
+            packed[i] = (uint32_t)e4m3x2(q0, q1) | ((uint32_t)e4m3x2(q2, q3) << 16);
+        }
+        for (int c = 0; c < ncopies; ++c) {
+            const size_t dst = slot_of != nullptr ? (size_t)slot_of[row * k + c] : (size_t)row;
+            *reinterpret_cast<uint2*>(x_q + dst * H + col) = make_uint2(packed[0], packed[1]);
+            if (sub == 0) x_s[dst * G + col / 128] = sc;
         }
     }
 }
@@ -97,7 +95,8 @@ cudaError_t launch_quant_fp8(const void* x, int T, int H, int k, const int32_t* 
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int blocks = min(cdiv(T, 8), sms * 8);
+    const long pairs = ((long)T * (H / 128) + 1) / 2;  // one warp per two (token, group) items
+    const int blocks = (int)min((pairs + 7) / 8, (long)sms * 16);
     quant_fp8_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), T, H, k, slot_of, x_q, x_s);
     return cudaGetLastError();
 }

@@ -97,6 +97,38 @@ __global__ void __launch_bounds__(256) topk_kernel(const __nv_bfloat16* __restri
     warp_topk(v, E, k, topk_w + (size_t)warp * k, topk_ids + (size_t)warp * k);
 }
 
+// The same from the router's fp32 chunk partials: logit = bf16(((P_0 + P_1) + P_2) + ...), written out, then ranked.
+__global__ void __launch_bounds__(256) topk_partials_kernel(const float* __restrict__ part, int chunks,
+                                                            __nv_bfloat16* __restrict__ logits,
+                                                            const float* __restrict__ bias, int T, int E, int k,
+                                                            float* __restrict__ topk_w, int32_t* __restrict__ topk_ids) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= T) return;
+    float v[kMaxEPT];
+#pragma unroll
+    for (int i = 0; i < kMaxEPT; ++i) {
+        const int e = lane + 32 * i;
+        v[i] = -INFINITY;
+        if (e < E) {
+            // sixteen chunk loads in flight per batch, then added in chunk order
+            float a = 0.0f;
+            for (int c0 = 0; c0 < chunks; c0 += 16) {
+                float pv[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) pv[j] = c0 + j < chunks ? part[((size_t)(c0 + j) * T + warp) * E + e] : 0.0f;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (c0 + j < chunks) a = (c0 + j == 0) ? pv[j] : a + pv[j];
+            }
+            const __nv_bfloat16 b = __float2bfloat16_rn(a);
+            logits[(size_t)warp * E + e] = b;
+            v[i] = __bfloat162float(b) + (bias != nullptr ? bias[e] : 0.0f);
+        }
+    }
+    warp_topk(v, E, k, topk_w + (size_t)warp * k, topk_ids + (size_t)warp * k);
+}
+
 // ------------------------------------------------------------------------------------------- alignment
 // Two launches over chunks of align_chunk(n) flat indices (at most kAlignMaxChunks chunks, so that every CTA of
 // the second pass can afford to read the whole count table).
@@ -117,12 +149,16 @@ __global__ void __launch_bounds__(256) align_count_kernel(const int32_t* __restr
     for (int e = threadIdx.x; e < E; e += blockDim.x) counts[(size_t)blockIdx.x * E + e] = cnt[e];
 }
 
-constexpr int kAlignEPT = 4;  // experts per thread in pass 2 (E <= 1024 with 256 threads)
+constexpr int kAlignEPT = 4;     // experts per thread in pass 2 (E <= 1024 with 256 threads)
+constexpr int kAlignRounds = 16;  // rounds of 256 indices a chunk may have for its ids to be held in registers
 
 // Pass 2: every CTA derives, from the count table, each expert's padded offset (an exclusive scan of the padded
 // totals) and the number of its indices in earlier chunks, then scatters its chunk's indices with stable ranks:
 // within a round of 256 indices, equal experts are ordered by warp (per-warp counts) and by lane (match mask).
-// CTA 0 also writes the block -> expert table, the padding slots (value n), the expert offsets and the total.
+// The block -> expert table and the padding slots (value n) are written warp-cooperatively, experts spread over
+// the CTAs; CTA 0 writes the expert offsets and the total.  With a single chunk (counts == nullptr) pass 1 is not
+// launched: every CTA counts the (at most one chunk of) indices itself, CTA 0 scatters them and the others only
+// share the padding writes.
 __global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __restrict__ ids, int n, int E, int chunk,
                                                             int nchunks, const int32_t* __restrict__ counts,
                                                             int32_t* __restrict__ sorted,
@@ -133,22 +169,55 @@ __global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __res
     extern __shared__ int32_t sm[];
     int32_t* base = sm;            // [E]  next slot of each expert for this chunk
     int32_t* pad = sm + E;         // [E]  padded totals, then padded offsets
-    int32_t* wcnt = sm + 2 * E;    // [8][E]
+    int32_t* totv = sm + 2 * E;    // [E]  indices per expert
+    int32_t* wcnt = sm + 3 * E;    // [8][E]
     __shared__ int32_t wsum[8];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool single = counts == nullptr;
+    const int cta_chunk = single ? 0 : (int)blockIdx.x;
+    const int lo = cta_chunk * chunk, hi = (single && blockIdx.x > 0) ? lo : min(n, lo + chunk);
+    const int rounds = (min(n, lo + chunk) - lo + 255) / 256;
+    const bool held = rounds <= kAlignRounds;
 
+    // this chunk's ids, loaded up front (their latency overlaps the count table reads)
+    int idv[kAlignRounds];
+#pragma unroll
+    for (int r = 0; r < kAlignRounds; ++r) {
+        const int i = lo + r * 256 + tid;
+        idv[r] = (held && r < rounds && i < min(n, lo + chunk)) ? ids[i] : -1;
+    }
     int tot[kAlignEPT], pre[kAlignEPT];
+    if (counts == nullptr) {  // single chunk: count here
+        for (int e = tid; e < E; e += 256) wcnt[e] = 0;
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < kAlignRounds; ++r)
+            if (idv[r] >= 0 && idv[r] < E) atomicAdd(&wcnt[idv[r]], 1);
+        __syncthreads();
+    }
 #pragma unroll
     for (int q = 0; q < kAlignEPT; ++q) {
         const int e = tid + 256 * q;
         tot[q] = pre[q] = 0;
-        if (e < E)
-            for (int c = 0; c < nchunks; ++c) {
-                const int v = counts[(size_t)c * E + e];
-                tot[q] += v;
-                if (c < (int)blockIdx.x) pre[q] += v;
+        if (e < E) {
+            if (single) {
+                tot[q] = wcnt[e];
+            } else {
+                // sixteen loads in flight per batch
+                for (int c0 = 0; c0 < nchunks; c0 += 16) {
+                    int v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = c0 + j < nchunks ? counts[(size_t)(c0 + j) * E + e] : 0;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        tot[q] += v[j];
+                        if (c0 + j < cta_chunk) pre[q] += v[j];
+                    }
+                }
             }
-        if (e < E) pad[e] = (tot[q] + kBlockM - 1) / kBlockM * kBlockM;
+            pad[e] = (tot[q] + kBlockM - 1) / kBlockM * kBlockM;
+            totv[e] = tot[q];
+        }
     }
     __syncthreads();
     // exclusive scan of pad[0..E): thread t owns entries [4t, 4t+4)
@@ -183,28 +252,37 @@ __global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __res
 #pragma unroll
     for (int q = 0; q < kAlignEPT; ++q) {
         const int e = tid + 256 * q;
-        if (e >= E) continue;
-        const int off = pad[e];
-        base[e] = off + pre[q];
-        if (blockIdx.x == 0) {
-            const int padded = (tot[q] + kBlockM - 1) / kBlockM * kBlockM;
-            for (int blk = off / kBlockM; blk < (off + padded) / kBlockM; ++blk) expert_ids[blk] = e;
-            for (int i = off + tot[q]; i < off + padded; ++i) sorted[i] = n;
-            if (expert_off != nullptr) expert_off[e] = off;
+        if (e < E) {
+            base[e] = pad[e] + pre[q];
+            if (blockIdx.x == 0 && expert_off != nullptr) expert_off[e] = pad[e];
         }
     }
     if (blockIdx.x == 0 && tid == 0) {
         *num_post_pad = total;
         if (expert_off != nullptr) expert_off[E] = total;
     }
+    // block table and padding slots: one warp per expert, experts spread over the CTAs; the padding run is written
+    // with 16-byte stores between its unaligned head and tail (sorted + i is 16-byte aligned iff (i + mis) % 4 == 0)
+    const int mis = (int)((reinterpret_cast<uintptr_t>(sorted) >> 2) & 3);
+    for (int e = (int)blockIdx.x * 8 + warp; e < E; e += (int)gridDim.x * 8) {
+        const int off = pad[e], te = totv[e];
+        const int padded = (te + kBlockM - 1) / kBlockM * kBlockM;
+        for (int blk = off / kBlockM + lane; blk < (off + padded) / kBlockM; blk += 32) expert_ids[blk] = e;
+        const int p0 = off + te, p1 = off + padded;
+        const int pa = min(p1, p0 + ((4 - ((p0 + mis) & 3)) & 3));
+        const int pb = pa + ((p1 - pa) & ~3);
+        if (p0 + lane < pa) sorted[p0 + lane] = n;
+        for (int i = pa + 4 * lane; i < pb; i += 128) *reinterpret_cast<int4*>(sorted + i) = make_int4(n, n, n, n);
+        if (pb + lane < p1) sorted[pb + lane] = n;
+    }
     __syncthreads();
 
-    const int lo = blockIdx.x * chunk, hi = min(n, lo + chunk);
-    for (int r0 = lo; r0 < hi; r0 += 256) {
+    // one round of up to 256 indices starting at r0; e_in is this thread's id (or -1 past the chunk)
+    auto round = [&](int r0, int e_in) {
         for (int q = tid; q < 8 * E; q += 256) wcnt[q] = 0;
         __syncthreads();
         const int i = r0 + tid;
-        const int e = (i < hi) ? ids[i] : -1 - lane;  // distinct sentinels keep idle lanes apart
+        const int e = (i < hi) ? e_in : -1 - lane;  // distinct sentinels keep idle lanes apart
         const uint32_t peers = __match_any_sync(0xffffffffu, e);
         const int rank = __popc(peers & ((1u << lane) - 1u));
         const bool valid = (i < hi) && e >= 0 && e < E;
@@ -223,6 +301,14 @@ __global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __res
             base[q] += s2;
         }
         __syncthreads();
+    };
+    if (hi <= lo) return;  // a padding-only CTA of a single-chunk call
+    if (held) {
+#pragma unroll
+        for (int r = 0; r < kAlignRounds; ++r)
+            if (r < rounds) round(lo + r * 256, idv[r]);
+    } else {
+        for (int r0 = lo; r0 < hi; r0 += 256) round(r0, r0 + tid < hi ? ids[r0 + tid] : -1);
     }
 }
 
@@ -236,18 +322,30 @@ cudaError_t launch_topk(const void* logits, const float* bias, int T, int E, int
     return cudaGetLastError();
 }
 
+cudaError_t launch_topk_partials(const float* part, int chunks, void* logits, const float* bias, int T, int E, int k,
+                                 float* topk_w, int32_t* topk_ids, cudaStream_t s) {
+    if (T == 0) return cudaSuccess;
+    const int blocks = cdiv((long)T * 32, 256);
+    topk_partials_kernel<<<blocks, 256, 0, s>>>(part, chunks, static_cast<__nv_bfloat16*>(logits), bias, T, E, k,
+                                                topk_w, topk_ids);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int32_t* sorted, int32_t* expert_ids,
                          int32_t* num_post_pad, int32_t* expert_off, int32_t* slot_of, cudaStream_t s) {
     if (E > kAlignEPT * 256) return cudaErrorInvalidValue;
     const int chunk = align_chunk(n);
     const int nchunks = align_chunks(n);
-    if (nchunks > 0) {
+    if (nchunks > 1) {
         align_count_kernel<<<nchunks, 256, sizeof(int32_t) * E, s>>>(ids, n, E, chunk, counts);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
-    align_scatter_kernel<<<nchunks > 0 ? nchunks : 1, 256, sizeof(int32_t) * 10 * E, s>>>(
-        ids, n, E, chunk, nchunks, counts, sorted, expert_ids, num_post_pad, expert_off, slot_of);
+    // a single chunk is scattered by CTA 0; the extra CTAs only share the padding writes
+    const int grid = nchunks > 1 ? nchunks : max(1, min(16, E / 8));
+    align_scatter_kernel<<<grid, 256, sizeof(int32_t) * 11 * E, s>>>(
+        ids, n, E, chunk, nchunks, nchunks > 1 ? counts : nullptr, sorted, expert_ids, num_post_pad, expert_off,
+        slot_of);
     return cudaGetLastError();
 }
 

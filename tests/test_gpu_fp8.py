@@ -100,6 +100,27 @@ def test_router_logits_and_topk(layer):
     np.testing.assert_allclose(bits(w), rw, rtol=1e-6)
 
 
+@pytest.mark.parametrize("T", [1, 37, 512, 2048, 2049])
+def test_router_split_and_fused_shapes_agree(layer, T):
+    """The layer forward runs the split router shape for small T (fp32 chunk partials summed by the top-k kernel),
+    the stage entry point the fused one; both must give the same logits and routing bit for bit."""
+    _, gpu = layer
+    x = gpu["x"][torch.arange(T, device=DEV) % 512].contiguous()
+    fused, w, ids = ops.router_topk(x, gpu["router_w"], K)
+    ops.forward_fp8(x, gpu["w1"], gpu["w1_s"], gpu["w2"], gpu["w2_s"], K, router_w=gpu["router_w"])
+    ws, _ = ops.workspace_for(x, T, H, I, E, K)
+    torch.cuda.synchronize()
+    split = _lib.workspace_region(T, H, I, E, K, 0, "router_part")[1] > 0
+    assert split == (T <= 2048)  # 16 x 4 fused CTAs at most for the split shape
+    region = lambda name: _lib.workspace_region(T, H, I, E, K, 0, name)
+    off, n = region("logits")
+    assert torch.equal(ws[off:off + n].view(torch.bfloat16).view(T, E), fused)
+    off, n = region("topk_ids")
+    assert torch.equal(ws[off:off + n].view(torch.int32).view(T, K), ids)
+    off, n = region("topk_w")
+    assert torch.equal(ws[off:off + n].view(torch.float32).view(T, K), w)
+
+
 def test_router_is_row_count_invariant(layer):
     _, gpu = layer
     full, _, _ = ops.router_topk(gpu["x"], gpu["router_w"], K)
@@ -130,6 +151,27 @@ def test_align_matches_oracle(T, E_, k_):
         blk = re == e
         if blk.any():
             assert offs[e] == np.argmax(blk) * 128
+
+
+@pytest.mark.parametrize("shift", [1, 2, 3])
+def test_align_into_outputs_that_are_not_16_byte_aligned(shift):
+    """The C ABI takes plain int32 pointers: the vectorised padding writes must respect any 4-byte alignment."""
+    T, E_, k_ = 300, 64, 4
+    g = torch.Generator().manual_seed(shift)
+    ids = torch.rand(T, E_, generator=g).argsort(dim=1)[:, :k_].contiguous().to(torch.int32).to(DEV)
+    ms = _lib.max_slots(T, E_, k_)
+    big = torch.full((ms + 8,), -7, dtype=torch.int32, device=DEV)
+    sorted_ids = big[shift:shift + ms]
+    eids = torch.full((ms // 128,), -1, dtype=torch.int32, device=DEV)
+    npp = torch.zeros(1, dtype=torch.int32, device=DEV)
+    scratch = torch.zeros(_lib.align_workspace_bytes(T, k_, E_) // 4, dtype=torch.int32, device=DEV)
+    P = lambda t: t.data_ptr()
+    _lib.call("pm_moe_align", P(ids), T, k_, E_, P(sorted_ids), P(eids), P(npp), None, None, P(scratch),
+              scratch.numel() * 4, torch.cuda.current_stream().cuda_stream)
+    rs, re, rn = O.align(bits(ids), E_, 128)
+    n = int(npp.item())
+    assert n == rn and np.array_equal(bits(sorted_ids)[:n], rs) and np.array_equal(bits(eids)[: n // 128], re)
+    assert (bits(big)[:shift] == -7).all() and (bits(big)[shift + n:] == -7).all()  # nothing outside the range
 
 
 def test_align_docstring_example(golden):
