@@ -241,6 +241,41 @@ int pm_moe_quant_fp8(const void* x, int T, int H, int k, const int32_t* slot_of,
     return cuda_status(launch_quant_fp8(x, T, H, k, slot_of, a_q, a_s, (cudaStream_t)stream));
 }
 
+// The few-tokens-per-expert GEMMs (weights as the 128-row MMA operand): used when T*k <= 32 E.
+static bool use_small_gemm(long n_valid, int H, int I, int E) {
+    return n_valid <= (long)kSmallTokensPerExpert * E && gemm_fp8_small_fits(0, H) && gemm_fp8_small_fits(1, I);
+}
+
+static int small_gemm_fp8(int mode, const uint8_t* a_q, const float* a_s, const uint8_t* w, const float* w_s,
+                          const int32_t* expert_ids, const int32_t* npp, const int32_t* sorted_ids,
+                          const float* topk_w, int max_slots, int n_valid, int H, int I, int E, uint8_t* out_q,
+                          float* out_s, void* c3, int32_t* err, int sms, cudaStream_t s) {
+    const int K = mode == 0 ? H : I, n_total = mode == 0 ? 2 * I : H;
+    CUtensorMap tt, tw;
+    if (!encode_tmap_2d_u8(&tt, a_q, (uint64_t)K, (uint64_t)max_slots, (uint64_t)K, 128, 32) ||
+        !encode_tmap_2d_u8(&tw, w, (uint64_t)K, (uint64_t)E * n_total, (uint64_t)K, 128, 128))
+        return PM_ERR_CUDA;
+    SmallGemmArgs g;
+    memset(&g, 0, sizeof(g));
+    g.a_scale = a_s;
+    g.b_scale = w_s;
+    g.expert_ids = expert_ids;
+    g.num_post_pad = npp;
+    g.sorted_ids = sorted_ids;
+    g.n_valid = n_valid;
+    g.n_total = n_total;
+    g.K = K;
+    g.n_tiles = (mode == 0 ? I : H) / 128;
+    g.max_units = (max_slots / kBlockM) * g.n_tiles;
+    g.inter = I;
+    g.out_q = out_q;
+    g.out_s = out_s;
+    g.topk_w = topk_w;
+    g.c3 = static_cast<__nv_bfloat16*>(c3);
+    g.err = err;
+    return cuda_status(launch_gemm_fp8_small(mode, tt, tw, g, sms, s));
+}
+
 int pm_moe_gemm1_fp8(const uint8_t* a_q, const float* a_s, const uint8_t* w1, const float* w1_s,
                      const int32_t* expert_ids, const int32_t* num_post_pad, int max_slots, int H, int I, int E,
                      uint8_t* out_q, float* out_s, int32_t* err, pm_stream_t stream) {
@@ -281,6 +316,10 @@ int pm_moe_gemm2_fp8(const uint8_t* a_q, const float* a_s, const uint8_t* w2, co
     if (!encode_tmap_2d_u8(&ta, a_q, (uint64_t)I, (uint64_t)max_slots, (uint64_t)I, 128, 128) ||
         !encode_tmap_2d_u8(&tb, w2, (uint64_t)I, (uint64_t)E * H, (uint64_t)I, 128, 128))
         return PM_ERR_CUDA;
+    // (the small kernel copies the activation scales in bulk: 16-byte aligned rows of scales)
+    if (use_small_gemm((long)T * k, H, I, E) && a16(a_s))
+        return small_gemm_fp8(1, a_q, a_s, w2, w2_s, expert_ids, num_post_pad, sorted_ids, topk_w, max_slots, T * k,
+                              H, I, E, nullptr, nullptr, c3, err, d.sms, (cudaStream_t)stream);
     GemmArgs g = gemm_args_common(a_s, w2_s, expert_ids, num_post_pad, H, I, H / 256, max_slots, I, err);
     g.sorted_ids = sorted_ids;
     g.topk_w = topk_w;
@@ -359,7 +398,11 @@ int pm_moe_forward_fp8(const void* x, const void* router_w, const void* logits, 
     if (e != cudaSuccess) return PM_ERR_CUDA;
     e = launch_quant_fp8(x, T, H, k, slot_of, a1, a1s, s);
     if (e != cudaSuccess) return PM_ERR_CUDA;
-    st = pm_moe_gemm1_fp8(a1, a1s, w1, w1_s, expert_ids, npp, L.max_slots, H, I, E, a2, a2s, status, stream);
+    if (use_small_gemm((long)T * k, H, I, E))
+        st = small_gemm_fp8(0, a1, a1s, w1, w1_s, expert_ids, npp, sorted, nullptr, L.max_slots, T * k, H, I, E, a2,
+                            a2s, nullptr, status, d.sms, s);
+    else
+        st = pm_moe_gemm1_fp8(a1, a1s, w1, w1_s, expert_ids, npp, L.max_slots, H, I, E, a2, a2s, status, stream);
     if (st != PM_OK) return st;
     st = pm_moe_gemm2_fp8(a2, a2s, w2, w2_s, expert_ids, npp, sorted, topk_w, L.max_slots, T, k, H, I, E, c3,
                           status, stream);

@@ -78,6 +78,34 @@ struct GemmArgs {
 cudaError_t launch_gemm_fp8(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, const GemmArgs& args,
                             int num_sms, cudaStream_t s);
 
+// Grouped FP8 GEMM for few tokens per expert (moe_gemm_fp8_small.cu): weights as the MMA's 128-row operand,
+// the real token sub-blocks of each 128-slot block as its N operand.
+struct SmallGemmArgs {
+    const float* a_scale;        // [rows, K/128]
+    const float* b_scale;        // [E, n_total/128, K/128]
+    const int32_t* expert_ids;   // [blocks]
+    const int32_t* num_post_pad; // [1]
+    const int32_t* sorted_ids;   // [rows] flat index per slot (n_valid = padding; a block's real slots first)
+    int n_valid;                 // T * k
+    int n_total;                 // rows of one expert's weight matrix (2I for gate_up, H for down)
+    int K;                       // reduction length (H for gate_up, I for down)
+    int n_tiles;                 // 128-column units along the output (I/128 or H/128)
+    int max_units;               // upper bound of units (grid sizing)
+    int inter;                   // I
+    int stages;                  // set by the launcher
+    uint8_t* out_q;              // gate_up: [rows, I] e4m3
+    float* out_s;                // gate_up: [rows, I/128]
+    const float* topk_w;         // down: [n_valid]
+    __nv_bfloat16* c3;           // down: [n_valid, H]
+    int* err;
+};
+// The small-token path is used when T*k <= kSmallTokensPerExpert * E and the K-block scale table fits.
+constexpr int kSmallTokensPerExpert = 32;
+bool gemm_fp8_small_fits(int mode, int K);
+// tm_tok: the slot-ordered FP8 activations with a {128, 32} box; tm_w: the weights with a {128, 128} box.
+cudaError_t launch_gemm_fp8_small(int mode, const CUtensorMap& tm_tok, const CUtensorMap& tm_w,
+                                  const SmallGemmArgs& args, int num_sms, cudaStream_t s);
+
 struct NvGemmArgs {
     const uint8_t* a_sf;          // blocked e4m3 scales of A: [rows/128][K/64][512]
     const uint8_t* b_sf;          // blocked e4m3 scales of B: [E][n_total/128][K/64][512]

@@ -268,6 +268,47 @@ def test_forward_matches_oracle(layer, T):
     assert l2 < 1e-2 and mx < 1e-2, (l2, mx)
 
 
+def test_small_token_gate_up_equals_the_large_tile_kernel(layer):
+    """At T*k <= 32 E the layer runs the swap-AB GEMMs (weights as the 128-row MMA operand).  Their gate_up output
+    must equal the large-tile kernel's on the same expert-ordered inputs: the same products and K-block
+    promotion, with the MMA operands exchanged."""
+    _, gpu = layer
+    T = 512
+    x = gpu["x"][:T].contiguous()
+    ops.forward_fp8(x, gpu["w1"], gpu["w1_s"], gpu["w2"], gpu["w2_s"], K, router_w=gpu["router_w"])
+    ws, _ = ops.workspace_for(x, T, H, I, E, K)
+    ms = _lib.max_slots(T, E, K)
+    reg = lambda name, dt, shape: ops.region(ws, T, H, I, E, K, 0, name, dt, shape).clone()
+    a1, a1s = reg("a1", torch.uint8, (ms, H)), reg("a1_scale", torch.float32, (ms, H // 128))
+    a2, a2s = reg("a2", torch.uint8, (ms, I)), reg("a2_scale", torch.float32, (ms, I // 128))
+    eids, npp = reg("expert_ids", torch.int32, (ms // 128,)), reg("num_post_pad", torch.int32, (1,))
+    srt = reg("sorted", torch.int32, (ms,))
+    big_q, big_s, err = ops.gemm1_fp8(a1, a1s, gpu["w1"], gpu["w1_s"], eids, npp)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    real = (srt < T * K).nonzero().squeeze(1)  # padding slots hold unspecified values in both
+    assert torch.equal(a2[real], big_q[real]) and torch.equal(a2s[real], big_s[real])
+
+
+def test_small_token_path_with_one_expert_taking_every_token(layer):
+    """Skewed routing at small T: one expert gets all 300 tokens (three 128-slot blocks, up to four 32-slot
+    sub-blocks per unit) while the rest share the other slots."""
+    L, gpu = layer
+    T = 300
+    x = gpu["x"][:T].contiguous()
+    g = torch.Generator().manual_seed(7)
+    logits = (torch.randn(T, E, generator=g) * 0.5)
+    logits[:, 5] = 6.0  # expert 5 is in every token's top-k
+    logits = logits.to(torch.bfloat16)
+    out = ops.forward_fp8(x, gpu["w1"], gpu["w1_s"], gpu["w2"], gpu["w2_s"], K, logits=logits.to(DEV))
+    ws, _ = ops.workspace_for(x, T, H, I, E, K)
+    ops.read_status(ws)
+    ref = O.moe_forward_fp8(bits(L["x"][:T]), bits(logits), bits(L["w1"]), bits(L["w1_s"]), bits(L["w2"]),
+                            bits(L["w2_s"]), K)
+    l2, mx = rel_err(bits(out), ref["out"])
+    assert l2 < 1e-2 and mx < 1e-2, (l2, mx)
+
+
 def test_forward_with_given_logits_equals_in_kernel_router(layer):
     _, gpu = layer
     x = gpu["x"][:256].contiguous()
