@@ -106,24 +106,33 @@ __global__ void __launch_bounds__(256) topk_partials_kernel(const float* __restr
     const int lane = threadIdx.x & 31;
     if (warp >= T) return;
     float v[kMaxEPT];
+    // all of this lane's chunk partials are loaded before any is added (one round trip for up to 8 chunks), then
+    // added in chunk order
+    constexpr int kC = 8;
+    for (int c0 = 0; c0 < chunks; c0 += kC) {
+        float pv[kMaxEPT][kC];
+#pragma unroll
+        for (int i = 0; i < kMaxEPT; ++i) {
+            const int e = lane + 32 * i;
+#pragma unroll
+            for (int j = 0; j < kC; ++j)
+                pv[i][j] = (e < E && c0 + j < chunks) ? part[((size_t)(c0 + j) * T + warp) * E + e] : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < kMaxEPT; ++i)
+#pragma unroll
+            for (int j = 0; j < kC; ++j)
+                if (c0 + j < chunks) v[i] = (c0 + j == 0) ? pv[i][j] : v[i] + pv[i][j];
+    }
 #pragma unroll
     for (int i = 0; i < kMaxEPT; ++i) {
         const int e = lane + 32 * i;
-        v[i] = -INFINITY;
         if (e < E) {
-            // sixteen chunk loads in flight per batch, then added in chunk order
-            float a = 0.0f;
-            for (int c0 = 0; c0 < chunks; c0 += 16) {
-                float pv[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) pv[j] = c0 + j < chunks ? part[((size_t)(c0 + j) * T + warp) * E + e] : 0.0f;
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    if (c0 + j < chunks) a = (c0 + j == 0) ? pv[j] : a + pv[j];
-            }
-            const __nv_bfloat16 b = __float2bfloat16_rn(a);
+            const __nv_bfloat16 b = __float2bfloat16_rn(v[i]);
             logits[(size_t)warp * E + e] = b;
             v[i] = __bfloat162float(b) + (bias != nullptr ? bias[e] : 0.0f);
+        } else {
+            v[i] = -INFINITY;
         }
     }
     warp_topk(v, E, k, topk_w + (size_t)warp * k, topk_ids + (size_t)warp * k);
