@@ -34,6 +34,19 @@ T_CTX, T_BRANCH, T_CPU_SAMPLE = 5120, 128, 512
 KERNELS_PER_STEP = 9  # router GEMM, top-k, 3 alignment passes, activation quant, gate_up, down, combine
 
 
+def profile_traffic(kernel: str):
+    """DRAM read + write bytes per launch of ``kernel`` ("gate_up") from the committed ncu summary of the T=5120
+    workload (the line ``traffic_bytes_per_launch <kernel>: <bytes>``), or None without one."""
+    try:
+        with open(ROOT / "profiles" / "gemm_fp8_t5120.md") as f:
+            for line in f:
+                if line.startswith(f"traffic_bytes_per_launch {kernel}:"):
+                    return int(line.split(":", 1)[1].strip())
+    except (OSError, ValueError):
+        pass
+    return None
+
+
 def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -326,13 +339,14 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
     x_dev = torch.empty_like(x)
 
     def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
         if world > 1:
-            o = ep_layer.forward(x_dev)
+            x_dev.copy_(x_host, non_blocking=True)
+            out_host.copy_(ep_layer.forward(x_dev), non_blocking=True)
         else:
-            o = ops.forward_fp8(x_dev, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K,
-                                router_w=layer["router_w"])
-        out_host.copy_(o, non_blocking=True)
+            # the public host-to-host call: 1024-row edge chunks around one long middle chunk, copies in both
+            # directions overlapping the layer
+            ops.forward_fp8_host(x_host, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K,
+                                 layer["router_w"], out_host=out_host)
 
     for _ in range(3):
         e2e_step()
@@ -396,7 +410,8 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
         "tflops": layer_tflops,
         "frac_fp8_peak": layer_tflops / fp8_peak,
         "roofline": {"bound": "tensor", "kernel": "moe_gemm_fp8_kernel<0> (gate_up)", "achieved": g1_tflops,
-                     "peak": fp8_peak, "unit": "TFLOP/s", "frac": g1_tflops / fp8_peak, "traffic": None,
+                     "peak": fp8_peak, "unit": "TFLOP/s", "frac": g1_tflops / fp8_peak,
+                     "traffic": profile_traffic("gate_up"),
                      "peak_source": f"2 x bf16_tflops of {pk['source']} MEASURED_PEAKS.json ({pk['bf16_tflops']})",
                      "flops_per_launch": fl["gemm1"]},
         "stages_ms": {k: round(v, 4) for k, v in st.items() if isinstance(v, float)},

@@ -125,6 +125,86 @@ def forward_fp8(x: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch
     return out
 
 
+class _HostPipe:
+    """Per-(device, thread) copy streams and device row buffers for :func:`forward_fp8_host` (grow-only, never
+    freed, so addresses stay stable across calls)."""
+
+    def __init__(self):
+        self._lock = threading.Lock()
+        self._state = {}
+
+    def get(self, device: torch.device, T: int, H: int):
+        key = (device.index, threading.get_ident())
+        with self._lock:
+            st = self._state.get(key)
+            if st is None:
+                st = {"h2d": torch.cuda.Stream(device), "d2h": torch.cuda.Stream(device), "rows": 0, "H": H}
+                self._state[key] = st
+            if st["rows"] < T or st["H"] != H:
+                st["x"] = torch.empty(T, H, dtype=torch.bfloat16, device=device)
+                st["out"] = torch.empty(T, H, dtype=torch.bfloat16, device=device)
+                st["rows"], st["H"] = T, H
+            return st
+
+
+_PIPE = _HostPipe()
+
+
+def host_chunks(T: int, edge_rows: int = 1024) -> list[tuple[int, int]]:
+    """Row ranges of :func:`forward_fp8_host`: a short first chunk (its upload is the only copy the GPU waits for),
+    one long middle chunk whose compute covers the long copies in both directions, and a short last chunk (its
+    download is the only copy left after the compute).  Every chunk streams all expert weights once, so there are
+    no more than three (at T=5120 on a B200 over PCIe 1024-row edges measured best: 0.96 ms per call against
+    1.17 ms for one upload, layer and download in series)."""
+    if T <= 4 * edge_rows:
+        return [(0, T)]
+    return [(0, edge_rows), (edge_rows, T - edge_rows), (T - edge_rows, T)]
+
+
+def forward_fp8_host(x_host: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch.Tensor,
+                     w2_s: torch.Tensor, top_k: int, router_w: torch.Tensor, out_host: torch.Tensor | None = None,
+                     edge_rows: int = 1024) -> torch.Tensor:
+    """The routed FP8 experts for a host-resident x [T, H] bf16 (pinned, so the copies overlap): rows go to the GPU,
+    through :func:`forward_fp8` and back in the chunks of :func:`host_chunks`, with the host-to-device copies, the
+    layer and the device-to-host copies on three streams so that both PCIe directions overlap the compute.  Every
+    row's result equals :func:`forward_fp8` on the whole batch (rows are independent, and the layer's launch shapes
+    agree bit for bit).  Ordered on the caller's current stream: returns once the work is queued; ``out_host``
+    [T, H] (pinned bf16) holds the result when that stream has reached this point."""
+    _need(x_host.dim() == 2 and x_host.dtype == torch.bfloat16 and x_host.device.type == "cpu",
+          "x_host must be a host bf16 [T, H] tensor")
+    dev = w1.device
+    T, H = x_host.shape
+    if out_host is None:
+        out_host = torch.empty(T, H, dtype=torch.bfloat16, pin_memory=True)
+    _need(tuple(out_host.shape) == (T, H) and out_host.dtype == torch.bfloat16 and out_host.device.type == "cpu",
+          "out_host must be a host bf16 [T, H] tensor")
+    if T == 0:
+        return out_host
+    st = _PIPE.get(dev, T, H)
+    comp = torch.cuda.current_stream(dev)
+    start = torch.cuda.Event()
+    start.record(comp)
+    st["h2d"].wait_event(start)  # the device row buffers are free once the caller's earlier work is done
+    st["d2h"].wait_event(start)
+    for r0, r1 in host_chunks(T, edge_rows):
+        xs, os_ = st["x"][r0:r1], st["out"][r0:r1]
+        with torch.cuda.stream(st["h2d"]):
+            xs.copy_(x_host[r0:r1], non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record(st["h2d"])
+        comp.wait_event(ready)
+        forward_fp8(xs, w1, w1_s, w2, w2_s, top_k, router_w=router_w, out=os_)
+        done = torch.cuda.Event()
+        done.record(comp)
+        st["d2h"].wait_event(done)
+        with torch.cuda.stream(st["d2h"]):
+            out_host[r0:r1].copy_(os_, non_blocking=True)
+    finished = torch.cuda.Event()
+    finished.record(st["d2h"])
+    comp.wait_event(finished)
+    return out_host
+
+
 def read_status(workspace: torch.Tensor) -> None:
     """Synchronise and raise if a kernel of the last forward on this workspace gave up on a bounded wait."""
     _lib.call("pm_moe_read_status", _p(workspace), _stream(workspace.device))

@@ -309,6 +309,21 @@ def test_small_token_path_with_one_expert_taking_every_token(layer):
     assert l2 < 1e-2 and mx < 1e-2, (l2, mx)
 
 
+@pytest.mark.parametrize("T,edge", [(512, 100), (300, 64), (5120, 512), (4096, 1000)])
+def test_host_pipelined_forward_equals_the_device_forward(layer, T, edge):
+    """Rows copied in, computed and copied out in chunks on three streams: the same bits as one device call (at
+    T=5120 the 512-row edge chunks take the few-tokens GEMMs and the middle the large-tile ones)."""
+    _, gpu = layer
+    x = gpu["x"][torch.arange(T, device=DEV) % 512].contiguous()
+    ref = ops.forward_fp8(x, gpu["w1"], gpu["w1_s"], gpu["w2"], gpu["w2_s"], K, router_w=gpu["router_w"]).cpu()
+    x_host = x.cpu().pin_memory()
+    assert len(ops.host_chunks(T, edge)) == 3
+    out = ops.forward_fp8_host(x_host, gpu["w1"], gpu["w1_s"], gpu["w2"], gpu["w2_s"], K, gpu["router_w"],
+                               edge_rows=edge)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+
+
 def test_forward_with_given_logits_equals_in_kernel_router(layer):
     _, gpu = layer
     x = gpu["x"][:256].contiguous()
