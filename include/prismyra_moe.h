@@ -137,7 +137,8 @@ int pm_moe_gemm2_fp8(const uint8_t *a_q, const float *a_s, const uint8_t *w2, co
 int pm_moe_combine(const void *c3, const int32_t *row_of, int T, int k, int H, void *out, pm_stream_t stream);
 
 /* Row scatter for expert parallelism (no counterpart in the reference, which runs on one device):
- * dst + dst_index[i]*dst_stride <- src + i*src_stride, row_bytes bytes per row (multiples of 16). */
+ * dst + dst_index[i]*dst_stride <- src + i*src_stride, row_bytes bytes per row (multiples of 16); rows whose
+ * dst_index is negative are skipped. */
 int pm_moe_scatter_rows(const void *src, int rows, int row_bytes, int src_stride, const int32_t *dst_index,
                         void *dst, int dst_stride, pm_stream_t stream);
 

@@ -101,7 +101,8 @@ cudaError_t launch_quant_fp8(const void* x, int T, int H, int k, const int32_t* 
     return cudaGetLastError();
 }
 
-// dst row dst_index[i] (dst_stride bytes apart) = src row i (src_stride bytes apart), row_bytes bytes each.
+// dst row dst_index[i] (dst_stride bytes apart) = src row i (src_stride bytes apart), row_bytes bytes each;
+// rows with a negative dst_index are skipped.
 __global__ void __launch_bounds__(256) scatter_rows_kernel(const uint8_t* __restrict__ src, int rows, int row_bytes,
                                                            int src_stride, const int32_t* __restrict__ dst_index,
                                                            uint8_t* __restrict__ dst, int dst_stride) {
@@ -110,8 +111,10 @@ __global__ void __launch_bounds__(256) scatter_rows_kernel(const uint8_t* __rest
     for (long q = (long)blockIdx.x * blockDim.x + threadIdx.x; q < total; q += (long)gridDim.x * blockDim.x) {
         const long r = q / per_row;
         const int c = (int)(q % per_row) * 16;
+        const int d = dst_index[r];
+        if (d < 0) continue;  // a row with no destination (padding received from an expert-parallel peer)
         const uint4 v = *reinterpret_cast<const uint4*>(src + r * src_stride + c);
-        *reinterpret_cast<uint4*>(dst + (size_t)dst_index[r] * dst_stride + c) = v;
+        *reinterpret_cast<uint4*>(dst + (size_t)d * dst_stride + c) = v;
     }
 }
 

@@ -20,6 +20,8 @@ logic can be exercised on CPU ranks (gloo) with a reference backend.
 
 from __future__ import annotations
 
+from typing import NamedTuple
+
 import torch
 import torch.distributed as dist
 
@@ -35,6 +37,25 @@ def plan_dispatch(ids: torch.Tensor, experts_per_rank: int, world: int):
     send_counts = torch.bincount(dest, minlength=world)
     local_sorted = (flat[order] - dest[order] * experts_per_rank).to(torch.int32)
     return send_pos.to(torch.int32), send_counts, order, local_sorted
+
+
+class Plan(NamedTuple):
+    """Where each (token, slot) pair goes: ``send_pos`` [T*k] int32 (its row of the send buffer), ``counts``
+    [world] (rows of the send buffer for each destination rank, in rank order; padding rows included), ``rows``
+    (allocated send-buffer rows) and ``meta`` [rows, 2] int32 per send row: the local expert id at the
+    destination (-1 for a padding row) and the routing weight's fp32 bits."""
+
+    send_pos: torch.Tensor
+    counts: torch.Tensor
+    rows: int
+    meta: torch.Tensor
+
+
+def plan_on_host_order(ids: torch.Tensor, w: torch.Tensor, experts_per_rank: int, world: int) -> Plan:
+    """The plan from :func:`plan_dispatch` (unpadded; runs on any device, e.g. CPU ranks)."""
+    send_pos, counts, order, local_sorted = plan_dispatch(ids, experts_per_rank, world)
+    meta = torch.stack([local_sorted, w.reshape(-1)[order].contiguous().view(torch.int32)], 1).contiguous()
+    return Plan(send_pos, counts, ids.numel(), meta)
 
 
 def _a2a(out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits, group):
@@ -56,11 +77,30 @@ class CudaBackend:
         _, w, ids = ops.router_topk(x, self.router_w, self.top_k, bias=self.bias)
         return w, ids
 
-    def quant_dispatch(self, x, send_pos, k):
+    def plan(self, ids, w, experts_per_rank: int, world: int) -> Plan:
+        """The dispatch plan on the GPU: the expert alignment run on the destination ranks (a stable counting sort
+        of the pairs by rank, each rank's segment padded to 128 rows), then each send row's local expert and
+        weight gathered from its pair."""
+        from . import ops
+
+        T, k = ids.shape
+        n = T * k
+        dest = torch.div(ids, experts_per_rank, rounding_mode="floor").to(torch.int32)
+        srt, _, _, off, slot_of, _ = ops.align(dest, world)
+        p = srt.long()
+        valid = p < n
+        pc = torch.where(valid, p, torch.zeros_like(p))
+        local = torch.where(valid, ids.reshape(-1)[pc] - dest.reshape(-1)[pc] * experts_per_rank,
+                            torch.full_like(pc, -1).to(ids.dtype))
+        wv = torch.where(valid, w.reshape(-1)[pc], torch.zeros((), dtype=w.dtype, device=w.device))
+        meta = torch.stack([local.to(torch.int32), wv.contiguous().view(torch.int32)], 1).contiguous()
+        return Plan(slot_of, (off[1:] - off[:-1]).to(torch.int64), srt.numel(), meta)
+
+    def quant_dispatch(self, x, send_pos, k, rows=None):
         from . import ops
 
         T = x.shape[0]
-        return ops.quant_fp8(x, send_pos, k, T * k)
+        return ops.quant_fp8(x, send_pos, k, T * k if rows is None else rows)
 
     def local_experts(self, rq, rs, re, rw):
         from . import ops
@@ -68,6 +108,7 @@ class CudaBackend:
         N, H = rq.shape
         if N == 0:
             return torch.empty(0, H, dtype=torch.bfloat16, device=rq.device)
+        # padding rows (local expert -1) keep slot -1 and are skipped by the row scatter and the GEMMs
         s, eids, npp, _, slot_of, _ = ops.align(re.view(N, 1), self.local_experts_n)
         ms = s.numel()
         a_q = torch.empty(ms, H, dtype=torch.uint8, device=rq.device)
@@ -97,26 +138,30 @@ class ExpertParallelLayer:
         T, H = x.shape
         k = self.k
         w, ids = self.b.route(x)
-        send_pos, send_counts, order, local_sorted = plan_dispatch(ids, self.epr, self.world)
-        q, s = self.b.quant_dispatch(x, send_pos, k)
-        meta = torch.stack([local_sorted, w.reshape(-1)[order].contiguous().view(torch.int32)], 1).contiguous()
+        if hasattr(self.b, "plan"):
+            plan = self.b.plan(ids, w, self.epr, self.world)
+        else:
+            plan = plan_on_host_order(ids, w, self.epr, self.world)
+        q, s = self.b.quant_dispatch(x, plan.send_pos, k, plan.rows)
         if self.world == 1:
-            rq, rs, rmeta = q, s, meta
+            n = int(plan.counts.sum())
+            rq, rs, rmeta = q[:n], s[:n], plan.meta[:n]
             sc = rc = None
         else:
-            counts_in = send_counts.to(x.device)
-            counts_out = torch.empty_like(counts_in)
-            dist.all_to_all_single(counts_out, counts_in, group=self.group)
-            sc, rc = send_counts.tolist(), counts_out.tolist()
-            n = int(sum(rc))
-            rq = _a2a(torch.empty(n, H, dtype=q.dtype, device=x.device), q, rc, sc, self.group)
-            rs = _a2a(torch.empty(n, s.shape[1], dtype=s.dtype, device=x.device), s, rc, sc, self.group)
-            rmeta = _a2a(torch.empty(n, 2, dtype=meta.dtype, device=x.device), meta, rc, sc, self.group)
+            counts_out = torch.empty_like(plan.counts)
+            dist.all_to_all_single(counts_out, plan.counts, group=self.group)
+            both = torch.cat([plan.counts, counts_out]).tolist()  # the one host synchronisation: split sizes
+            sc, rc = both[: self.world], both[self.world:]
+            ns, n = int(sum(sc)), int(sum(rc))
+            rq = _a2a(torch.empty(n, H, dtype=q.dtype, device=x.device), q[:ns], rc, sc, self.group)
+            rs = _a2a(torch.empty(n, s.shape[1], dtype=s.dtype, device=x.device), s[:ns], rc, sc, self.group)
+            rmeta = _a2a(torch.empty(n, 2, dtype=plan.meta.dtype, device=x.device), plan.meta[:ns], rc, sc,
+                         self.group)
         re = rmeta[:, 0].contiguous()
         rw = rmeta[:, 1].contiguous().view(torch.float32)
         c3 = self.b.local_experts(rq, rs, re, rw)
         if self.world == 1:
             back = c3
         else:
-            back = _a2a(torch.empty(T * k, H, dtype=c3.dtype, device=x.device), c3, sc, rc, self.group)
-        return self.b.combine(back, T, k, send_pos)
+            back = _a2a(torch.empty(ns, H, dtype=c3.dtype, device=x.device), c3, sc, rc, self.group)
+        return self.b.combine(back, T, k, plan.send_pos)

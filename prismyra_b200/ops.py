@@ -250,7 +250,7 @@ def align(ids: torch.Tensor, E: int, out=None):
         out = (torch.full((ms,), -1, dtype=torch.int32, device=dev),
                torch.full((ms // 128,), -1, dtype=torch.int32, device=dev),
                torch.zeros(1, dtype=torch.int32, device=dev), torch.zeros(E + 1, dtype=torch.int32, device=dev),
-               torch.zeros(T * k, dtype=torch.int32, device=dev),
+               torch.full((T * k,), -1, dtype=torch.int32, device=dev),  # stays -1 for ids outside [0, E)
                torch.zeros(_lib.align_workspace_bytes(T, k, E) // 4, dtype=torch.int32, device=dev))
     sorted_ids, expert_ids, npp, off, slot_of, scratch = out
     _lib.call("pm_moe_align", _p(ids), T, k, E, _p(sorted_ids), _p(expert_ids), _p(npp), _p(off), _p(slot_of),

@@ -33,9 +33,9 @@ class OracleBackend:
         w, ids = O.route_topk(logits, self.k)
         return torch.from_numpy(w), torch.from_numpy(ids)
 
-    def quant_dispatch(self, x, send_pos, k):
+    def quant_dispatch(self, x, send_pos, k, rows):
         xq, xs = O.quant_fp8_groups(_bits(x))
-        n = x.shape[0] * k
+        n = rows
         q = np.zeros((n, H), np.uint8)
         s = np.zeros((n, H // 128), np.float32)
         sp = send_pos.numpy().reshape(-1, k)
