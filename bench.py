@@ -31,7 +31,10 @@ sys.path.insert(0, str(ROOT))
 METRIC = "MoE-layer tokens/s and % FP8/FP4 tensor peak at T=5120; HBM GB/s at T=128"
 H, I, E, K = 2048, 768, 128, 8
 T_CTX, T_BRANCH, T_CPU_SAMPLE = 5120, 128, 512
-KERNELS_PER_STEP = 9  # router GEMM, top-k, 3 alignment passes, activation quant, gate_up, down, combine
+KERNELS_PER_STEP = 8  # router GEMM, top-k, 2 alignment passes, activation quant, gate_up, down, combine
+# expert parallel over peer memory: router GEMM, top-k, 2 alignment passes, count, 3 barriers, offsets, dispatching
+# quant, slot map, gate_up, down, return, combine
+KERNELS_PER_EP_STEP = 16
 
 
 def profile_traffic(kernel: str):
@@ -244,11 +247,14 @@ def ep_stack(dev, rank: int, world: int, layers: int, tokens: int, steps: int):
     lo, hi = rank * epr, (rank + 1) * epr
     bias = synth.zipf_bias(E).to(dev)
     stack = []
+    # one peer exchange shared by all layers (a layer's exchange buffers are live only during its forward)
+    exchange = ep.PeerExchange(E, K, H, I, rank, world, tokens, dev) if world > 1 else None
     for li in range(layers):
         L = synth.make_fp8_layer(8, H, I, E, seed=li, device=dev, gen_device="cuda")
         b = ep.CudaBackend(L["w1"][lo:hi].contiguous(), L["w1_s"][lo:hi].contiguous(), L["w2"][lo:hi].contiguous(),
                            L["w2_s"][lo:hi].contiguous(), L["router_w"], K, bias=bias)
-        stack.append(ep.ExpertParallelLayer(b, E, K, rank, world))
+        stack.append(ep.PeerExpertParallelLayer(b, E, K, rank, world, exchange=exchange) if world > 1
+                     else ep.ExpertParallelLayer(b, E, K, rank, world))
         del L
     g = torch.Generator("cuda").manual_seed(1000 + rank)
     x = torch.randn(tokens, H, generator=g, device=dev).to(torch.bfloat16)
@@ -273,6 +279,8 @@ def ep_stack(dev, rank: int, world: int, layers: int, tokens: int, steps: int):
     _, _, ids = ops.router_topk(x, stack[0].b.router_w, K, bias=bias)
     load = torch.bincount(ids.reshape(-1).long(), minlength=E).float()
     del stack
+    if exchange is not None:
+        exchange.close()
     return ms, float(load.max() / load.sum())
 
 
@@ -289,17 +297,18 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
     x = layer["x"]
     stream = torch.cuda.current_stream()
     if world > 1:
-        # every rank owns E/world experts and its own T_CTX tokens (weak scaling); NCCL all-to-all dispatch/combine
+        # every rank owns E/world experts and its own T_CTX tokens (weak scaling); rows move between the ranks by
+        # the kernels' own NVLink peer stores (no host synchronisation, no collective library on the data path)
         from prismyra_b200 import ep
 
         gx = torch.Generator("cuda").manual_seed(1000 + rank)
         x = torch.randn(T_CTX, H, generator=gx, device=dev).to(torch.bfloat16)
         epr = E // world
         lo, hi = rank * epr, (rank + 1) * epr
-        ep_layer = ep.ExpertParallelLayer(
+        ep_layer = ep.PeerExpertParallelLayer(
             ep.CudaBackend(layer["w1"][lo:hi].contiguous(), layer["w1_s"][lo:hi].contiguous(),
                            layer["w2"][lo:hi].contiguous(), layer["w2_s"][lo:hi].contiguous(), layer["router_w"], K),
-            E, K, rank, world)
+            E, K, rank, world, max_tokens=T_CTX)
 
         def step():
             return ep_layer.forward(x)
@@ -391,6 +400,8 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
     nv_tflops = fl["total"] / (nv_ms * 1e-3) / 1e12
     fp4_peak = 4.0 * pk["bf16_tflops"]  # B200 FP4 dense rate is four times its BF16 dense rate
 
+    if world > 1:
+        ep_layer.close()  # every rank together: frees this layer's exchange before the stack makes its own
     stack_ms, stack_peak = ep_stack(dev, rank, world, args.stack_layers, 4096, max(2, args.steps // 20))
 
     if rank != 0:
@@ -405,7 +416,8 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
         "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
         "config": {"workload": f"FP8 block-scaled routed-expert layer, T={T_CTX} tokens per GPU (BASELINE configs[1])",
                    "tokens": T_CTX, "hidden": H, "intermediate": I, "experts": E, "top_k": K,
-                   "parallelism": f"expert parallel x{world} (NCCL all-to-all)" if world > 1 else "single GPU",
+                   "parallelism": f"expert parallel x{world} (NVLink peer stores from the kernels)" if world > 1
+                   else "single GPU",
                    "l2": "no flush: 604 MB of expert weights (> 126 MB L2) stream from HBM every step"},
         "tflops": layer_tflops,
         "frac_fp8_peak": layer_tflops / fp8_peak,
@@ -428,7 +440,7 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
                      "tokens_per_s": world * 4096 / (stack_ms * 1e-3), "zipf_peak_expert_share": stack_peak,
                      "config": "BASELINE configs[4]: FP8 layers, per-layer weights from seed = layer, Zipf(1.1) "
                                "expert bias, experts sharded over the ranks"},
-        "gpu_launches": KERNELS_PER_STEP * args.steps,
+        "gpu_launches": (KERNELS_PER_EP_STEP if world > 1 else KERNELS_PER_STEP) * args.steps,
         "clocks": clk.summary(),
     }
     if cb is not None:

@@ -198,6 +198,39 @@ int pm_moe_forward_nvfp4(const void *x, const void *router_w, const void *logits
 int pm_moe_align_noalloc(const int32_t *topk_ids, int T, int k, int E, int32_t *sorted_ids, int32_t *expert_ids,
                          int32_t *num_post_pad, int32_t *expert_off, pm_stream_t stream);
 
+/* ---- Expert parallelism over peer memory.  No counterpart in the reference, which runs the layer on one
+ * device: these move a layer's rows between the ranks of one node by direct NVLink loads and stores.
+ * pm_ep_alloc: device memory (zeroed) plus its 64-byte CUDA IPC handle for the other ranks; pm_ep_open maps a
+ * peer's handle into this process (pm_ep_close / pm_ep_free undo them).  The other calls take device arrays of G
+ * addresses (peer_*, one per rank, this rank's own included) and are stream-ordered, without host synchronisation.
+ *   pm_ep_count       store this rank's per-expert pair counts into row `rank` of every rank's count matrix [G][E]
+ *   pm_ep_barrier     add 1 to every rank's counter and wait (bounded; on timeout *err = 1) until the own counter
+ *                     reaches target
+ *   pm_ep_offsets     from the full count matrix: for each global expert, where this rank's pairs of it start in
+ *                     the owner's slot space (experts padded to 128 slots, sources in rank order), and the block
+ *                     table and slot count of this rank's own experts
+ *   pm_ep_dispatch_quant  per-token per-128 e4m3 quantisation (as pm_moe_quant_fp8) stored straight into the
+ *                     owners' slots, with each slot's (source rank << 24 | pair index) and routing weight; T*k < 2^24
+ *   pm_ep_local_sorted    slot -> slot for filled slots (cap_slots for padding): the down GEMM's row map
+ *   pm_ep_return      each filled slot's bf16 row [H] to its source rank's result row for its pair */
+int pm_ep_alloc(size_t bytes, void **ptr, void *ipc_handle);
+int pm_ep_open(const void *ipc_handle, void **ptr);
+int pm_ep_close(void *ptr);
+int pm_ep_free(void *ptr);
+int pm_ep_count(const int32_t *ids, int n, int E, int G, int rank, const uint64_t *peer_cm, pm_stream_t stream);
+int pm_ep_barrier(const uint64_t *peer_flag, unsigned *own_flag, int G, unsigned target, int32_t *err,
+                  pm_stream_t stream);
+int pm_ep_offsets(const int32_t *cm, int G, int E, int epr, int rank, int32_t *base, int32_t *expert_ids,
+                  int32_t *num_post_pad, int cap_slots, int32_t *err, pm_stream_t stream);
+int pm_ep_dispatch_quant(const void *x, int T, int H, int k, const int32_t *topk_ids, const float *topk_w,
+                         const int32_t *slot_local, const int32_t *expert_off_local, const int32_t *base, int E,
+                         int epr, int rank, int cap_slots, const uint64_t *peer_a1, const uint64_t *peer_a1_scale,
+                         const uint64_t *peer_meta, const uint64_t *peer_weight, int32_t *err, pm_stream_t stream);
+int pm_ep_local_sorted(const int32_t *meta, const int32_t *num_post_pad, int cap_slots, int32_t *sorted_ids,
+                       pm_stream_t stream);
+int pm_ep_return(const void *c3, const int32_t *meta, const int32_t *num_post_pad, int cap_slots, int H, int G,
+                 int n_pairs, const uint64_t *peer_back, int32_t *err, pm_stream_t stream);
+
 /* Synchronise the stream and report PM_ERR_TIMEOUT if any kernel of the last calls on this workspace gave up
  * on a bounded wait (the flag is cleared by each pm_moe_forward_* call). */
 int pm_moe_read_status(const void *workspace, pm_stream_t stream);

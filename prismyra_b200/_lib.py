@@ -54,6 +54,16 @@ SIGNATURES: dict[str, tuple] = {
     "pm_moe_gemm2_nvfp4": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
     "pm_moe_forward_nvfp4": (_I, [_P, _P, _P, _P, _P, _P, ctypes.c_float, _P, _P, _P, ctypes.c_float, _I, _I, _I,
                                   _I, _I, _P, _P, _Z, _P]),
+    "pm_ep_alloc": (_I, [_Z, ctypes.POINTER(_P), _P]),
+    "pm_ep_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "pm_ep_close": (_I, [_P]),
+    "pm_ep_free": (_I, [_P]),
+    "pm_ep_count": (_I, [_P, _I, _I, _I, _I, _P, _P]),
+    "pm_ep_barrier": (_I, [_P, _P, _I, ctypes.c_uint, _P, _P]),
+    "pm_ep_offsets": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _I, _P, _P]),
+    "pm_ep_dispatch_quant": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
+    "pm_ep_local_sorted": (_I, [_P, _P, _I, _P, _P]),
+    "pm_ep_return": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P]),
 }
 
 

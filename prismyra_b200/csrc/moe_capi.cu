@@ -553,6 +553,97 @@ int pm_moe_forward_nvfp4(const void* x, const void* router_w, const void* logits
     return cuda_status(launch_combine(R(PM_WS_C3), nullptr, T, k, H, out, s));
 }
 
+// ---------------------------------------------------------------------------------------- expert parallelism
+int pm_ep_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+    if (!ptr || !ipc_handle || bytes == 0) return PM_ERR_INVALID;
+    DeviceInfo d;
+    const int st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return PM_ERR_CUDA;
+    cudaIpcMemHandle_t h;
+    if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+        cudaFree(p);
+        return PM_ERR_CUDA;
+    }
+    memcpy(ipc_handle, &h, sizeof(h));
+    *ptr = p;
+    return PM_OK;
+}
+
+int pm_ep_open(const void* ipc_handle, void** ptr) {
+    if (!ptr || !ipc_handle) return PM_ERR_INVALID;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof(h));
+    return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? PM_OK : PM_ERR_CUDA;
+}
+
+int pm_ep_close(void* ptr) { return ptr && cudaIpcCloseMemHandle(ptr) == cudaSuccess ? PM_OK : PM_ERR_CUDA; }
+
+int pm_ep_free(void* ptr) { return ptr && cudaFree(ptr) == cudaSuccess ? PM_OK : PM_ERR_CUDA; }
+
+int pm_ep_count(const int32_t* ids, int n, int E, int G, int rank, const uint64_t* peer_cm, pm_stream_t stream) {
+    if (n < 0 || E <= 0 || E > kMaxExperts || G <= 0 || rank < 0 || rank >= G) return PM_ERR_INVALID;
+    if ((n > 0 && !ids) || !peer_cm) return PM_ERR_INVALID;
+    return cuda_status(launch_ep_count(ids, n, E, G, rank, peer_cm, (cudaStream_t)stream));
+}
+
+int pm_ep_barrier(const uint64_t* peer_flag, unsigned* own_flag, int G, unsigned target, int32_t* err,
+                  pm_stream_t stream) {
+    if (!peer_flag || !own_flag || G <= 0) return PM_ERR_INVALID;
+    return cuda_status(launch_ep_barrier(peer_flag, own_flag, G, target, err, (cudaStream_t)stream));
+}
+
+int pm_ep_offsets(const int32_t* cm, int G, int E, int epr, int rank, int32_t* base, int32_t* expert_ids,
+                  int32_t* num_post_pad, int cap_slots, int32_t* err, pm_stream_t stream) {
+    if (!cm || !base || !expert_ids || !num_post_pad || !err || G <= 0 || epr <= 0 || E != G * epr ||
+        E > kMaxExperts || rank < 0 || rank >= G || cap_slots % kBlockM != 0)
+        return PM_ERR_INVALID;
+    return cuda_status(launch_ep_offsets(cm, G, E, epr, rank, base, expert_ids, num_post_pad, cap_slots / kBlockM,
+                                         err, (cudaStream_t)stream));
+}
+
+int pm_ep_dispatch_quant(const void* x, int T, int H, int k, const int32_t* topk_ids, const float* topk_w,
+                         const int32_t* slot_local, const int32_t* expert_off_local, const int32_t* base, int E,
+                         int epr, int rank, int cap_slots, const uint64_t* peer_a1, const uint64_t* peer_a1_scale,
+                         const uint64_t* peer_meta, const uint64_t* peer_weight, int32_t* err, pm_stream_t stream) {
+    if (T < 0 || H <= 0 || H % 128 != 0 || k <= 0 || epr <= 0 || E <= 0 || rank < 0 || cap_slots <= 0)
+        return PM_ERR_INVALID;
+    if ((long)T * k >= (1L << 24) || rank >= 128) return PM_ERR_TOO_LARGE;
+    if (T == 0) return PM_OK;
+    if (!x || !topk_ids || !topk_w || !slot_local || !expert_off_local || !base || !peer_a1 || !peer_a1_scale ||
+        !peer_meta || !peer_weight || !err)
+        return PM_ERR_INVALID;
+    if (!a16(x)) return PM_ERR_ALIGN;
+    DeviceInfo d;
+    const int st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    return cuda_status(launch_ep_dispatch_quant(x, T, H, k, topk_ids, topk_w, slot_local, expert_off_local, base, E,
+                                                epr, rank, cap_slots, peer_a1, peer_a1_scale, peer_meta, peer_weight,
+                                                err, d.sms, (cudaStream_t)stream));
+}
+
+int pm_ep_local_sorted(const int32_t* meta, const int32_t* num_post_pad, int cap_slots, int32_t* sorted_ids,
+                       pm_stream_t stream) {
+    if (!meta || !num_post_pad || !sorted_ids || cap_slots <= 0) return PM_ERR_INVALID;
+    DeviceInfo d;
+    const int st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    return cuda_status(launch_ep_local_sorted(meta, num_post_pad, cap_slots, sorted_ids, d.sms, (cudaStream_t)stream));
+}
+
+int pm_ep_return(const void* c3, const int32_t* meta, const int32_t* num_post_pad, int cap_slots, int H, int G,
+                 int n_pairs, const uint64_t* peer_back, int32_t* err, pm_stream_t stream) {
+    if (!c3 || !meta || !num_post_pad || !peer_back || !err || cap_slots <= 0 || H <= 0 || H % 8 != 0 || G <= 0)
+        return PM_ERR_INVALID;
+    if (!a16(c3)) return PM_ERR_ALIGN;
+    DeviceInfo d;
+    const int st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    return cuda_status(launch_ep_return(c3, meta, num_post_pad, cap_slots, H, G, n_pairs, peer_back, err, d.sms,
+                                        (cudaStream_t)stream));
+}
+
 int pm_moe_read_status(const void* workspace, pm_stream_t stream) {
     if (!workspace) return PM_ERR_INVALID;
     int32_t flag = 0;

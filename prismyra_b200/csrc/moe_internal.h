@@ -140,4 +140,21 @@ inline bool encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner
     return encode_tmap_2d(map, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, inner, outer, row_bytes, box_inner, box_outer);
 }
 
+// Expert parallelism over peer memory (moe_ep.cu); peer_* are device arrays of G addresses (one per rank).
+cudaError_t launch_ep_count(const int32_t* ids, int n, int E, int G, int rank, const uint64_t* peer_cm,
+                            cudaStream_t s);
+cudaError_t launch_ep_barrier(const uint64_t* peer_flag, unsigned* own_flag, int G, unsigned target, int32_t* err,
+                              cudaStream_t s);
+cudaError_t launch_ep_offsets(const int32_t* cm, int G, int E, int epr, int rank, int32_t* base, int32_t* expert_ids,
+                              int32_t* npp, int cap_blocks, int32_t* err, cudaStream_t s);
+cudaError_t launch_ep_dispatch_quant(const void* x, int T, int H, int k, const int32_t* ids, const float* topk_w,
+                                     const int32_t* slot_local, const int32_t* off_local, const int32_t* base,
+                                     int E, int epr, int rank, int cap, const uint64_t* peer_a1,
+                                     const uint64_t* peer_a1s, const uint64_t* peer_meta, const uint64_t* peer_wgt,
+                                     int32_t* err, int sms, cudaStream_t s);
+cudaError_t launch_ep_local_sorted(const int32_t* meta, const int32_t* npp, int cap, int32_t* sorted, int sms,
+                                   cudaStream_t s);
+cudaError_t launch_ep_return(const void* c3, const int32_t* meta, const int32_t* npp, int cap, int H, int G,
+                             int n_pairs, const uint64_t* peer_back, int32_t* err, int sms, cudaStream_t s);
+
 }  // namespace pm

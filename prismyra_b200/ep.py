@@ -165,3 +165,176 @@ class ExpertParallelLayer:
         else:
             back = _a2a(torch.empty(ns, H, dtype=c3.dtype, device=x.device), c3, sc, rc, self.group)
         return self.b.combine(back, T, k, plan.send_pos)
+
+
+# ------------------------------------------------------------------------------------------- peer memory path
+class _DeviceMemory:
+    """A zero-copy view of raw device memory for torch (``__cuda_array_interface__``)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+
+def _view(ptr: int, nbytes: int, dev: torch.device) -> torch.Tensor:
+    return torch.as_tensor(_DeviceMemory(ptr, nbytes), device=dev)
+
+
+def _align256(n: int) -> int:
+    return (n + 255) // 256 * 256
+
+
+class PeerExchange:
+    """The peer-mapped region and local buffers of :class:`PeerExpertParallelLayer`, shareable by every layer of a
+    stack with the same shapes (one layer runs at a time on a stream).
+
+    Every rank allocates one region (count matrix, barrier counter, its experts' slot-ordered FP8 rows, scales,
+    per-slot source and weight, and the result rows of its own pairs) and maps every other rank's region through
+    CUDA IPC here (a host-side exchange of handles over ``group``), for up to ``max_tokens`` tokens per rank and
+    call.  ``close()`` releases the mappings (all ranks call it together)."""
+
+    def __init__(self, num_experts: int, top_k: int, hidden: int, intermediate: int, rank: int, world: int,
+                 max_tokens: int, device: torch.device, group=None):
+        from . import _lib
+
+        if num_experts % world:
+            raise ValueError(f"{num_experts} experts do not split over {world} ranks")
+        self.E, self.k, self.rank, self.world, self.group = num_experts, top_k, rank, world, group
+        self.epr = num_experts // world
+        self.max_tokens, self.H, self.I, self.dev = max_tokens, hidden, intermediate, device
+        G, E, k, H, I = world, num_experts, top_k, hidden, intermediate
+        self.cap = (G * max_tokens * k + self.epr * 127 + 127) // 128 * 128
+        cap = self.cap
+        sizes = [("cm", G * E * 4), ("flag", 256), ("a1", cap * H), ("a1s", cap * (H // 128) * 4),
+                 ("meta", cap * 4), ("wgt", cap * 4), ("back", max_tokens * k * H * 2)]
+        self.off, total = {}, 0
+        for name, n in sizes:
+            self.off[name] = total
+            total += _align256(n)
+        own = _lib.ctypes.c_void_p()
+        handle = (_lib.ctypes.c_ubyte * 64)()
+        _lib.call("pm_ep_alloc", total, _lib.ctypes.byref(own), _lib.ctypes.addressof(handle))
+        self._own = own.value
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        ptrs, self._opened = [], []
+        for d in range(world):
+            if d == rank:
+                ptrs.append(self._own)
+                continue
+            p = _lib.ctypes.c_void_p()
+            buf = (_lib.ctypes.c_ubyte * 64).from_buffer_copy(handles[d])
+            _lib.call("pm_ep_open", _lib.ctypes.addressof(buf), _lib.ctypes.byref(p))
+            ptrs.append(p.value)
+            self._opened.append(p.value)
+        mk = lambda name: torch.tensor([p + self.off[name] for p in ptrs], dtype=torch.int64, device=device)
+        self.peer = {name: mk(name) for name, _ in sizes}
+        region = _view(self._own, total, device)
+
+        def own_view(name, dtype, shape):
+            o, n = self.off[name], 1
+            for s_ in shape:
+                n *= s_
+            nb = n * torch.tensor([], dtype=dtype).element_size()
+            return region[o:o + nb].view(dtype).view(*shape)
+
+        self.cm = own_view("cm", torch.int32, (G, E))
+        self.flag = own_view("flag", torch.int32, (64,))
+        self.a1 = own_view("a1", torch.uint8, (cap, H))
+        self.a1s = own_view("a1s", torch.float32, (cap, H // 128))
+        self.meta = own_view("meta", torch.int32, (cap,))
+        self.wgt = own_view("wgt", torch.float32, (cap,))
+        self.back = own_view("back", torch.bfloat16, (max_tokens * k, H))
+        self.a2 = torch.empty(cap, I, dtype=torch.uint8, device=device)
+        self.a2s = torch.empty(cap, I // 128, dtype=torch.float32, device=device)
+        self.c3 = torch.empty(cap, H, dtype=torch.bfloat16, device=device)
+        self.sorted = torch.empty(cap, dtype=torch.int32, device=device)
+        self.base = torch.empty(E, dtype=torch.int32, device=device)
+        self.eids = torch.zeros(cap // 128, dtype=torch.int32, device=device)
+        self.npp = torch.zeros(1, dtype=torch.int32, device=device)
+        self.err = torch.zeros(4, dtype=torch.int32, device=device)
+        self.epoch = 0
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)  # every rank has mapped every region
+
+    def barrier(self, stream: int) -> None:
+        """Device barrier over the ranks (stream-ordered, bounded wait; on timeout the error word is set)."""
+        from . import _lib
+
+        self.epoch += 1
+        _lib.call("pm_ep_barrier", self.peer["flag"].data_ptr(), self.flag.data_ptr(), self.world,
+                  (self.epoch * self.world) & 0xFFFFFFFF, self.err.data_ptr(), stream)
+
+    def errors(self) -> int:
+        """Non-zero if any kernel gave up on a bounded wait or met an out-of-range slot (synchronises)."""
+        return int(self.err.sum().item())
+
+    def close(self) -> None:
+        from . import _lib
+
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)  # no rank still reads or writes a peer region
+        for p in self._opened:
+            _lib.call("pm_ep_close", p)
+        self._opened = []
+        if self._own:
+            _lib.call("pm_ep_free", self._own)
+            self._own = 0
+
+
+class PeerExpertParallelLayer:
+    """The expert-parallel layer with its exchanges done by the kernels themselves over NVLink peer memory
+    (``pm_ep_*`` in the C ABI): no host synchronisation and no collective library on the data path.
+
+    ``forward(x)`` for up to ``max_tokens`` tokens per rank: route; count pairs per expert into every rank's count
+    matrix; barrier; offsets; quantise and store each token's rows into the owners' slots; barrier; local gate_up /
+    down GEMMs; store each weighted row back to its source; barrier; fixed-order combine.  Bit-identical to the
+    single-GPU layer.  All ranks must call ``forward`` the same number of times (the barriers pair up by count).
+    Give ``exchange`` to share one :class:`PeerExchange` among the layers of a stack; otherwise the layer makes
+    its own, released by ``close()``."""
+
+    def __init__(self, backend: CudaBackend, num_experts: int, top_k: int, rank: int, world: int,
+                 max_tokens: int = 0, group=None, exchange: PeerExchange | None = None):
+        self.b, self.E, self.k, self.rank, self.world = backend, num_experts, top_k, rank, world
+        _, I2, H = backend.w1.shape
+        self._own_exchange = exchange is None
+        self.x = exchange or PeerExchange(num_experts, top_k, H, I2 // 2, rank, world, max_tokens,
+                                          backend.w1.device, group)
+        if (self.x.E, self.x.k, self.x.H, self.x.I, self.x.world) != (num_experts, top_k, H, I2 // 2, world):
+            raise ValueError("the exchange was made for another layer shape")
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        from . import _lib, ops
+
+        X = self.x
+        T, H = x.shape
+        if T > X.max_tokens or H != X.H:
+            raise ValueError(f"x [{T}, {H}] exceeds the exchange's buffers ([{X.max_tokens}, {X.H}])")
+        k, E, G = self.k, self.E, self.world
+        P = lambda t: t.data_ptr()
+        stream = torch.cuda.current_stream(X.dev).cuda_stream
+        w, ids = self.b.route(x)
+        _, _, _, off, slot_of, _ = ops.align(ids, E)  # own pairs by global expert: rank within the expert
+        X.meta.fill_(-1)
+        _lib.call("pm_ep_count", P(ids), T * k, E, G, self.rank, P(X.peer["cm"]), stream)
+        X.barrier(stream)
+        _lib.call("pm_ep_offsets", P(X.cm), G, E, X.epr, self.rank, P(X.base), P(X.eids), P(X.npp), X.cap,
+                  P(X.err), stream)
+        _lib.call("pm_ep_dispatch_quant", P(x), T, H, k, P(ids), P(w), P(slot_of), P(off), P(X.base), E, X.epr,
+                  self.rank, X.cap, P(X.peer["a1"]), P(X.peer["a1s"]), P(X.peer["meta"]), P(X.peer["wgt"]),
+                  P(X.err), stream)
+        X.barrier(stream)
+        _lib.call("pm_ep_local_sorted", P(X.meta), P(X.npp), X.cap, P(X.sorted), stream)
+        ops.gemm1_fp8(X.a1, X.a1s, self.b.w1, self.b.w1_s, X.eids, X.npp, out=(X.a2, X.a2s, X.err[1:2]))
+        ops.gemm2_fp8(X.a2, X.a2s, self.b.w2, self.b.w2_s, X.eids, X.npp, X.sorted, X.wgt, X.cap, 1,
+                      out=(X.c3, X.err[2:3]))
+        _lib.call("pm_ep_return", P(X.c3), P(X.meta), P(X.npp), X.cap, H, G, X.max_tokens * k, P(X.peer["back"]),
+                  P(X.err), stream)
+        X.barrier(stream)
+        return ops.combine(X.back[: T * k], T, k)
+
+    def errors(self) -> int:
+        return self.x.errors()
+
+    def close(self) -> None:
+        if self._own_exchange:
+            self.x.close()

@@ -89,3 +89,53 @@ def test_two_nccl_ranks_match_the_single_gpu_layer():
             p.join(300)
         assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
         assert dict(errors) == {}
+
+
+def _peer_rank(rank, world, port, errors):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    layer = None
+    try:
+        dev = torch.device("cuda", rank)
+        L = _layer(dev)
+        epr = E // world
+        lo, hi = rank * epr, (rank + 1) * epr
+        b = ep.CudaBackend(L["w1"][lo:hi].contiguous(), L["w1_s"][lo:hi].contiguous(), L["w2"][lo:hi].contiguous(),
+                           L["w2_s"][lo:hi].contiguous(), L["router_w"], K)
+        layer = ep.PeerExpertParallelLayer(b, E, K, rank, world, max_tokens=T)
+        for call, (seed, n) in enumerate(((100 + rank, T), (200 + rank, T - 37))):  # buffers reused, fewer tokens
+            g = torch.Generator("cuda").manual_seed(seed)
+            x = torch.randn(n, H, generator=g, device=dev).to(torch.bfloat16)
+            out = layer.forward(x)
+            ref = ops.forward_fp8(x, L["w1"], L["w1_s"], L["w2"], L["w2_s"], K, router_w=L["router_w"])
+            torch.cuda.synchronize()
+            if layer.errors():
+                errors[(rank, call)] = "kernel error flag"
+            elif not torch.equal(out, ref):
+                errors[(rank, call)] = float((out.float() - ref.float()).abs().max())
+    finally:
+        if layer is not None:
+            layer.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not cuda_ok() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_over_peer_memory_match_the_single_gpu_layer():
+    """The peer-memory expert-parallel layer (rows stored straight into the owners' slots and back over NVLink,
+    device barriers, no host synchronisation): bit-identical to one GPU, twice in a row on the same buffers."""
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        errors = mgr.dict()
+        procs = [ctx.Process(target=_peer_rank, args=(r, 2, port, errors)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(300)
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        assert dict(errors) == {}
