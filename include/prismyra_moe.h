@@ -211,8 +211,9 @@ int pm_moe_align_noalloc(const int32_t *topk_ids, int T, int k, int E, int32_t *
  *                     table and slot count of this rank's own experts
  *   pm_ep_dispatch_quant  per-token per-128 e4m3 quantisation (as pm_moe_quant_fp8) stored straight into the
  *                     owners' slots, with each slot's (source rank << 24 | pair index) and routing weight; T*k < 2^24
- *   pm_ep_local_sorted    slot -> slot for filled slots (cap_slots for padding): the down GEMM's row map
- *   pm_ep_return      each filled slot's bf16 row [H] to its source rank's result row for its pair */
+ *   pm_ep_local_rows  per slot, the address of its source rank's result row for its pair (0 for padding)
+ *   pm_ep_gemm2_fp8   the down GEMM of pm_moe_gemm2_fp8 over this rank's slots, each weighted bf16 row stored to
+ *                     dst_rows[slot] (another rank's memory over NVLink) instead of a local C3 */
 int pm_ep_alloc(size_t bytes, void **ptr, void *ipc_handle);
 int pm_ep_open(const void *ipc_handle, void **ptr);
 int pm_ep_close(void *ptr);
@@ -226,10 +227,11 @@ int pm_ep_dispatch_quant(const void *x, int T, int H, int k, const int32_t *topk
                          const int32_t *slot_local, const int32_t *expert_off_local, const int32_t *base, int E,
                          int epr, int rank, int cap_slots, const uint64_t *peer_a1, const uint64_t *peer_a1_scale,
                          const uint64_t *peer_meta, const uint64_t *peer_weight, int32_t *err, pm_stream_t stream);
-int pm_ep_local_sorted(const int32_t *meta, const int32_t *num_post_pad, int cap_slots, int32_t *sorted_ids,
-                       pm_stream_t stream);
-int pm_ep_return(const void *c3, const int32_t *meta, const int32_t *num_post_pad, int cap_slots, int H, int G,
-                 int n_pairs, const uint64_t *peer_back, int32_t *err, pm_stream_t stream);
+int pm_ep_local_rows(const int32_t *meta, const int32_t *num_post_pad, int cap_slots, int H, int G, int n_pairs,
+                     const uint64_t *peer_back, uint64_t *dst_rows, int32_t *err, pm_stream_t stream);
+int pm_ep_gemm2_fp8(const uint8_t *a_q, const float *a_s, const uint8_t *w2, const float *w2_s,
+                    const int32_t *expert_ids, const int32_t *num_post_pad, const float *weight,
+                    const uint64_t *dst_rows, int cap_slots, int H, int I, int E, int32_t *err, pm_stream_t stream);
 
 /* Synchronise the stream and report PM_ERR_TIMEOUT if any kernel of the last calls on this workspace gave up
  * on a bounded wait (the flag is cleared by each pm_moe_forward_* call). */

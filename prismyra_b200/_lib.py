@@ -62,8 +62,8 @@ SIGNATURES: dict[str, tuple] = {
     "pm_ep_barrier": (_I, [_P, _P, _I, ctypes.c_uint, _P, _P]),
     "pm_ep_offsets": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _I, _P, _P]),
     "pm_ep_dispatch_quant": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
-    "pm_ep_local_sorted": (_I, [_P, _P, _I, _P, _P]),
-    "pm_ep_return": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P]),
+    "pm_ep_local_rows": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "pm_ep_gemm2_fp8": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
 }
 
 

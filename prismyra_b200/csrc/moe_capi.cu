@@ -623,25 +623,38 @@ int pm_ep_dispatch_quant(const void* x, int T, int H, int k, const int32_t* topk
                                                 err, d.sms, (cudaStream_t)stream));
 }
 
-int pm_ep_local_sorted(const int32_t* meta, const int32_t* num_post_pad, int cap_slots, int32_t* sorted_ids,
-                       pm_stream_t stream) {
-    if (!meta || !num_post_pad || !sorted_ids || cap_slots <= 0) return PM_ERR_INVALID;
+int pm_ep_local_rows(const int32_t* meta, const int32_t* num_post_pad, int cap_slots, int H, int G, int n_pairs,
+                     const uint64_t* peer_back, uint64_t* dst_rows, int32_t* err, pm_stream_t stream) {
+    if (!meta || !num_post_pad || !peer_back || !dst_rows || !err || cap_slots <= 0 || H <= 0 || G <= 0)
+        return PM_ERR_INVALID;
     DeviceInfo d;
     const int st = current_device_info(&d);
     if (st != PM_OK) return st;
-    return cuda_status(launch_ep_local_sorted(meta, num_post_pad, cap_slots, sorted_ids, d.sms, (cudaStream_t)stream));
+    return cuda_status(launch_ep_local_rows(meta, num_post_pad, cap_slots, H, G, n_pairs, peer_back, dst_rows, err,
+                                            d.sms, (cudaStream_t)stream));
 }
 
-int pm_ep_return(const void* c3, const int32_t* meta, const int32_t* num_post_pad, int cap_slots, int H, int G,
-                 int n_pairs, const uint64_t* peer_back, int32_t* err, pm_stream_t stream) {
-    if (!c3 || !meta || !num_post_pad || !peer_back || !err || cap_slots <= 0 || H <= 0 || H % 8 != 0 || G <= 0)
-        return PM_ERR_INVALID;
-    if (!a16(c3)) return PM_ERR_ALIGN;
-    DeviceInfo d;
-    const int st = current_device_info(&d);
+int pm_ep_gemm2_fp8(const uint8_t* a_q, const float* a_s, const uint8_t* w2, const float* w2_s,
+                    const int32_t* expert_ids, const int32_t* num_post_pad, const float* weight,
+                    const uint64_t* dst_rows, int cap_slots, int H, int I, int E, int32_t* err, pm_stream_t stream) {
+    int st = check_dims(1, H, I, E, 1);
     if (st != PM_OK) return st;
-    return cuda_status(launch_ep_return(c3, meta, num_post_pad, cap_slots, H, G, n_pairs, peer_back, err, d.sms,
-                                        (cudaStream_t)stream));
+    if (cap_slots <= 0 || cap_slots % kBlockM != 0) return PM_ERR_SHAPE;
+    if (!a_q || !a_s || !w2 || !w2_s || !expert_ids || !num_post_pad || !weight || !dst_rows) return PM_ERR_INVALID;
+    if (!a16(a_q) || !a16(w2)) return PM_ERR_ALIGN;
+    DeviceInfo d;
+    st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    CUtensorMap ta, tb;
+    if (!encode_tmap_2d_u8(&ta, a_q, (uint64_t)I, (uint64_t)cap_slots, (uint64_t)I, 128, 128) ||
+        !encode_tmap_2d_u8(&tb, w2, (uint64_t)I, (uint64_t)E * H, (uint64_t)I, 128, 128))
+        return PM_ERR_CUDA;
+    GemmArgs g = gemm_args_common(a_s, w2_s, expert_ids, num_post_pad, H, I, H / 256, cap_slots, I, err);
+    g.sorted_ids = nullptr;  // the slot is the row: weight[slot], destination dst_rows[slot]
+    g.topk_w = weight;
+    g.dst_rows = dst_rows;
+    g.n_valid = cap_slots;
+    return cuda_status(launch_gemm_fp8(1, ta, tb, g, d.sms, (cudaStream_t)stream));
 }
 
 int pm_moe_read_status(const void* workspace, pm_stream_t stream) {

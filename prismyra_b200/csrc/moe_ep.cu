@@ -11,9 +11,10 @@
 //   3. dispatch: each token is quantised once (per-128 e4m3, IEEE division, as the single-GPU path) and its row is
 //      stored straight into the owner's slot of each of its k pairs, with (source rank, pair, routing weight);
 //      barrier.
-//   4. the owner runs its local gate_up / down GEMMs on its slots (the existing kernels) into a local C3;
-//   5. return: each slot's weighted bf16 row is stored into the source rank's result row for that pair; barrier;
-//      then the ordinary fixed-order combine.
+//   4. the owner runs its local gate_up / down GEMMs on its slots (the existing kernels); the down GEMM's
+//      epilogue stores each slot's weighted bf16 row straight into the source rank's result row for that pair
+//      (per-slot destination addresses), so the return overlaps the GEMM; barrier; then the ordinary fixed-order
+//      combine.
 // The rows, their arithmetic and the combine order are those of one GPU, so the result is bit-identical.
 //
 // Barrier: a one-thread kernel adds 1 to every rank's counter (system-scope atomics after a system fence) and
@@ -167,35 +168,22 @@ __global__ void __launch_bounds__(256) ep_dispatch_quant_kernel(
     }
 }
 
-// ---------------------------------------------------------------------------------------------- local prep
-// The local down GEMM writes C3 row = slot for real slots: sorted[slot] = slot, padding slots get cap (invalid).
-__global__ void ep_local_sorted_kernel(const int32_t* __restrict__ meta, const int32_t* __restrict__ npp, int cap,
-                                       int32_t* __restrict__ sorted) {
+// ---------------------------------------------------------------------------------------------- local rows
+// For each filled slot, the address of its source rank's result row for its pair (0 for padding): the local down
+// GEMM stores each weighted row there directly, over NVLink when the source is another rank.
+__global__ void ep_local_rows_kernel(const int32_t* __restrict__ meta, const int32_t* __restrict__ npp, int cap,
+                                     int H, int G, int n_pairs, const uint64_t* __restrict__ peer_back,
+                                     uint64_t* __restrict__ dst_rows, int32_t* err) {
     const int n = *npp;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < cap; i += gridDim.x * blockDim.x)
-        sorted[i] = (i < n && meta[i] >= 0) ? i : cap;
-}
-
-// ---------------------------------------------------------------------------------------------- return
-// One warp per slot: the bf16 row (H * 2 bytes) goes to the source rank's result row for its pair.
-__global__ void __launch_bounds__(256) ep_return_kernel(const __nv_bfloat16* __restrict__ c3,
-                                                        const int32_t* __restrict__ meta,
-                                                        const int32_t* __restrict__ npp, int H, int G, int n_pairs,
-                                                        const uint64_t* __restrict__ peer_back, int32_t* err) {
-    const int n = *npp;
-    const int lane = threadIdx.x & 31;
-    const long nwarps = ((long)gridDim.x * blockDim.x) >> 5;
-    for (long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < n; i += nwarps) {
-        const int m = meta[i];
-        if (m < 0) continue;
-        const int s = m >> 24, p = m & 0xFFFFFF;
-        if (s >= G || p >= n_pairs) {
-            if (lane == 0) atomicExch(err, 1);
-            continue;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < cap; i += gridDim.x * blockDim.x) {
+        uint64_t d = 0;
+        const int m = i < n ? meta[i] : -1;
+        if (m >= 0) {
+            const int s = m >> 24, p = m & 0xFFFFFF;
+            if (s < G && p < n_pairs) d = peer_back[s] + (uint64_t)p * H * sizeof(__nv_bfloat16);
+            else atomicExch(err, 1);
         }
-        const uint4* src = reinterpret_cast<const uint4*>(c3 + (size_t)i * H);
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peer_back[s]) + (size_t)p * H);
-        for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
+        dst_rows[i] = d;
     }
 }
 
@@ -240,16 +228,11 @@ cudaError_t launch_ep_dispatch_quant(const void* x, int T, int H, int k, const i
     return cudaGetLastError();
 }
 
-cudaError_t launch_ep_local_sorted(const int32_t* meta, const int32_t* npp, int cap, int32_t* sorted, int sms,
-                                   cudaStream_t s) {
-    ep_local_sorted_kernel<<<grid_for(cap, 256, sms), 256, 0, s>>>(meta, npp, cap, sorted);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_ep_return(const void* c3, const int32_t* meta, const int32_t* npp, int cap, int H, int G,
-                             int n_pairs, const uint64_t* peer_back, int32_t* err, int sms, cudaStream_t s) {
-    ep_return_kernel<<<grid_for(cap, 8, sms * 2), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(c3), meta, npp, H,
-                                                               G, n_pairs, peer_back, err);
+cudaError_t launch_ep_local_rows(const int32_t* meta, const int32_t* npp, int cap, int H, int G, int n_pairs,
+                                 const uint64_t* peer_back, uint64_t* dst_rows, int32_t* err, int sms,
+                                 cudaStream_t s) {
+    ep_local_rows_kernel<<<grid_for(cap, 256, sms), 256, 0, s>>>(meta, npp, cap, H, G, n_pairs, peer_back, dst_rows,
+                                                                  err);
     return cudaGetLastError();
 }
 

@@ -245,7 +245,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             // the two block-scale rows this thread multiplies by (gate/up halves, or its column half)
             const float* bs0 = bs + (size_t)(MODE == 0 ? nt : nt * 2 + half) * KB;
             const float* bs1 = bs + (size_t)(MODE == 0 ? args.inter / 128 + nt : nt * 2 + half) * KB;
-            const int flat = MODE == 1 ? args.sorted_ids[grow] : 0;
+            // down: the row's flat index (the slot itself when there is no row map) and, with a destination table,
+            // the address its weighted row is stored to (0: the slot holds no row)
+            const int flat = MODE == 1 ? (args.sorted_ids != nullptr ? args.sorted_ids[grow] : grow) : 0;
+            const uint64_t drow = (MODE == 1 && args.dst_rows != nullptr) ? args.dst_rows[grow] : 0;
             float w = 0.0f;
 #pragma unroll
             for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
@@ -350,9 +353,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int sub = lane >> 4, chunk = lane & 15;
                 for (int r = 0; r < 32; r += 2) {
                     const int f = __shfl_sync(0xffffffffu, flat, r + sub);
-                    if (f < args.n_valid) {
+                    const uint64_t dr = __shfl_sync(0xffffffffu, drow, r + sub);
+                    if (f < args.n_valid && (args.dst_rows == nullptr || dr != 0)) {
                         const uint4 v = *reinterpret_cast<const uint4*>(wst + (r + sub) * RB + chunk * 16);
-                        *reinterpret_cast<uint4*>(args.c3 + (size_t)f * H + nt * kBN + 128 * half + chunk * 8) = v;
+                        __nv_bfloat16* row = args.dst_rows != nullptr ? reinterpret_cast<__nv_bfloat16*>(dr)
+                                                                      : args.c3 + (size_t)f * H;
+                        *reinterpret_cast<uint4*>(row + nt * kBN + 128 * half + chunk * 8) = v;
                     }
                 }
                 __syncwarp();

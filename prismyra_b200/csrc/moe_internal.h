@@ -68,9 +68,11 @@ struct GemmArgs {
     uint8_t* out_q;           // [rows, I] e4m3
     float* out_s;             // [rows, I/128]
     // down epilogue
-    const int32_t* sorted_ids;   // [rows] flat index per row (n_valid = padding)
+    const int32_t* sorted_ids;   // [rows] flat index per row (n_valid = padding); nullptr: the row index itself
     const float* topk_w;      // [n_valid]
     __nv_bfloat16* c3;        // [n_valid, H]
+    const uint64_t* dst_rows; // [rows] or nullptr: the address each row's [H] bf16 result is stored to (0: none),
+                              // instead of c3 -- e.g. another GPU's memory over NVLink
     int n_valid;
     int* err;                 // set to 1 when a wait timed out
 };
@@ -152,9 +154,8 @@ cudaError_t launch_ep_dispatch_quant(const void* x, int T, int H, int k, const i
                                      int E, int epr, int rank, int cap, const uint64_t* peer_a1,
                                      const uint64_t* peer_a1s, const uint64_t* peer_meta, const uint64_t* peer_wgt,
                                      int32_t* err, int sms, cudaStream_t s);
-cudaError_t launch_ep_local_sorted(const int32_t* meta, const int32_t* npp, int cap, int32_t* sorted, int sms,
-                                   cudaStream_t s);
-cudaError_t launch_ep_return(const void* c3, const int32_t* meta, const int32_t* npp, int cap, int H, int G,
-                             int n_pairs, const uint64_t* peer_back, int32_t* err, int sms, cudaStream_t s);
+cudaError_t launch_ep_local_rows(const int32_t* meta, const int32_t* npp, int cap, int H, int G, int n_pairs,
+                                 const uint64_t* peer_back, uint64_t* dst_rows, int32_t* err, int sms,
+                                 cudaStream_t s);
 
 }  // namespace pm

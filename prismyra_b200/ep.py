@@ -246,8 +246,7 @@ class PeerExchange:
         self.back = own_view("back", torch.bfloat16, (max_tokens * k, H))
         self.a2 = torch.empty(cap, I, dtype=torch.uint8, device=device)
         self.a2s = torch.empty(cap, I // 128, dtype=torch.float32, device=device)
-        self.c3 = torch.empty(cap, H, dtype=torch.bfloat16, device=device)
-        self.sorted = torch.empty(cap, dtype=torch.int32, device=device)
+        self.dst_rows = torch.zeros(cap, dtype=torch.int64, device=device)  # per slot: its source's result row
         self.base = torch.empty(E, dtype=torch.int32, device=device)
         self.eids = torch.zeros(cap // 128, dtype=torch.int32, device=device)
         self.npp = torch.zeros(1, dtype=torch.int32, device=device)
@@ -286,8 +285,9 @@ class PeerExpertParallelLayer:
     (``pm_ep_*`` in the C ABI): no host synchronisation and no collective library on the data path.
 
     ``forward(x)`` for up to ``max_tokens`` tokens per rank: route; count pairs per expert into every rank's count
-    matrix; barrier; offsets; quantise and store each token's rows into the owners' slots; barrier; local gate_up /
-    down GEMMs; store each weighted row back to its source; barrier; fixed-order combine.  Bit-identical to the
+    matrix; barrier; offsets; quantise and store each token's rows into the owners' slots; barrier; local gate_up
+    GEMM; down GEMM whose epilogue stores each weighted row straight into its source rank's result row; barrier;
+    fixed-order combine.  Bit-identical to the
     single-GPU layer.  All ranks must call ``forward`` the same number of times (the barriers pair up by count).
     Give ``exchange`` to share one :class:`PeerExchange` among the layers of a stack; otherwise the layer makes
     its own, released by ``close()``."""
@@ -323,12 +323,13 @@ class PeerExpertParallelLayer:
                   self.rank, X.cap, P(X.peer["a1"]), P(X.peer["a1s"]), P(X.peer["meta"]), P(X.peer["wgt"]),
                   P(X.err), stream)
         X.barrier(stream)
-        _lib.call("pm_ep_local_sorted", P(X.meta), P(X.npp), X.cap, P(X.sorted), stream)
+        _lib.call("pm_ep_local_rows", P(X.meta), P(X.npp), X.cap, H, G, X.max_tokens * k, P(X.peer["back"]),
+                  P(X.dst_rows), P(X.err), stream)
         ops.gemm1_fp8(X.a1, X.a1s, self.b.w1, self.b.w1_s, X.eids, X.npp, out=(X.a2, X.a2s, X.err[1:2]))
-        ops.gemm2_fp8(X.a2, X.a2s, self.b.w2, self.b.w2_s, X.eids, X.npp, X.sorted, X.wgt, X.cap, 1,
-                      out=(X.c3, X.err[2:3]))
-        _lib.call("pm_ep_return", P(X.c3), P(X.meta), P(X.npp), X.cap, H, G, X.max_tokens * k, P(X.peer["back"]),
-                  P(X.err), stream)
+        # the down GEMM stores each weighted row straight into its source rank's result row
+        w2 = self.b.w2
+        _lib.call("pm_ep_gemm2_fp8", P(X.a2), P(X.a2s), P(ops._u8(w2)), P(self.b.w2_s), P(X.eids), P(X.npp),
+                  P(X.wgt), P(X.dst_rows), X.cap, H, X.I, w2.shape[0], P(X.err[2:3]), stream)
         X.barrier(stream)
         return ops.combine(X.back[: T * k], T, k)
 
