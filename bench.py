@@ -400,6 +400,44 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
     nv_tflops = fl["total"] / (nv_ms * 1e-3) / 1e12
     fp4_peak = 4.0 * pk["bf16_tflops"]  # B200 FP4 dense rate is four times its BF16 dense rate
 
+    # NVFP4 weight preparation on the GPU (pm_nvfp4_prepare over both expert stacks of the layer):
+    # algorithmic bytes = e4m3 read once + packed codes and e4m3 scales written (1 + 1/2 + 1/16 bytes per weight)
+    def prep_step():
+        ops.nvfp4_prepare(layer["w1"], layer["w1_s"])
+        ops.nvfp4_prepare(layer["w2"], layer["w2_s"])
+
+    prep_step()
+    prep_ms = time_region(prep_step, 5, stream)
+    n_weights = layer["w1"].numel() + layer["w2"].numel()
+    prep_bytes = n_weights * (1.0 + 0.5 + 1.0 / 16.0)
+    prep = {"ms": prep_ms, "gbs": prep_bytes / (prep_ms * 1e-3) / 1e9,
+            "frac_hbm": prep_bytes / (prep_ms * 1e-3) / 1e9 / pk["hbm_gbs"], "weights": n_weights,
+            "algorithmic_bytes": prep_bytes,
+            "note": "three launches per stack: a zeroing, the per-matrix maxima (reads the weights), the quantisation "
+                    "(reads them again), so DRAM traffic is about 2.56 bytes per weight"}
+
+    # the whole block (routed + shared expert + bf16 sum) in one library call; synthetic block-FP8 shared expert
+    # with the transformers Qwen3.5-MoE default shared_expert_intermediate_size of 512
+    block = None
+    if world == 1:
+        gs = torch.Generator("cuda").manual_seed(77)
+        IS = 512
+        sw13, sw13_s = synth.quantize_fp8_blocks(torch.randn(2 * IS, H, generator=gs, device=dev) * 0.02)
+        sw2, sw2_s = synth.quantize_fp8_blocks(torch.randn(H, IS, generator=gs, device=dev) * 0.02)
+        w_sg = (torch.randn(H, generator=gs, device=dev) * 0.02).to(torch.bfloat16)
+
+        def block_step():
+            return ops.block_fp8(x, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K, w_sg, sw13, sw13_s,
+                                 sw2, sw2_s, router_w=layer["router_w"])
+
+        for _ in range(5):
+            block_step()
+        blk_ms = time_region(block_step, max(20, args.steps), stream)
+        shared_flops = T_CTX * 2 * 3 * H * IS
+        block = {"ms": blk_ms, "tokens_per_s": T_CTX / (blk_ms * 1e-3), "shared_intermediate": IS,
+                 "shared_ms_over_routed": blk_ms - ms,
+                 "tflops": (fl["total"] + shared_flops) / (blk_ms * 1e-3) / 1e12}
+
     if world > 1:
         ep_layer.close()  # every rank together: frees this layer's exchange before the stack makes its own
     stack_ms, stack_peak = ep_stack(dev, rank, world, args.stack_layers, 4096, max(2, args.steps // 20))
@@ -443,6 +481,9 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
         "gpu_launches": (KERNELS_PER_EP_STEP if world > 1 else KERNELS_PER_STEP) * args.steps,
         "clocks": clk.summary(),
     }
+    line["nvfp4_prepare"] = prep
+    if block is not None:
+        line["block_t5120"] = block
     if cb is not None:
         line["cpu_baseline"] = cb
     print(json.dumps(line), flush=True)

@@ -149,6 +149,27 @@ int pm_moe_forward_fp8(const void *x, const void *router_w, const void *logits, 
                        const float *w1_s, const uint8_t *w2, const float *w2_s, int T, int H, int I, int E, int k,
                        void *out, void *workspace, size_t workspace_bytes, pm_stream_t stream);
 
+/* The shared expert, `torch.sigmoid(self._gate(x)) * self.shared_expert(x)` (prismyra/kernels/qwen3_moe.py:198):
+ * gate = bf16(sigmoid(bf16(x . w_sg))) (w_sg bf16 [H], the shared_expert_gate weight, qwen3_moe.py:172-183), and
+ * the MLP down(bf16(silu(gate_proj x)) * up_proj x) on 128x128 block-FP8 weights with the reference's Fp8Linear
+ * arithmetic (per_token_group_quant_fp8 + w8a8 block-scaled matmul, qwen3_moe.py:211-230): w13 e4m3 [2*Is, H]
+ * (gate_proj rows, then up_proj rows), w13_s f32 [2*Is/128, H/128], w2 e4m3 [H, Is], w2_s f32 [H/128, Is/128].
+ * The MLP output is rounded to bf16 before the bf16 product with the gate.  out bf16 [T, H].  H % 256 == 0,
+ * Is % 128 == 0.  Every row is computed in a fixed order (row-count invariant, deterministic). */
+size_t pm_moe_shared_workspace_bytes(int T, int H, int Is);
+int pm_moe_shared_fp8(const void *x, const void *w_sg, const uint8_t *w13, const float *w13_s, const uint8_t *w2,
+                      const float *w2_s, int T, int H, int Is, void *out, void *workspace, size_t workspace_bytes,
+                      pm_stream_t stream);
+
+/* The whole FusedExperts.forward (prismyra/kernels/qwen3_moe.py:184-199): routed experts as pm_moe_forward_fp8
+ * plus the shared expert as pm_moe_shared_fp8, summed as two bf16 tensors (`routed + shared`, :199: the routed
+ * top-k sum is rounded to bf16 first).  Status word at the start of the workspace, as for pm_moe_forward_fp8. */
+size_t pm_moe_block_workspace_bytes(int T, int H, int I, int Is, int E, int k);
+int pm_moe_block_fp8(const void *x, const void *router_w, const void *logits, const uint8_t *w1, const float *w1_s,
+                     const uint8_t *w2, const float *w2_s, const void *w_sg, const uint8_t *sw13,
+                     const float *sw13_s, const uint8_t *sw2, const float *sw2_s, int T, int H, int I, int Is, int E,
+                     int k, void *out, void *workspace, size_t workspace_bytes, pm_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------------------------------
  * NVFP4 (e2m1 values, one e4m3 scale per 16 elements, one fp32 global scale per tensor): the routed path of
  * prismyra/kernels/nvfp4.py:112-312 (FusedExpertsFp4, which calls FlashInfer's cutlass_fused_moe).
@@ -186,6 +207,15 @@ int pm_moe_forward_nvfp4(const void *x, const void *router_w, const void *logits
                          const uint8_t *w1_sf, const float *alpha1, float a1_gs, const uint8_t *w2,
                          const uint8_t *w2_sf, const float *alpha2, float a2_gs, int T, int H, int I, int E, int k,
                          void *out, void *workspace, size_t workspace_bytes, pm_stream_t stream);
+
+/* NVFP4 weight preparation on the GPU: prismyra/kernels/nvfp4.py:315-331 (prepare_layer without the optional
+ * importance search) for a stack of E expert matrices of R x C, bit for bit.  w: e4m3 [E, R, C] with fp32 block
+ * multipliers s [E, R/128, C/128] (the checkpoint's *_scale_inv, restored as in _dequant_fp8, nvfp4.py:97-100).
+ * Outputs: packed e2m1 [E, R, C/2] (even column in the low nibble), row-major e4m3 scales [E, R, C/16] and the
+ * global scales g [E] = reciprocal(max(amax, 1e-12)) * 2688 (nvfp4.py:321, which torch evaluates that way), with
+ * quantize's arithmetic (nvfp4.py:41-51).  R % 128 == 0, C % 128 == 0; w 16-byte and packed 8-byte aligned. */
+int pm_nvfp4_prepare(const uint8_t *w, const float *s, int E, int R, int C, uint8_t *packed, uint8_t *scales,
+                     float *g, pm_stream_t stream);
 
 /* Expert alignment that allocates nothing -- no counterpart in the reference.  Same results as pm_moe_align,
  * for callers that cannot hand the library scratch memory on demand: hosts that route every device byte through

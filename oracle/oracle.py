@@ -193,6 +193,36 @@ def moe_forward_fp8(x_bits, logits_bits, w1, w1_s, w2, w2_s, k: int, want_interm
     return r
 
 
+def shared_gate(x_bits, w_sg_bits) -> np.ndarray:
+    """bf16(sigmoid(bf16(x . w_sg))) per token as fp32 (reference qwen3_moe.py:172-183 and :198): the dot is
+    exact in float64 before its bf16 rounding; the sigmoid is evaluated in float64 and rounded to fp32, then
+    bf16."""
+    x = bf16_to_f32(_c(x_bits, np.uint16)).astype(np.float64)
+    w = bf16_to_f32(_c(w_sg_bits, np.uint16).reshape(-1)).astype(np.float64)
+    logit = bf16_to_f32(f32_to_bf16((x @ w).astype(np.float32))).astype(np.float64)
+    sig = (1.0 / (1.0 + np.exp(-logit))).astype(np.float32)
+    return bf16_to_f32(f32_to_bf16(sig))
+
+
+def shared_expert_fp8(x_bits, w_sg_bits, w13, w13_s, w2, w2_s) -> np.ndarray:
+    """The shared expert sigmoid(gate) * MLP(x) as bf16 bits [T, H] (reference qwen3_moe.py:198 with Fp8Linear
+    projections, :211-230): the MLP is the routed restatement with one expert and top-1 (weight exactly 1), so it
+    shares its quantisation, block-scaled GEMM and two-rounding silu*mul; the bf16 MLP output is then multiplied
+    by the bf16 gate and rounded."""
+    x = _c(x_bits, np.uint16)
+    T = x.shape[0]
+    one = np.zeros((T, 1), np.uint16)
+    mlp = moe_forward_fp8(x, one, _c(w13, np.uint8)[None], _c(w13_s, np.float32)[None], _c(w2, np.uint8)[None],
+                          _c(w2_s, np.float32)[None], 1)["out"]
+    g = shared_gate(x, w_sg_bits)
+    return f32_to_bf16(g[:, None] * bf16_to_f32(mlp))
+
+
+def add_bf16(a_bits, b_bits) -> np.ndarray:
+    """bf16(a + b) of two bf16 tensors (`routed + shared`, reference qwen3_moe.py:199)."""
+    return f32_to_bf16(bf16_to_f32(_c(a_bits, np.uint16)) + bf16_to_f32(_c(b_bits, np.uint16)))
+
+
 def nvfp4_quant_act(x_bits, gs: float):
     x = _c(x_bits, np.uint16)
     R, C = x.shape
@@ -209,6 +239,18 @@ def nvfp4_quant_weight(w, g: float):
     sf = np.empty((R, C // 16), np.uint8)
     lib().or_nvfp4_quant_weight(_p(w), R, C, ctypes.c_float(g), _p(packed), _p(sf))
     return packed, sf
+
+
+def nvfp4_prepare(w_bits, s):
+    """FP8 stack e4m3 bytes [E, R, C] + fp32 multipliers [E, R/128, C/128] -> (packed, sf, g) as prepare_layer."""
+    w = _c(w_bits, np.uint8)
+    s = _c(s, np.float32)
+    E, R, C = w.shape
+    packed = np.empty((E, R, C // 2), np.uint8)
+    sf = np.empty((E, R, C // 16), np.uint8)
+    g = np.empty(E, np.float32)
+    lib().or_nvfp4_prepare(_p(w), _p(s), E, R, C, _p(packed), _p(sf), _p(g))
+    return packed, sf, g
 
 
 def moe_forward_nvfp4(x_bits, logits_bits, w1, s1, w2, s2, alpha1, alpha2, a1_gs: float, a2_gs: float, k: int,

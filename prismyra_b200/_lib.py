@@ -54,6 +54,12 @@ SIGNATURES: dict[str, tuple] = {
     "pm_moe_gemm2_nvfp4": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
     "pm_moe_forward_nvfp4": (_I, [_P, _P, _P, _P, _P, _P, ctypes.c_float, _P, _P, _P, ctypes.c_float, _I, _I, _I,
                                   _I, _I, _P, _P, _Z, _P]),
+    "pm_nvfp4_prepare": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P]),
+    "pm_moe_shared_workspace_bytes": (_Z, [_I, _I, _I]),
+    "pm_moe_shared_fp8": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _P, _Z, _P]),
+    "pm_moe_block_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I]),
+    "pm_moe_block_fp8": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _Z,
+                              _P]),
     "pm_ep_alloc": (_I, [_Z, ctypes.POINTER(_P), _P]),
     "pm_ep_open": (_I, [_P, ctypes.POINTER(_P)]),
     "pm_ep_close": (_I, [_P]),

@@ -354,9 +354,11 @@ int pm_moe_combine(const void* c3, const int32_t* row_of, int T, int k, int H, v
     return cuda_status(launch_combine(c3, row_of, T, k, H, out, (cudaStream_t)stream));
 }
 
-int pm_moe_forward_fp8(const void* x, const void* router_w, const void* logits, const uint8_t* w1,
-                       const float* w1_s, const uint8_t* w2, const float* w2_s, int T, int H, int I, int E, int k,
-                       void* out, void* workspace, size_t workspace_bytes, pm_stream_t stream) {
+// The routed layer; with add, the final sum adds add[t] (after waiting on add_ready when given).
+static int forward_fp8_impl(const void* x, const void* router_w, const void* logits, const uint8_t* w1,
+                            const float* w1_s, const uint8_t* w2, const float* w2_s, int T, int H, int I, int E,
+                            int k, const void* add, cudaEvent_t add_ready, void* out, void* workspace,
+                            size_t workspace_bytes, pm_stream_t stream, bool clear_status) {
     int st = check_dims(T, H, I, E, k);
     if (st != PM_OK) return st;
     if (T == 0) return PM_OK;
@@ -384,7 +386,7 @@ int pm_moe_forward_fp8(const void* x, const void* router_w, const void* logits, 
     float* a2s = reinterpret_cast<float*>(R(PM_WS_A2_SCALE));
     void* c3 = R(PM_WS_C3);
 
-    if (cudaMemsetAsync(status, 0, L.len[PM_WS_STATUS], s) != cudaSuccess) return PM_ERR_CUDA;
+    if (clear_status && cudaMemsetAsync(status, 0, L.len[PM_WS_STATUS], s) != cudaSuccess) return PM_ERR_CUDA;
     cudaError_t e;
     if (logits != nullptr)
         e = launch_topk(logits, nullptr, T, E, k, topk_w, topk_ids, s);
@@ -407,7 +409,168 @@ int pm_moe_forward_fp8(const void* x, const void* router_w, const void* logits, 
     st = pm_moe_gemm2_fp8(a2, a2s, w2, w2_s, expert_ids, npp, sorted, topk_w, L.max_slots, T, k, H, I, E, c3,
                           status, stream);
     if (st != PM_OK) return st;
-    return cuda_status(launch_combine(c3, nullptr, T, k, H, out, s));
+    if (add_ready != nullptr && cudaStreamWaitEvent(s, add_ready, 0) != cudaSuccess) return PM_ERR_CUDA;
+    return cuda_status(launch_combine(c3, nullptr, T, k, H, out, s, add));
+}
+
+int pm_moe_forward_fp8(const void* x, const void* router_w, const void* logits, const uint8_t* w1,
+                       const float* w1_s, const uint8_t* w2, const float* w2_s, int T, int H, int I, int E, int k,
+                       void* out, void* workspace, size_t workspace_bytes, pm_stream_t stream) {
+    return forward_fp8_impl(x, router_w, logits, w1, w1_s, w2, w2_s, T, H, I, E, k, nullptr, nullptr, out,
+                            workspace, workspace_bytes, stream, true);
+}
+
+// ------------------------------------------------------------------------------------------- shared expert
+// Scratch of the shared expert: status word, gate [T], the one-expert plan, the quantised input rows, the
+// quantised silu*mul rows, and (for the whole block) the shared output before it is added to the routed sum.
+struct SharedLayout {
+    size_t status, gate, expert_ids, npp, xq, xs, a2, a2s, out, total;
+    int rows;  // T rounded up to the 128-row blocks
+};
+
+// One non-blocking side stream and a fork/join event pair per (thread, device), created on first use and kept
+// for the life of the thread (make the first call before any stream capture begins).
+struct SideStream {
+    cudaStream_t stream = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+static SideStream* side_stream() {
+    thread_local SideStream per_device[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    SideStream& ss = per_device[dev];
+    if (ss.stream == nullptr) {
+        if (cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+        if (cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming) != cudaSuccess)
+            return nullptr;
+    }
+    return &ss;
+}
+
+static SharedLayout shared_layout_of(int T, int H, int Is, bool with_out) {
+    SharedLayout L;
+    const int rows = (T + kBlockM - 1) / kBlockM * kBlockM;
+    size_t o = 0;
+    auto take = [&](size_t bytes) { const size_t at = o; o = align256(o + bytes); return at; };
+    L.status = take(4 * sizeof(int32_t));
+    L.gate = take((size_t)T * 4);
+    L.expert_ids = take((size_t)(rows / kBlockM) * 4);
+    L.npp = take(4);
+    L.xq = take((size_t)rows * H);
+    L.xs = take((size_t)rows * (H / 128) * 4);
+    L.a2 = take((size_t)rows * Is);
+    L.a2s = take((size_t)rows * (Is / 128) * 4);
+    L.out = with_out ? take((size_t)T * H * 2) : 0;
+    L.total = o;
+    L.rows = rows;
+    return L;
+}
+
+static int check_shared_dims(int T, int H, int Is) {
+    if (T < 0 || H <= 0 || Is <= 0) return PM_ERR_INVALID;
+    if (H % 256 != 0 || Is % 128 != 0 || (long)T * H > (1L << 34)) return PM_ERR_SHAPE;
+    return PM_OK;
+}
+
+// sigmoid(gate(x)) * MLP(x) into out [T, H] bf16, scratch at ws (layout L), timeouts reported to err.
+static int shared_fp8_run(const void* x, const void* w_sg, const uint8_t* w13, const float* w13_s,
+                          const uint8_t* w2, const float* w2_s, int T, int H, int Is, void* out,
+                          const SharedLayout& L, uint8_t* ws, int32_t* err, const DeviceInfo& d, cudaStream_t s) {
+    float* gate = reinterpret_cast<float*>(ws + L.gate);
+    int32_t* expert_ids = reinterpret_cast<int32_t*>(ws + L.expert_ids);
+    int32_t* npp = reinterpret_cast<int32_t*>(ws + L.npp);
+    uint8_t* xq = ws + L.xq;
+    float* xs = reinterpret_cast<float*>(ws + L.xs);
+    uint8_t* a2 = ws + L.a2;
+    float* a2s = reinterpret_cast<float*>(ws + L.a2s);
+    if (launch_shared_gate(x, w_sg, T, H, gate, expert_ids, npp, d.sms, s) != cudaSuccess) return PM_ERR_CUDA;
+    if (launch_quant_fp8(x, T, H, 1, nullptr, xq, xs, s) != cudaSuccess) return PM_ERR_CUDA;
+    CUtensorMap ta, tb;
+    if (!encode_tmap_2d_u8(&ta, xq, (uint64_t)H, (uint64_t)L.rows, (uint64_t)H, 128, 128) ||
+        !encode_tmap_2d_u8(&tb, w13, (uint64_t)H, (uint64_t)2 * Is, (uint64_t)H, 128, 128))
+        return PM_ERR_CUDA;
+    GemmArgs g1 = gemm_args_common(xs, w13_s, expert_ids, npp, 2 * Is, H, Is / 128, L.rows, Is, err);
+    g1.out_q = a2;
+    g1.out_s = a2s;
+    if (launch_gemm_fp8(0, ta, tb, g1, d.sms, s) != cudaSuccess) return PM_ERR_CUDA;
+    if (!encode_tmap_2d_u8(&ta, a2, (uint64_t)Is, (uint64_t)L.rows, (uint64_t)Is, 128, 128) ||
+        !encode_tmap_2d_u8(&tb, w2, (uint64_t)Is, (uint64_t)H, (uint64_t)Is, 128, 128))
+        return PM_ERR_CUDA;
+    GemmArgs g2 = gemm_args_common(a2s, w2_s, expert_ids, npp, H, Is, H / 256, L.rows, Is, err);
+    g2.sorted_ids = nullptr;  // row t of the block is token t
+    g2.topk_w = gate;
+    g2.c3 = static_cast<__nv_bfloat16*>(out);
+    g2.n_valid = T;
+    g2.round_first = 1;  // MLP output rounded to bf16, then the bf16 product with the bf16 gate
+    return cuda_status(launch_gemm_fp8(1, ta, tb, g2, d.sms, s));
+}
+
+size_t pm_moe_shared_workspace_bytes(int T, int H, int Is) {
+    if (check_shared_dims(T, H, Is) != PM_OK) return 0;
+    return shared_layout_of(T, H, Is, false).total;
+}
+
+int pm_moe_shared_fp8(const void* x, const void* w_sg, const uint8_t* w13, const float* w13_s, const uint8_t* w2,
+                      const float* w2_s, int T, int H, int Is, void* out, void* workspace, size_t workspace_bytes,
+                      pm_stream_t stream) {
+    int st = check_shared_dims(T, H, Is);
+    if (st != PM_OK) return st;
+    if (T == 0) return PM_OK;
+    if (!x || !w_sg || !w13 || !w13_s || !w2 || !w2_s || !out || !workspace) return PM_ERR_INVALID;
+    if (!a16(x) || !a16(w_sg) || !a16(w13) || !a16(w2) || !a16(out) || !a16(workspace)) return PM_ERR_ALIGN;
+    const SharedLayout L = shared_layout_of(T, H, Is, false);
+    if (workspace_bytes < L.total) return PM_ERR_WORKSPACE;
+    DeviceInfo d;
+    st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    int32_t* status = reinterpret_cast<int32_t*>(ws + L.status);
+    if (cudaMemsetAsync(status, 0, 4 * sizeof(int32_t), s) != cudaSuccess) return PM_ERR_CUDA;
+    return shared_fp8_run(x, w_sg, w13, w13_s, w2, w2_s, T, H, Is, out, L, ws, status, d, s);
+}
+
+size_t pm_moe_block_workspace_bytes(int T, int H, int I, int Is, int E, int k) {
+    if (check_dims(T, H, I, E, k) != PM_OK || check_shared_dims(T, H, Is) != PM_OK) return 0;
+    return layout_of(T, H, I, E, k, PM_FMT_FP8).total + shared_layout_of(T, H, Is, true).total;
+}
+
+int pm_moe_block_fp8(const void* x, const void* router_w, const void* logits, const uint8_t* w1, const float* w1_s,
+                     const uint8_t* w2, const float* w2_s, const void* w_sg, const uint8_t* sw13,
+                     const float* sw13_s, const uint8_t* sw2, const float* sw2_s, int T, int H, int I, int Is, int E,
+                     int k, void* out, void* workspace, size_t workspace_bytes, pm_stream_t stream) {
+    int st = check_dims(T, H, I, E, k);
+    if (st != PM_OK) return st;
+    st = check_shared_dims(T, H, Is);
+    if (st != PM_OK) return st;
+    if (T == 0) return PM_OK;
+    if (!x || !out || !w_sg || !sw13 || !sw13_s || !sw2 || !sw2_s || !workspace) return PM_ERR_INVALID;
+    if (!a16(x) || !a16(out) || !a16(w_sg) || !a16(sw13) || !a16(sw2) || !a16(workspace)) return PM_ERR_ALIGN;
+    const size_t routed = layout_of(T, H, I, E, k, PM_FMT_FP8).total;
+    const SharedLayout L = shared_layout_of(T, H, Is, true);
+    if (workspace_bytes < routed + L.total) return PM_ERR_WORKSPACE;
+    DeviceInfo d;
+    st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    int32_t* status = reinterpret_cast<int32_t*>(ws);  // the routed layout's status region comes first
+    if (cudaMemsetAsync(status, 0, 4 * sizeof(int32_t), s) != cudaSuccess) return PM_ERR_CUDA;
+    uint8_t* sws = ws + routed;
+    // The shared expert runs on this thread's side stream, forked from and joined back into the caller's stream
+    // (events, so a graph capture records two branches): its kernels overlap the routed routing kernels, which
+    // leave most SMs idle, and the final sum waits for it.
+    SideStream* side = side_stream();
+    if (side == nullptr) return PM_ERR_CUDA;
+    if (cudaEventRecord(side->fork, s) != cudaSuccess || cudaStreamWaitEvent(side->stream, side->fork, 0) != cudaSuccess)
+        return PM_ERR_CUDA;
+    st = shared_fp8_run(x, w_sg, sw13, sw13_s, sw2, sw2_s, T, H, Is, sws + L.out, L, sws, status, d, side->stream);
+    if (st != PM_OK) return st;
+    if (cudaEventRecord(side->join, side->stream) != cudaSuccess) return PM_ERR_CUDA;
+    return forward_fp8_impl(x, router_w, logits, w1, w1_s, w2, w2_s, T, H, I, E, k, sws + L.out, side->join, out,
+                            workspace, routed, stream, false);
 }
 
 int pm_moe_quant_nvfp4(const void* x, int T, int H, int k, const int32_t* slot_of, float gs, uint8_t* a_q,
@@ -551,6 +714,22 @@ int pm_moe_forward_nvfp4(const void* x, const void* router_w, const void* logits
                             L.max_slots, T, k, H, I, E, R(PM_WS_C3), status, stream);
     if (st != PM_OK) return st;
     return cuda_status(launch_combine(R(PM_WS_C3), nullptr, T, k, H, out, s));
+}
+
+int pm_nvfp4_prepare(const uint8_t* w, const float* s, int E, int R, int C, uint8_t* packed, uint8_t* scales,
+                     float* g, pm_stream_t stream) {
+    if (E < 0 || R < 0 || C < 0) return PM_ERR_INVALID;
+    if (R % 128 != 0 || C % 128 != 0 || (long)E * R > (1L << 31) || (long)E * R * C / 16 > (1L << 31))
+        return PM_ERR_SHAPE;
+    if (E == 0 || R == 0 || C == 0) return PM_OK;
+    if (!w || !s || !packed || !scales || !g) return PM_ERR_INVALID;
+    if (!a16(w) || (reinterpret_cast<uintptr_t>(packed) & 7u) != 0 || (reinterpret_cast<uintptr_t>(s) & 3u) != 0 ||
+        (reinterpret_cast<uintptr_t>(g) & 3u) != 0)
+        return PM_ERR_ALIGN;
+    DeviceInfo d;
+    const int st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    return cuda_status(launch_nvfp4_prepare(w, s, E, R, C, packed, scales, g, d.sms, (cudaStream_t)stream));
 }
 
 // ---------------------------------------------------------------------------------------- expert parallelism

@@ -87,7 +87,12 @@ __device__ __forceinline__ void promote32(uint32_t taddr, float scale, float* ac
     }
 }
 
-template <int MODE>
+// Down-GEMM epilogue variants (EPI): kEpiPlain stores bf16(acc * w) to c3; kEpiRoundFirst stores
+// bf16(bf16(acc) * w), the bf16 product of a rounded result and a bf16 weight; kEpiDstRows stores each row to the
+// address args.dst_rows gives for it (0: not stored).
+constexpr int kEpiPlain = 0, kEpiRoundFirst = 1, kEpiDstRows = 2;
+
+template <int MODE, int EPI = kEpiPlain>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                         const GemmArgs args) {
@@ -248,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // down: the row's flat index (the slot itself when there is no row map) and, with a destination table,
             // the address its weighted row is stored to (0: the slot holds no row)
             const int flat = MODE == 1 ? (args.sorted_ids != nullptr ? args.sorted_ids[grow] : grow) : 0;
-            const uint64_t drow = (MODE == 1 && args.dst_rows != nullptr) ? args.dst_rows[grow] : 0;
+            const uint64_t drow = (MODE == 1 && EPI == kEpiDstRows) ? args.dst_rows[grow] : 0;
             float w = 0.0f;
 #pragma unroll
             for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
@@ -337,6 +342,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // thread), then write the rows out as coalesced 256-byte segments, two rows per instruction.
                 constexpr int RB = Cfg<MODE>::kStageRowBytes;
                 uint8_t* wst = staging + (size_t)(warp - kEpiWarp0) * 32 * RB;
+                if constexpr (EPI == kEpiRoundFirst) {
+#pragma unroll
+                    for (int i = 0; i < 128; ++i) acc[i] = __bfloat162float(__float2bfloat16_rn(acc[i]));
+                }
 #pragma unroll
                 for (int u = 0; u < 16; ++u) {
                     uint4 o;
@@ -353,12 +362,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int sub = lane >> 4, chunk = lane & 15;
                 for (int r = 0; r < 32; r += 2) {
                     const int f = __shfl_sync(0xffffffffu, flat, r + sub);
-                    const uint64_t dr = __shfl_sync(0xffffffffu, drow, r + sub);
-                    if (f < args.n_valid && (args.dst_rows == nullptr || dr != 0)) {
+                    if constexpr (EPI == kEpiDstRows) {
+                        const uint64_t dr = __shfl_sync(0xffffffffu, drow, r + sub);
+                        if (f < args.n_valid && dr != 0) {
+                            const uint4 v = *reinterpret_cast<const uint4*>(wst + (r + sub) * RB + chunk * 16);
+                            __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(dr);
+                            *reinterpret_cast<uint4*>(row + nt * kBN + 128 * half + chunk * 8) = v;
+                        }
+                    } else if (f < args.n_valid) {
                         const uint4 v = *reinterpret_cast<const uint4*>(wst + (r + sub) * RB + chunk * 16);
-                        __nv_bfloat16* row = args.dst_rows != nullptr ? reinterpret_cast<__nv_bfloat16*>(dr)
-                                                                      : args.c3 + (size_t)f * H;
-                        *reinterpret_cast<uint4*>(row + nt * kBN + 128 * half + chunk * 8) = v;
+                        *reinterpret_cast<uint4*>(args.c3 + (size_t)f * H + nt * kBN + 128 * half + chunk * 8) = v;
                     }
                 }
                 __syncwarp();
@@ -379,24 +392,33 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 cudaError_t launch_gemm_fp8(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, const GemmArgs& args,
                             int num_sms, cudaStream_t s) {
-    static bool configured[64][2] = {};
+    // variant 0: gate_up; 1..3: down with the plain, round-first or per-row-destination epilogue
+    static bool configured[64][4] = {};
+    const int variant = mode == 0 ? 0 : (args.dst_rows != nullptr ? 3 : (args.round_first ? 2 : 1));
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !configured[dev][mode]) {
-        cudaError_t e = mode == 0 ? cudaFuncSetAttribute(moe_gemm_fp8_kernel<0>,
-                                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                         (int)smem_bytes<0>())
-                                  : cudaFuncSetAttribute(moe_gemm_fp8_kernel<1>,
-                                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                         (int)smem_bytes<1>());
+    if (dev < 64 && !configured[dev][variant]) {
+        cudaError_t e;
+        switch (variant) {
+            case 0: e = cudaFuncSetAttribute(moe_gemm_fp8_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem_bytes<0>()); break;
+            case 1: e = cudaFuncSetAttribute(moe_gemm_fp8_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem_bytes<1>()); break;
+            case 2: e = cudaFuncSetAttribute(moe_gemm_fp8_kernel<1, kEpiRoundFirst>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<1>()); break;
+            default: e = cudaFuncSetAttribute(moe_gemm_fp8_kernel<1, kEpiDstRows>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<1>());
+        }
         if (e != cudaSuccess) return e;
-        configured[dev][mode] = true;
+        configured[dev][variant] = true;
     }
     const int grid = args.max_tiles < num_sms ? (args.max_tiles > 0 ? args.max_tiles : 1) : num_sms;
-    if (mode == 0)
-        moe_gemm_fp8_kernel<0><<<grid, kThreads, smem_bytes<0>(), s>>>(tm_a, tm_b, args);
-    else
-        moe_gemm_fp8_kernel<1><<<grid, kThreads, smem_bytes<1>(), s>>>(tm_a, tm_b, args);
+    switch (variant) {
+        case 0: moe_gemm_fp8_kernel<0><<<grid, kThreads, smem_bytes<0>(), s>>>(tm_a, tm_b, args); break;
+        case 1: moe_gemm_fp8_kernel<1><<<grid, kThreads, smem_bytes<1>(), s>>>(tm_a, tm_b, args); break;
+        case 2: moe_gemm_fp8_kernel<1, kEpiRoundFirst><<<grid, kThreads, smem_bytes<1>(), s>>>(tm_a, tm_b, args); break;
+        default: moe_gemm_fp8_kernel<1, kEpiDstRows><<<grid, kThreads, smem_bytes<1>(), s>>>(tm_a, tm_b, args);
+    }
     return cudaGetLastError();
 }
 

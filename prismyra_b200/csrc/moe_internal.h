@@ -49,7 +49,12 @@ cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int3
 cudaError_t launch_quant_fp8(const void* x, int T, int H, int k, const int32_t* slot_of, uint8_t* x_q, float* x_s,
                              cudaStream_t s);
 // out[t] = bf16(sum_j c3[row(t*k + j)]) in fp32, j ascending; row = identity or row_of.
-cudaError_t launch_combine(const void* c3, const int32_t* row_of, int T, int k, int H, void* out, cudaStream_t s);
+cudaError_t launch_combine(const void* c3, const int32_t* row_of, int T, int k, int H, void* out, cudaStream_t s,
+                           const void* add = nullptr);
+// Shared-expert gate g[t] = bf16(sigmoid(bf16(x[t] . w_sg))) as fp32, plus the one-expert plan of the shared
+// expert's GEMMs (expert_ids[b] = 0 for the ceil(T/128) blocks, *num_post_pad = their slots).
+cudaError_t launch_shared_gate(const void* x, const void* w_sg, int T, int H, float* gate, int32_t* expert_ids,
+                               int32_t* num_post_pad, int sms, cudaStream_t s);
 // dst[dst_index[i]] = src[i] for rows of row_bytes (multiple of 16) with the given byte strides.
 cudaError_t launch_scatter_rows(const void* src, int rows, int row_bytes, int src_stride, const int32_t* dst_index,
                                 void* dst, int dst_stride, cudaStream_t s);
@@ -74,6 +79,7 @@ struct GemmArgs {
     const uint64_t* dst_rows; // [rows] or nullptr: the address each row's [H] bf16 result is stored to (0: none),
                               // instead of c3 -- e.g. another GPU's memory over NVLink
     int n_valid;
+    int round_first;          // down epilogue: bf16(bf16(acc) * w) instead of bf16(acc * w) (a bf16 product)
     int* err;                 // set to 1 when a wait timed out
 };
 
@@ -132,6 +138,9 @@ cudaError_t launch_quant_nvfp4(const void* x, int T, int H, int k, const int32_t
                                uint8_t* a_sf, cudaStream_t s);
 cudaError_t launch_gemm_nvfp4(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, const NvGemmArgs& args,
                               int num_sms, cudaStream_t s);
+// NVFP4 weight preparation of E FP8 block-scaled matrices of R x C (g doubles as the scratch of the maxima).
+cudaError_t launch_nvfp4_prepare(const uint8_t* w, const float* s, int E, int R, int C, uint8_t* packed,
+                                 uint8_t* sf, float* g, int sms, cudaStream_t stream);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda): a 2-D row-major
 // tensor of `outer` rows x `inner` elements, rows `row_bytes` apart, 128-byte swizzled boxes.

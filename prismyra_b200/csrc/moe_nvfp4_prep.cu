@@ -1,0 +1,147 @@
+// NVFP4 weight preparation on the GPU: a stack of FP8 (e4m3, 128x128 fp32 block multipliers) expert matrices ->
+// packed e2m1 codes, one e4m3 scale per 16 elements and one fp32 global scale per matrix, bit for bit what the
+// reference's prepare_layer computes (prismyra/kernels/nvfp4.py:315-331) with _dequant_fp8 (nvfp4.py:97-100) and
+// quantize (nvfp4.py:41-51) in fp32 torch arithmetic (for finite weights):
+//
+//   d     = fp32(q) * s_block                                   one rounding
+//   g     = reciprocal(max(amax|d|, 1e-12)) * 2688              torch evaluates `448.0 * 6.0 / t` as
+//                                                               t.reciprocal() * 2688: two roundings
+//   sf    = e4m3(min((amax16 / 6) * g, 448))                    amax over each 16-element group of a row
+//   eff   = fp32(sf) / g
+//   x     = eff > 0 ? clamp(d / eff, -6, 6) : 0
+//   code  = first j minimising |(|x| - E2M1[j])|, | 8 if x < 0  (torch.argmin keeps the first minimum, so a tie
+//                                                               takes the smaller magnitude; computed as the
+//                                                               count of grid midpoints below |x|)
+//
+// Launches: a zeroing of the per-matrix maxima, the maxima (byte-wise magnitude maxima of the e4m3 codes, then an
+// unsigned max on the bit patterns of non-negative floats -- exact and order-free), the global scales, and the
+// quantisation of every 16-element group (one thread per group, 16-byte loads).  The maxima pass streams the
+// weights at HBM speed; the quantisation is instruction-bound (an IEEE division per weight).
+#include "moe_internal.h"
+#include "ptx.cuh"
+
+#include <cuda_fp16.h>
+
+namespace pm {
+namespace {
+
+__device__ __forceinline__ float e4m3_to_f32(uint32_t byte) {
+    const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(byte), __NV_E4M3);
+    return __half2float(__half(h));
+}
+
+// The largest magnitude code of 16 e4m3 bytes: e4m3 is sign-magnitude with magnitudes ordered like their 7-bit
+// codes, and fl(|q| * s) grows with |q|, so max_i |fl(q_i * s)| = fl(e4m3(max code) * s) exactly.
+__device__ __forceinline__ uint32_t max_magnitude_code(uint4 q) {
+    const uint32_t m = __vmaxu4(__vmaxu4(q.x & 0x7f7f7f7fu, q.y & 0x7f7f7f7fu),
+                                __vmaxu4(q.z & 0x7f7f7f7fu, q.w & 0x7f7f7f7fu));
+    const uint32_t h = __vmaxu4(m, m >> 16);
+    return max(h & 0xffu, (h >> 8) & 0xffu);
+}
+
+// A grid-stride walk over the 16-byte vectors of a row-major [rows, C] byte matrix that keeps (row, vector within
+// the row) up to date by addition: one division per thread instead of two per vector.
+struct VecWalk {
+    unsigned row, cv;                 // current row and 16-byte vector within it
+    unsigned step_rows, step_cv;      // the grid stride, in rows and vectors
+    unsigned per_row;                 // vectors per row (C / 16)
+
+    __device__ VecWalk(unsigned start, unsigned stride, unsigned per_row_)
+        : row(start / per_row_), cv(start % per_row_), step_rows(stride / per_row_), step_cv(stride % per_row_),
+          per_row(per_row_) {}
+    __device__ void next() {
+        cv += step_cv;
+        row += step_rows;
+        if (cv >= per_row) {
+            cv -= per_row;
+            ++row;
+        }
+    }
+};
+
+__global__ void __launch_bounds__(256) prep_amax_kernel(const uint8_t* __restrict__ w, const float* __restrict__ s,
+                                                        int R, int C, unsigned* __restrict__ amax_bits) {
+    const unsigned m = blockIdx.y;
+    const unsigned per_row = C / 16, cb = C / 128;
+    const uint8_t* wm = w + (size_t)m * R * C;
+    const float* sm = s + (size_t)m * (R / 128) * cb;
+    float amax = 0.0f;
+    for (VecWalk it(blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x, per_row); it.row < (unsigned)R;
+         it.next()) {
+        const uint4 q = *reinterpret_cast<const uint4*>(wm + (size_t)it.row * C + it.cv * 16);
+        const float sb = sm[(it.row / 128) * cb + it.cv / 8];
+        amax = fmaxf(amax, fabsf(__fmul_rn(e4m3_to_f32(max_magnitude_code(q)), sb)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    __shared__ float warp_max[8];
+    if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float b = warp_max[0];
+        for (int i = 1; i < (int)(blockDim.x >> 5); ++i) b = fmaxf(b, warp_max[i]);
+        atomicMax(amax_bits + m, __float_as_uint(b));  // non-negative floats order like their bit patterns
+    }
+}
+
+// In place: the maximum's bit pattern -> g = reciprocal(max(amax, 1e-12)) * 2688.
+__global__ void prep_global_kernel(float* __restrict__ g, int E) {
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m >= E) return;
+    const float amax = fmaxf(__uint_as_float(reinterpret_cast<unsigned*>(g)[m]), 1e-12f);
+    g[m] = __fmul_rn(__frcp_rn(amax), 2688.0f);
+}
+
+// e2m1 magnitude code of a in [0, 6]: the number of midpoints of the e2m1 grid strictly below a.  This equals the
+// reference's first arg-min of |fl(a - grid[j])| (ties to the smaller magnitude) for every fp32 a in [0, 6];
+// the equality was checked exhaustively over all 1,086,324,737 such values.
+__device__ __forceinline__ uint32_t e2m1_magnitude(float a) {
+    return (uint32_t)(a > 0.25f) + (uint32_t)(a > 0.75f) + (uint32_t)(a > 1.25f) + (uint32_t)(a > 1.75f) +
+           (uint32_t)(a > 2.5f) + (uint32_t)(a > 3.5f) + (uint32_t)(a > 5.0f);
+}
+
+// One thread per 16-element group of the stacked [E * R, C] matrix (matrix m = row / R).
+__global__ void __launch_bounds__(256) prep_quant_kernel(const uint8_t* __restrict__ w, const float* __restrict__ s,
+                                                         const float* __restrict__ g, int E, int R, int C,
+                                                         uint8_t* __restrict__ packed, uint8_t* __restrict__ sf) {
+    const unsigned per_row = C / 16, cb = C / 128, rows = (unsigned)E * R;
+    for (VecWalk it(blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x, per_row); it.row < rows;
+         it.next()) {
+        const size_t i = (size_t)it.row * per_row + it.cv;  // group index = 16-byte vector index
+        const uint4 q = *reinterpret_cast<const uint4*>(w + i * 16);
+        const float sb = s[(it.row / 128) * cb + it.cv / 8];  // R % 128 == 0: blocks never straddle matrices
+        const float amax = fabsf(__fmul_rn(e4m3_to_f32(max_magnitude_code(q)), sb));
+        const float gm = g[it.row / (unsigned)R];
+        const float scale = fminf(__fmul_rn(__fdiv_rn(amax, 6.0f), gm), 448.0f);
+        const __nv_fp8_storage_t sbyte = __nv_cvt_float_to_fp8(scale, __NV_SATFINITE, __NV_E4M3);
+        const float eff = __fdiv_rn(e4m3_to_f32(sbyte), gm);
+        const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+        uint32_t out[2] = {0u, 0u};
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const float d = __fmul_rn(e4m3_to_f32((words[j / 4] >> (8 * (j % 4))) & 0xffu), sb);
+            const float x = eff > 0.0f ? fminf(fmaxf(__fdiv_rn(d, eff), -6.0f), 6.0f) : 0.0f;
+            const uint32_t code = e2m1_magnitude(fabsf(x)) | (x < 0.0f ? 8u : 0u);
+            out[j / 8] |= code << (4 * (j % 8));
+        }
+        *reinterpret_cast<uint2*>(packed + i * 8) = make_uint2(out[0], out[1]);
+        sf[i] = static_cast<uint8_t>(sbyte);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_nvfp4_prepare(const uint8_t* w, const float* s, int E, int R, int C, uint8_t* packed,
+                                 uint8_t* sf, float* g, int sms, cudaStream_t stream) {
+    cudaError_t e = cudaMemsetAsync(g, 0, sizeof(float) * (size_t)E, stream);
+    if (e != cudaSuccess) return e;
+    const long groups = (long)R * C / 16;  // per matrix
+    const int per_matrix = (int)std::min<long>(std::max(1, (8 * sms + E - 1) / E), (groups + 255) / 256);
+    prep_amax_kernel<<<dim3(per_matrix, E), 256, 0, stream>>>(w, s, R, C, reinterpret_cast<unsigned*>(g));
+    prep_global_kernel<<<(E + 255) / 256, 256, 0, stream>>>(g, E);
+    const long blocks = std::min<long>((long)sms * 8, (groups * E + 255) / 256);
+    prep_quant_kernel<<<(int)blocks, 256, 0, stream>>>(w, s, g, E, R, C, packed, sf);
+    return cudaGetLastError();
+}
+
+}  // namespace pm

@@ -61,9 +61,12 @@ __global__ void __launch_bounds__(256) quant_fp8_kernel(const __nv_bfloat16* __r
 }
 
 // out[t, c..c+7] = bf16(sum_j c3[row(t*k + j), c..c+7]) with an fp32 running sum, j ascending; row() is the
-// identity or the row_of map (rows returned by expert-parallel ranks arrive in their send order).
+// identity or the row_of map (rows returned by expert-parallel ranks arrive in their send order).  With add, the
+// rounded sum is then added to add[t] and rounded again: `routed + shared` of two bf16 tensors (reference
+// prismyra/kernels/qwen3_moe.py:199).
 __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ c3,
                                                       const int32_t* __restrict__ row_of, int T, int k, int H,
+                                                      const __nv_bfloat16* __restrict__ add,
                                                       __nv_bfloat16* __restrict__ out) {
     const long total = (long)T * (H / 8);
     for (long q = (long)blockIdx.x * blockDim.x + threadIdx.x; q < total; q += (long)gridDim.x * blockDim.x) {
@@ -83,6 +86,12 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
         __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
 #pragma unroll
         for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(acc[i]);
+        if (add != nullptr) {
+            const uint4 u = *reinterpret_cast<const uint4*>(add + (size_t)t * H + c);
+            const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(__bfloat162float(ob[i]) + __bfloat162float(b[i]));
+        }
         *reinterpret_cast<uint4*>(out + (size_t)t * H + c) = o;
     }
 }
@@ -132,7 +141,8 @@ cudaError_t launch_scatter_rows(const void* src, int rows, int row_bytes, int sr
     return cudaGetLastError();
 }
 
-cudaError_t launch_combine(const void* c3, const int32_t* row_of, int T, int k, int H, void* out, cudaStream_t s) {
+cudaError_t launch_combine(const void* c3, const int32_t* row_of, int T, int k, int H, void* out, cudaStream_t s,
+                           const void* add) {
     if (T == 0) return cudaSuccess;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
@@ -141,7 +151,7 @@ cudaError_t launch_combine(const void* c3, const int32_t* row_of, int T, int k, 
     const long want = (total + 255) / 256;
     const int blocks = (int)(want < (long)sms * 16 ? want : (long)sms * 16);
     combine_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(c3), row_of, T, k, H,
-                                          static_cast<__nv_bfloat16*>(out));
+                                          static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out));
     return cudaGetLastError();
 }
 

@@ -5,7 +5,10 @@
 ``shared_expert``, ``shared_expert_gate``, ``top_k``, ``w1`` and ``w2``, and its ``forward`` maps bf16
 ``[..., H]`` to bf16 of the same shape.  The routed path (router projection, softmax / top-k, expert alignment,
 both grouped FP8 GEMMs with silu-and-mul between them, and the weighted top-k sum) runs in
-``libprismyra_moe.so``; the shared expert and its gate stay the framework's own modules, as in the reference.
+``libprismyra_moe.so``.  When the block's shared expert holds 128x128 block-FP8 projections (transformers'
+``FP8Linear`` or the reference's ``Fp8Linear``) the shared expert, its sigmoid gate and the final ``routed +
+shared`` run in the same library call (``pm_moe_block_fp8``) with the reference's arithmetic; otherwise they stay
+the framework's own modules, as in the reference.
 """
 
 from __future__ import annotations
@@ -37,6 +40,50 @@ def _fp8_expert_tensors(experts: nn.Module):
     return w1, s1, w2, s2
 
 
+def _fp8_linear(m: nn.Module | None):
+    """(weight e4m3 [out, in], block multipliers f32 [out/128, in/128]) of a bias-free block-FP8 projection with
+    dynamic activation quantisation, or None."""
+    if m is None:
+        return None
+    w = getattr(m, "weight", None)
+    s = getattr(m, "weight_scale_inv", None)
+    if s is None:
+        s = getattr(m, "scale", None)
+    if w is None or s is None or w.dtype != torch.float8_e4m3fn or getattr(m, "bias", None) is not None:
+        return None
+    if getattr(m, "activation_scheme", "dynamic") != "dynamic":
+        return None
+    o, i = w.shape
+    if o % 128 or i % 128 or tuple(s.shape) != (o // 128, i // 128):
+        return None
+    return w, s
+
+
+def _fp8_shared_tensors(block: nn.Module, hidden: int):
+    """(w_sg bf16 [H], w13 e4m3 [2 Is, H], w13_s, w2 e4m3 [H, Is], w2_s) of a silu-gated block-FP8 shared expert
+    with a bf16 one-row gate, or None."""
+    se = getattr(block, "shared_expert", None)
+    gate = getattr(block, "shared_expert_gate", None)
+    if se is None or gate is None:
+        return None
+    parts = [_fp8_linear(getattr(se, n, None)) for n in ("gate_proj", "up_proj", "down_proj")]
+    if any(p is None for p in parts):
+        return None
+    act = type(getattr(se, "act_fn", None)).__name__
+    w_sg = getattr(gate, "weight", None)
+    if act not in ("SiLU", "SiLUActivation") or w_sg is None or w_sg.dtype != torch.bfloat16:
+        return None
+    (wg, sg), (wu, su), (wd, sd) = parts
+    Is = wg.shape[0]
+    if (tuple(w_sg.shape) != (1, hidden) or tuple(wg.shape) != (Is, hidden) or wu.shape != wg.shape
+            or tuple(wd.shape) != (hidden, Is)):
+        return None
+    w13 = torch.cat([wg.detach(), wu.detach()], 0).contiguous()
+    s13 = torch.cat([sg.detach(), su.detach()], 0).to(torch.float32).contiguous()
+    return (w_sg.detach().reshape(hidden).contiguous(), w13, s13, wd.detach().contiguous(),
+            sd.detach().to(torch.float32).contiguous())
+
+
 class FusedExperts(nn.Module):
     """Routed experts through the B200 kernels; router and shared expert kept as in the framework block."""
 
@@ -60,6 +107,8 @@ class FusedExperts(nn.Module):
         if (E > LIMITS["max_experts"] or self.top_k > min(LIMITS["max_top_k"], E)
                 or H % LIMITS["hidden_multiple"] or self.inter % LIMITS["intermediate_multiple"]):
             raise AdapterError(f"shape outside the kernel's range: E={E} k={self.top_k} H={H} I={self.inter}")
+        #: (w_sg, w13, w13_s, w2, w2_s) when the shared expert runs in the library, else None
+        self.shared_fp8 = _fp8_shared_tensors(block, H)
 
     def _route(self, x: torch.Tensor) -> torch.Tensor:
         """Router logits (bf16 [T, E]), row-count invariant: each logit is reduced over H in a fixed order."""
@@ -74,7 +123,12 @@ class FusedExperts(nn.Module):
 
     def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
         shape = hidden_states.shape
-        x = hidden_states.reshape(-1, shape[-1])
+        x = hidden_states.reshape(-1, shape[-1]).contiguous()
+        if self.shared_fp8 is not None:
+            w_sg, w13, s13, w2, s2 = self.shared_fp8
+            out = ops.block_fp8(x, self.w1, self.w1_scale, self.w2, self.w2_scale, self.top_k, w_sg, w13, s13, w2,
+                                s2, router_w=self.gate.weight.contiguous())
+            return out.reshape(shape)
         routed = self.routed(x)
         shared = torch.sigmoid(F.linear(x, self.shared_expert_gate.weight)) * self.shared_expert(x)
         return (routed + shared).reshape(shape)

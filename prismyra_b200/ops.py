@@ -125,6 +125,74 @@ def forward_fp8(x: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch
     return out
 
 
+def _shared_checks(x, w_sg, w13, w13_s, w2, w2_s):
+    T, H = x.shape
+    I2s = w13.shape[0]
+    Is = I2s // 2
+    _cuda(w_sg, "w_sg", torch.bfloat16)
+    _need(w_sg.numel() == H, f"w_sg must hold H={H} values")
+    _cuda(w13, "w13", (FP8, torch.uint8), (2 * Is, H))
+    _cuda(w13_s, "w13_s", torch.float32, (2 * Is // 128, H // 128))
+    _cuda(w2, "w2", (FP8, torch.uint8), (H, Is))
+    _cuda(w2_s, "w2_s", torch.float32, (H // 128, Is // 128))
+    return T, H, Is
+
+
+def shared_fp8(x: torch.Tensor, w_sg: torch.Tensor, w13: torch.Tensor, w13_s: torch.Tensor, w2: torch.Tensor,
+               w2_s: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The shared expert on block-FP8 weights: sigmoid(x . w_sg) * down(silu(gate x) * up x) -> bf16 [T, H]
+    (reference qwen3_moe.py:198); w13 = gate_proj rows then up_proj rows [2 Is, H]."""
+    _need(x.dim() == 2, "x must be [T, H]")
+    _cuda(x, "x", torch.bfloat16)
+    T, H, Is = _shared_checks(x, w_sg, w13, w13_s, w2, w2_s)
+    if out is None:
+        out = torch.empty_like(x)
+    _cuda(out, "out", torch.bfloat16, (T, H))
+    if T == 0:
+        return out
+    n = _lib.load().pm_moe_shared_workspace_bytes(T, H, Is)
+    _need(n > 0, f"unsupported shared-expert shape T={T} H={H} Is={Is}")
+    ws = POOL.get(x.device, n, "shared")
+    _lib.call("pm_moe_shared_fp8", _p(x), _p(w_sg), _p(_u8(w13)), _p(w13_s), _p(_u8(w2)), _p(w2_s), T, H, Is,
+              _p(out), _p(ws), n, _stream(x.device))
+    return out
+
+
+def block_fp8(x: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch.Tensor, w2_s: torch.Tensor,
+              top_k: int, w_sg: torch.Tensor, sw13: torch.Tensor, sw13_s: torch.Tensor, sw2: torch.Tensor,
+              sw2_s: torch.Tensor, router_w: torch.Tensor | None = None, logits: torch.Tensor | None = None,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed experts plus the shared expert, summed as two bf16 tensors: the whole FusedExperts.forward
+    (reference qwen3_moe.py:184-199) in one library call."""
+    _need(x.dim() == 2, "x must be [T, H]")
+    _cuda(x, "x", torch.bfloat16)
+    T, H = x.shape
+    E, I2, _ = w1.shape
+    I = I2 // 2
+    _cuda(w1, "w1", (FP8, torch.uint8), (E, 2 * I, H))
+    _cuda(w2, "w2", (FP8, torch.uint8), (E, H, I))
+    _cuda(w1_s, "w1_s", torch.float32, (E, 2 * I // 128, H // 128))
+    _cuda(w2_s, "w2_s", torch.float32, (E, H // 128, I // 128))
+    _, _, Is = _shared_checks(x, w_sg, sw13, sw13_s, sw2, sw2_s)
+    _need(router_w is not None or logits is not None, "give router_w or logits")
+    if logits is not None:
+        _cuda(logits, "logits", torch.bfloat16, (T, E))
+    else:
+        _cuda(router_w, "router_w", torch.bfloat16, (E, H))
+    if out is None:
+        out = torch.empty_like(x)
+    _cuda(out, "out", torch.bfloat16, (T, H))
+    if T == 0:
+        return out
+    n = _lib.load().pm_moe_block_workspace_bytes(T, H, I, Is, E, top_k)
+    _need(n > 0, f"unsupported MoE block shape T={T} H={H} I={I} Is={Is} E={E} k={top_k}")
+    ws = POOL.get(x.device, n, "block")
+    _lib.call("pm_moe_block_fp8", _p(x), _p(router_w), _p(logits), _p(_u8(w1)), _p(w1_s), _p(_u8(w2)), _p(w2_s),
+              _p(w_sg), _p(_u8(sw13)), _p(sw13_s), _p(_u8(sw2)), _p(sw2_s), T, H, I, Is, E, top_k, _p(out), _p(ws),
+              n, _stream(x.device))
+    return out
+
+
 class _HostPipe:
     """Per-(device, thread) copy streams and device row buffers for :func:`forward_fp8_host` (grow-only, never
     freed, so addresses stay stable across calls)."""
@@ -401,3 +469,18 @@ def gemm2_nvfp4(a_q, a_sf, w2, w2_sf, alpha2, expert_ids, npp, sorted_ids, topk_
     _lib.call("pm_moe_gemm2_nvfp4", _p(a_q), _p(a_sf), _p(w2), _p(w2_sf), _p(alpha2), _p(expert_ids), _p(npp),
               _p(sorted_ids), _p(topk_w), ms, T, k, H, I, E, _p(c3), _p(err), _stream(a_q.device))
     return c3, err
+
+
+def nvfp4_prepare(w: torch.Tensor, s: torch.Tensor):
+    """FP8 expert stack -> NVFP4 on the GPU: w e4m3 (or its bytes) [E, R, C], s fp32 [E, R/128, C/128] ->
+    (packed u8 [E, R, C/2], row-major e4m3 scales [E, R, C/16], g fp32 [E]); bit for bit the reference's
+    prepare_layer arithmetic (prismyra/kernels/nvfp4.py:315-331)."""
+    _cuda(w, "w", (torch.float8_e4m3fn, torch.uint8))
+    _need(w.dim() == 3, "w must be [E, R, C]")
+    E, R, C = w.shape
+    _cuda(s, "s", torch.float32, (E, R // 128, C // 128))
+    packed = torch.empty(E, R, C // 2, dtype=torch.uint8, device=w.device)
+    scales = torch.empty(E, R, C // 16, dtype=torch.float8_e4m3fn, device=w.device)
+    g = torch.empty(E, dtype=torch.float32, device=w.device)
+    _lib.call("pm_nvfp4_prepare", _p(w), _p(s), E, R, C, _p(packed), _p(scales), _p(g), _stream(w.device))
+    return packed, scales, g

@@ -22,6 +22,10 @@ the code that actually defines it, run on the CPU:
 * ``nvfp4.npz`` -- the reference's own ``prismyra.kernels.nvfp4.quantize`` / ``_dequant_fp8`` / ``prepare_layer``
   and vLLM's Triton ``_nvfp4_quant_dequant_kernel`` (the activation quantisation of its NVFP4 emulation path),
   interpreted on the CPU.
+* ``nvfp4_search.npz`` -- the reference's ``quantize_search`` (with and without importance weights),
+  ``prepare_layer`` with importance weights (one expert with no tokens), and the global scale ``448.0 * 6.0 / t``
+  over many maxima (torch evaluates it as ``t.reciprocal() * 2688``, which a true division misses about one time
+  in four).
 """
 
 from __future__ import annotations
@@ -244,14 +248,46 @@ def make_nvfp4():
     )
 
 
+def make_nvfp4_search():
+    from prismyra.kernels.nvfp4 import prepare_layer, quantize_search
+
+    g = torch.Generator().manual_seed(9)
+    w = torch.randn(96, 256, generator=g) * 0.04
+    w[3] = 0.0
+    imp = torch.rand(256, generator=g) * 2.0
+    gs = 448.0 * 6.0 / w.abs().amax()
+    p_imp, s_imp = quantize_search(w, gs, imp)
+    p_one, s_one = quantize_search(w, gs, None)
+    wq, ws = _fp8_blocks(torch.randn(3, 256, 256, generator=g) * 0.02)
+    wq2, ws2 = _fp8_blocks(torch.randn(3, 256, 128, generator=g) * 0.02)
+    imp_in = torch.rand(3, 256, generator=g)
+    imp_mid = torch.rand(3, 128, generator=g)
+    tok = torch.tensor([5, 0, 2])
+    prep = prepare_layer(wq, ws, wq2, ws2, "cpu", imp_in=imp_in, imp_mid=imp_mid, tok=tok)
+    amax = torch.rand(4096, generator=g) * 0.5 + 1e-4
+    np.savez_compressed(
+        OUT / "nvfp4_search.npz", w=_bits(w), imp=_bits(imp), gs=_bits(gs.reshape(1)),
+        p_imp=_bits(p_imp), s_imp=_bits(s_imp), p_one=_bits(p_one), s_one=_bits(s_one),
+        fp8_w=_bits(wq), fp8_s=_bits(ws), fp8_w2=_bits(wq2), fp8_s2=_bits(ws2), imp_in=_bits(imp_in),
+        imp_mid=_bits(imp_mid), tok=tok.numpy(),
+        prep_w1=_bits(prep["w1"]), prep_s1=_bits(prep["s1"]), prep_g1=_bits(prep["g1"]),
+        prep_w2=_bits(prep["w2"]), prep_s2=_bits(prep["s2"]), prep_g2=_bits(prep["g2"]),
+        amax=_bits(amax), gscale=_bits(448.0 * 6.0 / amax),
+    )
+
+
 if __name__ == "__main__":
     if not any("reference" in p for p in sys.path):
         print("note: PYTHONPATH should hold the reference checkout for the NVFP4 fixtures", file=sys.stderr)
+    if sys.argv[1:] == ["nvfp4_search"]:
+        make_nvfp4_search()
+        sys.exit(0)
     _patch_interpreter_rounding()
     make_align_kat()
     make_router()
     make_quant_edges()
     make_fp8_layer()
     make_nvfp4()
+    make_nvfp4_search()
     for f in sorted(OUT.glob("*.npz")):
         print(f.name, f.stat().st_size)

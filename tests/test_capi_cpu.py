@@ -71,6 +71,10 @@ def test_null_pointers_are_rejected_without_a_device():
     assert lib.pm_moe_topk(None, None, 4, 128, 8, None, None, None) == 1
     assert lib.pm_moe_combine(None, None, 4, 8, 2048, None, None) == 1
     assert lib.pm_moe_read_status(None, None) == 1
+    assert lib.pm_nvfp4_prepare(None, None, 4, 256, 256, None, None, None, None) == 1
+    assert lib.pm_nvfp4_prepare(None, None, 4, 200, 256, None, None, None, None) == 2
+    assert lib.pm_nvfp4_prepare(None, None, 4, 256, 100, None, None, None, None) == 2
+    assert lib.pm_nvfp4_prepare(None, None, 0, 256, 256, None, None, None, None) == 0
 
 
 def test_zero_tokens_is_a_no_op():

@@ -54,7 +54,7 @@ def layer():
     }
     cpu = {"x": bits(fp8["x"]), "w1": bits(prep["w1"]), "w2": bits(prep["w2"]), "s1": bits(prep["s1"]),
            "s2": bits(prep["s2"]), "alpha1": bits(g["alpha1"]), "alpha2": bits(g["alpha2"])}
-    cpu["prep"], cpu["act"] = prep, act
+    cpu["prep"], cpu["act"], cpu["fp8"] = prep, act, fp8
     return g, cpu, a1, a2
 
 
@@ -154,3 +154,31 @@ def test_nvfp4_module_matches_routed_plus_shared(layer):
     routed = forward(g, a1, a2, xf.contiguous(), router_w=g["router_w"])
     shared = torch.sigmoid(torch.nn.functional.linear(xf, blk.shared_expert_gate.weight)) * blk.shared_expert(xf)
     assert torch.equal(y.reshape(-1, H), routed + shared)
+
+
+def test_prepare_on_gpu_matches_cpu_prepare_and_oracle(layer):
+    """pm_nvfp4_prepare on the full stacks (E=128; w13 1536 x 2048, w2 2048 x 768): bit-identical to the torch
+    prepare_layer on the CPU (the reference's arithmetic), and on four experts to the C oracle."""
+    _, cpu, _, _ = layer
+    fp8, prep = cpu["fp8"], cpu["prep"]
+    got = nvfp4.prepare_layer(fp8["w1"], fp8["w1_s"], fp8["w2"], fp8["w2_s"], DEV)
+    for key in ("w1", "s1", "g1", "w2", "s2", "g2"):
+        assert got[key].dtype == prep[key].dtype and got[key].shape == prep[key].shape, key
+        assert np.array_equal(bits(got[key]), bits(prep[key])), key
+    for wk, sk, tag in (("w1", "w1_s", "1"), ("w2", "w2_s", "2")):
+        packed, sf, gs = O.nvfp4_prepare(bits(fp8[wk][:4]), fp8[sk][:4].float().numpy())
+        assert np.array_equal(packed, bits(got["w" + tag][:4]))
+        assert np.array_equal(sf, bits(got["s" + tag][:4]))
+        assert np.array_equal(gs, bits(got["g" + tag][:4]))
+
+
+def test_prepare_on_gpu_matches_reference_fixture(golden):
+    """The reference's own prepare_layer outputs (tests/golden/nvfp4.npz) from the same FP8 stacks."""
+    g = golden("nvfp4")
+    for wk, sk, tag in (("fp8_w", "fp8_s", "1"), ("fp8_w2", "fp8_s2", "2")):
+        w = torch.from_numpy(g[wk]).to(DEV)
+        s = torch.from_numpy(g[sk]).to(DEV)
+        packed, sf, gs = ops.nvfp4_prepare(w, s)
+        assert np.array_equal(bits(packed), g["prep_w" + tag])
+        assert np.array_equal(bits(sf), g["prep_s" + tag])
+        assert np.array_equal(bits(gs), g["prep_g" + tag])

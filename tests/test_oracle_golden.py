@@ -165,21 +165,35 @@ def test_nvfp4_weight_quant_matches_reference(golden):
 
 
 def test_nvfp4_prepare_layer_matches_reference(golden):
-    """prepare_layer = FP8-block dequant, per-matrix global scale g = 2688/amax, then quantize."""
+    """prepare_layer = FP8-block dequant, per-matrix global scale g = reciprocal(amax) * 2688, then quantize."""
     g = golden("nvfp4")
-    for wk, sk, pw, ps, pg in (("fp8_w", "fp8_s", "prep_w1", "prep_s1", "prep_g1"),
-                               ("fp8_w2", "fp8_s2", "prep_w2", "prep_s2", "prep_g2")):
-        wq, ws = g[wk], g[sk]
-        for e in range(wq.shape[0]):
-            R, C = wq[e].shape
-            d = (O.e4m3_to_f32(wq[e]).reshape(R // 128, 128, C // 128, 128)
-                 * ws[e].reshape(R // 128, 1, C // 128, 1)).reshape(R, C).astype(np.float32)
-            if wk == "fp8_w" and e == 0:
-                assert np.array_equal(d, g["dequant0"])
-            gscale = np.float32(448.0 * 6.0) / np.float32(max(np.abs(d).max(), 1e-12))
-            assert np.float32(gscale) == g[pg][e]
-            packed, sf = O.nvfp4_quant_weight(d, float(gscale))
-            assert np.array_equal(sf, g[ps][e]) and np.array_equal(packed, g[pw][e])
+    wq = g["fp8_w"]
+    R, C = wq[0].shape
+    d = (O.e4m3_to_f32(wq[0]).reshape(R // 128, 128, C // 128, 128)
+         * g["fp8_s"][0].reshape(R // 128, 1, C // 128, 1)).reshape(R, C).astype(np.float32)
+    assert np.array_equal(d, g["dequant0"])
+    for wk, sk, tag in (("fp8_w", "fp8_s", "1"), ("fp8_w2", "fp8_s2", "2")):
+        packed, sf, gs = O.nvfp4_prepare(g[wk], g[sk])
+        assert np.array_equal(gs, g["prep_g" + tag])
+        assert np.array_equal(sf, g["prep_s" + tag]) and np.array_equal(packed, g["prep_w" + tag])
+
+
+def test_nvfp4_global_scale_is_reciprocal_times_2688(golden):
+    """The reference's `448.0 * 6.0 / t` is t.reciprocal() * 2688 in torch: two fp32 roundings.  The oracle's
+    rule reproduces all 4096 fixture maxima; a single true division would not."""
+    g = golden("nvfp4_search")
+    amax = g["amax"].astype(np.float32)
+    two = (np.float32(1.0) / amax).astype(np.float32) * np.float32(2688.0)
+    assert np.array_equal(two.astype(np.float32), g["gscale"])
+    assert not np.array_equal((np.float32(2688.0) / amax).astype(np.float32), g["gscale"])
+    # the same rule inside the oracle's prepare, one single-block matrix per maximum
+    E = 64
+    w = np.zeros((E, 128, 128), np.uint8)
+    w[:, 5, 7] = 0x7E  # e4m3 448
+    s = (amax[:E] / np.float32(448.0)).astype(np.float32).reshape(E, 1, 1)
+    _, _, gs = O.nvfp4_prepare(w, s)
+    d_max = (np.float32(448.0) * s.reshape(E)).astype(np.float32)
+    assert np.array_equal(gs, ((np.float32(1.0) / d_max).astype(np.float32) * np.float32(2688.0)).astype(np.float32))
 
 
 def test_nvfp4_act_quant_matches_vllm_emulation(golden):
