@@ -410,7 +410,18 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
     prep_ms = time_region(prep_step, 5, stream)
     n_weights = layer["w1"].numel() + layer["w2"].numel()
     prep_bytes = n_weights * (1.0 + 0.5 + 1.0 / 16.0)
-    prep = {"ms": prep_ms, "gbs": prep_bytes / (prep_ms * 1e-3) / 1e9,
+    # the reference's way: prepare_layer's per-expert torch loop (dequantise, global scale, quantize) on this GPU
+    from prismyra_b200.kernels import nvfp4 as nv_mod
+
+    def torch_prep():
+        for e in range(E):
+            for w, sc in ((layer["w1"], layer["w1_s"]), (layer["w2"], layer["w2_s"])):
+                d = nv_mod.dequant_fp8(w[e], sc[e])
+                nv_mod.quantize(d, 448.0 * 6.0 / d.abs().amax().clamp_min(1e-12))
+
+    torch.cuda.synchronize()
+    t_ref = time_region(torch_prep, 1, stream)
+    prep = {"ms": prep_ms, "reference_torch_ms": t_ref, "gbs": prep_bytes / (prep_ms * 1e-3) / 1e9,
             "frac_hbm": prep_bytes / (prep_ms * 1e-3) / 1e9 / pk["hbm_gbs"], "weights": n_weights,
             "algorithmic_bytes": prep_bytes,
             "note": "three launches per stack: a zeroing, the per-matrix maxima (reads the weights), the quantisation "

@@ -161,6 +161,15 @@ int pm_moe_shared_fp8(const void *x, const void *w_sg, const uint8_t *w13, const
                       const float *w2_s, int T, int H, int Is, void *out, void *workspace, size_t workspace_bytes,
                       pm_stream_t stream);
 
+/* A dense block-FP8 projection, the reference's Fp8Linear.forward (prismyra/kernels/qwen3_moe.py:211-230: vLLM
+ * per_token_group_quant_fp8 of x, then w8a8_triton_block_scaled_mm): out bf16 [T, N] = x [T, K] bf16 times
+ * w e4m3 [N, K] with fp32 128x128 block multipliers w_s [N/128, K/128], each 128-deep K block's exact product sum
+ * scaled by the activation and weight scales and added in K order in fp32, then rounded to bf16.  Row-count
+ * invariant and deterministic.  K % 128 == 0, N % 256 == 0.  Status word at the start of the workspace. */
+size_t pm_fp8_linear_workspace_bytes(int T, int K, int N);
+int pm_fp8_linear(const void *x, const uint8_t *w, const float *w_s, int T, int K, int N, void *out,
+                  void *workspace, size_t workspace_bytes, pm_stream_t stream);
+
 /* The whole FusedExperts.forward (prismyra/kernels/qwen3_moe.py:184-199): routed experts as pm_moe_forward_fp8
  * plus the shared expert as pm_moe_shared_fp8, summed as two bf16 tensors (`routed + shared`, :199: the routed
  * top-k sum is rounded to bf16 first).  Status word at the start of the workspace, as for pm_moe_forward_fp8. */

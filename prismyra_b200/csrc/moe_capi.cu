@@ -716,6 +716,75 @@ int pm_moe_forward_nvfp4(const void* x, const void* router_w, const void* logits
     return cuda_status(launch_combine(R(PM_WS_C3), nullptr, T, k, H, out, s));
 }
 
+// ------------------------------------------------------------------------------------------- dense projection
+struct DenseLayout {
+    size_t status, ones, expert_ids, npp, xq, xs, total;
+    int rows;
+};
+
+static DenseLayout dense_layout_of(int T, int K) {
+    DenseLayout L;
+    const int rows = (T + kBlockM - 1) / kBlockM * kBlockM;
+    size_t o = 0;
+    auto take = [&](size_t bytes) { const size_t at = o; o = align256(o + bytes); return at; };
+    L.status = take(4 * sizeof(int32_t));
+    L.ones = take((size_t)T * 4);
+    L.expert_ids = take((size_t)(rows / kBlockM) * 4);
+    L.npp = take(4);
+    L.xq = take((size_t)rows * K);
+    L.xs = take((size_t)rows * (K / 128) * 4);
+    L.total = o;
+    L.rows = rows;
+    return L;
+}
+
+static int check_dense_dims(int T, int K, int N) {
+    if (T < 0 || K <= 0 || N <= 0) return PM_ERR_INVALID;
+    if (K % 128 != 0 || N % 256 != 0 || (long)T * (K > N ? K : N) > (1L << 34) || T > (1 << 30))
+        return PM_ERR_SHAPE;
+    return PM_OK;
+}
+
+size_t pm_fp8_linear_workspace_bytes(int T, int K, int N) {
+    if (check_dense_dims(T, K, N) != PM_OK) return 0;
+    return dense_layout_of(T, K).total;
+}
+
+int pm_fp8_linear(const void* x, const uint8_t* w, const float* w_s, int T, int K, int N, void* out,
+                  void* workspace, size_t workspace_bytes, pm_stream_t stream) {
+    int st = check_dense_dims(T, K, N);
+    if (st != PM_OK) return st;
+    if (T == 0) return PM_OK;
+    if (!x || !w || !w_s || !out || !workspace) return PM_ERR_INVALID;
+    if (!a16(x) || !a16(w) || !a16(out) || !a16(workspace)) return PM_ERR_ALIGN;
+    const DenseLayout L = dense_layout_of(T, K);
+    if (workspace_bytes < L.total) return PM_ERR_WORKSPACE;
+    DeviceInfo d;
+    st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    int32_t* status = reinterpret_cast<int32_t*>(ws + L.status);
+    float* ones = reinterpret_cast<float*>(ws + L.ones);
+    int32_t* expert_ids = reinterpret_cast<int32_t*>(ws + L.expert_ids);
+    int32_t* npp = reinterpret_cast<int32_t*>(ws + L.npp);
+    uint8_t* xq = ws + L.xq;
+    float* xs = reinterpret_cast<float*>(ws + L.xs);
+    if (cudaMemsetAsync(status, 0, 4 * sizeof(int32_t), s) != cudaSuccess) return PM_ERR_CUDA;
+    if (launch_dense_plan(T, ones, expert_ids, npp, d.sms, s) != cudaSuccess) return PM_ERR_CUDA;
+    if (launch_quant_fp8(x, T, K, 1, nullptr, xq, xs, s) != cudaSuccess) return PM_ERR_CUDA;
+    CUtensorMap ta, tb;
+    if (!encode_tmap_2d_u8(&ta, xq, (uint64_t)K, (uint64_t)L.rows, (uint64_t)K, 128, 128) ||
+        !encode_tmap_2d_u8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, 128, 128))
+        return PM_ERR_CUDA;
+    GemmArgs g = gemm_args_common(xs, w_s, expert_ids, npp, N, K, N / 256, L.rows, K, status);
+    g.sorted_ids = nullptr;  // row t is token t
+    g.topk_w = ones;
+    g.c3 = static_cast<__nv_bfloat16*>(out);
+    g.n_valid = T;
+    return cuda_status(launch_gemm_fp8(1, ta, tb, g, d.sms, s));
+}
+
 int pm_nvfp4_prepare(const uint8_t* w, const float* s, int E, int R, int C, uint8_t* packed, uint8_t* scales,
                      float* g, pm_stream_t stream) {
     if (E < 0 || R < 0 || C < 0) return PM_ERR_INVALID;

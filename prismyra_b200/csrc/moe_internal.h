@@ -55,6 +55,9 @@ cudaError_t launch_combine(const void* c3, const int32_t* row_of, int T, int k, 
 // expert's GEMMs (expert_ids[b] = 0 for the ceil(T/128) blocks, *num_post_pad = their slots).
 cudaError_t launch_shared_gate(const void* x, const void* w_sg, int T, int H, float* gate, int32_t* expert_ids,
                                int32_t* num_post_pad, int sms, cudaStream_t s);
+// The one-expert plan of a dense block-FP8 projection: expert_ids = 0, *num_post_pad, ones[t] = 1.
+cudaError_t launch_dense_plan(int T, float* ones, int32_t* expert_ids, int32_t* num_post_pad, int sms,
+                              cudaStream_t s);
 // dst[dst_index[i]] = src[i] for rows of row_bytes (multiple of 16) with the given byte strides.
 cudaError_t launch_scatter_rows(const void* src, int rows, int row_bytes, int src_stride, const int32_t* dst_index,
                                 void* dst, int dst_stride, cudaStream_t s);

@@ -10,13 +10,12 @@
 //   eff   = fp32(sf) / g
 //   x     = eff > 0 ? clamp(d / eff, -6, 6) : 0
 //   code  = first j minimising |(|x| - E2M1[j])|, | 8 if x < 0  (torch.argmin keeps the first minimum, so a tie
-//                                                               takes the smaller magnitude; computed as the
-//                                                               count of grid midpoints below |x|)
+//                                                               takes the smaller magnitude; computed from d
+//                                                               and per-group bounds, see e2m1_bounds)
 //
 // Launches: a zeroing of the per-matrix maxima, the maxima (byte-wise magnitude maxima of the e4m3 codes, then an
 // unsigned max on the bit patterns of non-negative floats -- exact and order-free), the global scales, and the
-// quantisation of every 16-element group (one thread per group, 16-byte loads).  The maxima pass streams the
-// weights at HBM speed; the quantisation is instruction-bound (an IEEE division per weight).
+// quantisation of every 16-element group (one thread per group, 16-byte loads, no division per weight).
 #include "moe_internal.h"
 #include "ptx.cuh"
 
@@ -92,12 +91,32 @@ __global__ void prep_global_kernel(float* __restrict__ g, int E) {
     g[m] = __fmul_rn(__frcp_rn(amax), 2688.0f);
 }
 
-// e2m1 magnitude code of a in [0, 6]: the number of midpoints of the e2m1 grid strictly below a.  This equals the
-// reference's first arg-min of |fl(a - grid[j])| (ties to the smaller magnitude) for every fp32 a in [0, 6];
-// the equality was checked exhaustively over all 1,086,324,737 such values.
-__device__ __forceinline__ uint32_t e2m1_magnitude(float a) {
-    return (uint32_t)(a > 0.25f) + (uint32_t)(a > 0.75f) + (uint32_t)(a > 1.25f) + (uint32_t)(a > 1.75f) +
-           (uint32_t)(a > 2.5f) + (uint32_t)(a > 3.5f) + (uint32_t)(a > 5.0f);
+// The e2m1 code needs x = fl(d / eff) only through "fl(|x|) > m_j" for the seven midpoints m_j of the e2m1 grid
+// (0.25 ... 5): the count of midpoints below |x| equals the reference's first arg-min of |fl(|x| - grid[j])|, ties
+// to the smaller magnitude (checked exhaustively over every fp32 value in [0, 6]).  Round-half-even keeps m_j (an
+// even mantissa) for quotients up to m_j + ulp(m_j)/2 =: B_j, so fl(|d| / eff) > m_j exactly when |d| > B_j * eff.
+// B_j * eff is exact in double (at most 49 significant bits), and F_j, the smallest float above it, turns the test
+// into |d| >= F_j: seven float comparisons per weight and no division (checked against the IEEE quotient on 14.4
+// million cases, every neighbour of every F_j included).
+__device__ __forceinline__ void e2m1_bounds(float eff, float F[7]) {
+    const double kB[7] = {0.25 + 0x1p-26, 0.75 + 0x1p-25, 1.25 + 0x1p-24, 1.75 + 0x1p-24,
+                          2.5 + 0x1p-23,  3.5 + 0x1p-23,  5.0 + 0x1p-22};
+#pragma unroll
+    for (int j = 0; j < 7; ++j) {
+        const double t = kB[j] * (double)eff;
+        float f = __double2float_ru(t);
+        if ((double)f == t) f = __int_as_float(__float_as_int(f) + 1);  // strictly above (f is finite and > 0)
+        F[j] = f;
+    }
+}
+
+// The count of bounds at or below |d| (the bounds ascend) by a three-step branchless binary search.
+__device__ __forceinline__ uint32_t e2m1_code(float d, const float F[7], bool live) {
+    const float a = fabsf(d);
+    const bool b2 = a >= F[3];
+    const bool b1 = a >= (b2 ? F[5] : F[1]);
+    const bool b0 = a >= (b2 ? (b1 ? F[6] : F[4]) : (b1 ? F[2] : F[0]));
+    return (b2 ? 4u : 0u) | (b1 ? 2u : 0u) | (b0 ? 1u : 0u) | (live && d < 0.0f ? 8u : 0u);
 }
 
 // One thread per 16-element group of the stacked [E * R, C] matrix (matrix m = row / R).
@@ -115,14 +134,25 @@ __global__ void __launch_bounds__(256) prep_quant_kernel(const uint8_t* __restri
         const float scale = fminf(__fmul_rn(__fdiv_rn(amax, 6.0f), gm), 448.0f);
         const __nv_fp8_storage_t sbyte = __nv_cvt_float_to_fp8(scale, __NV_SATFINITE, __NV_E4M3);
         const float eff = __fdiv_rn(e4m3_to_f32(sbyte), gm);
+        // eff == 0 (a zero scale): every x is 0, so every code is 0 -- bounds at +inf, no sign
+        const bool live = eff > 0.0f;
+        float F[7];
+        if (live) {
+            e2m1_bounds(eff, F);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 7; ++j) F[j] = __int_as_float(0x7f800000);
+        }
         const uint32_t words[4] = {q.x, q.y, q.z, q.w};
         uint32_t out[2] = {0u, 0u};
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const float d = __fmul_rn(e4m3_to_f32((words[j / 4] >> (8 * (j % 4))) & 0xffu), sb);
-            const float x = eff > 0.0f ? fminf(fmaxf(__fdiv_rn(d, eff), -6.0f), 6.0f) : 0.0f;
-            const uint32_t code = e2m1_magnitude(fabsf(x)) | (x < 0.0f ? 8u : 0u);
-            out[j / 8] |= code << (4 * (j % 8));
+        for (int p = 0; p < 8; ++p) {
+            const __half2_raw h2 = __nv_cvt_fp8x2_to_halfraw2(
+                static_cast<__nv_fp8x2_storage_t>((words[p / 2] >> (16 * (p % 2))) & 0xffffu), __NV_E4M3);
+            const float2 v = __half22float2(__half2(h2));
+            const uint32_t c0 = e2m1_code(__fmul_rn(v.x, sb), F, live);
+            const uint32_t c1 = e2m1_code(__fmul_rn(v.y, sb), F, live);
+            out[p / 4] |= (c0 | (c1 << 4)) << (8 * (p % 4));
         }
         *reinterpret_cast<uint2*>(packed + i * 8) = make_uint2(out[0], out[1]);
         sf[i] = static_cast<uint8_t>(sbyte);

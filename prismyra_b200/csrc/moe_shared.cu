@@ -41,7 +41,27 @@ __global__ void __launch_bounds__(256) shared_gate_kernel(const __nv_bfloat16* _
     }
 }
 
+// The one-expert plan of a dense projection run on the grouped GEMMs: expert_ids[b] = 0 for the ceil(T/128)
+// blocks, *num_post_pad = their slots, and a row weight of exactly 1 for every token (bf16(acc * 1) = bf16(acc)).
+__global__ void __launch_bounds__(256) dense_plan_kernel(int T, float* __restrict__ ones,
+                                                         int32_t* __restrict__ expert_ids,
+                                                         int32_t* __restrict__ num_post_pad) {
+    const long gtid = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long stride = (long)gridDim.x * blockDim.x;
+    const int blocks = (T + kBlockM - 1) / kBlockM;
+    for (long b = gtid; b < blocks; b += stride) expert_ids[b] = 0;
+    for (long t = gtid; t < T; t += stride) ones[t] = 1.0f;
+    if (gtid == 0) *num_post_pad = blocks * kBlockM;
+}
+
 }  // namespace
+
+cudaError_t launch_dense_plan(int T, float* ones, int32_t* expert_ids, int32_t* num_post_pad, int sms,
+                              cudaStream_t s) {
+    const int blocks = (int)std::min<long>(((long)T + 255) / 256 + 1, (long)sms * 4);
+    dense_plan_kernel<<<blocks, 256, 0, s>>>(T, ones, expert_ids, num_post_pad);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_shared_gate(const void* x, const void* w_sg, int T, int H, float* gate, int32_t* expert_ids,
                                int32_t* num_post_pad, int sms, cudaStream_t s) {

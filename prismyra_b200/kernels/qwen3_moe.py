@@ -134,6 +134,55 @@ class FusedExperts(nn.Module):
         return (routed + shared).reshape(shape)
 
 
+class Fp8Linear(nn.Module):
+    """A block-quantised projection on the library's kernel, wrapping the original module's weights (the reference's
+    Fp8Linear, prismyra/kernels/qwen3_moe.py:211-230): per-token-group FP8 quantisation of the input and the
+    block-scaled matmul, bf16 out.  The weight stays (out, in); its scale_inv widens to fp32."""
+
+    def __init__(self, inner: nn.Module):
+        super().__init__()
+        t = _fp8_linear(inner)
+        if t is None:
+            raise AdapterError("Fp8Linear needs a bias-free e4m3 weight with 128x128 fp32 block scales")
+        self.inner = inner
+        self.weight = inner.weight
+        self.register_buffer("scale", t[1].detach().to(torch.float32).contiguous(), persistent=False)
+        self.out_features, self.in_features = inner.weight.shape
+        if self.out_features % 256 or self.in_features % 128:
+            raise AdapterError(f"Fp8Linear on the B200 kernel needs out % 256 == 0 and in % 128 == 0, got "
+                               f"{self.out_features} x {self.in_features}")
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return ops.fp8_linear(x.contiguous(), self.weight.detach(), self.scale)
+
+
+class FusedDenseProjection(nn.Module):
+    """One block-FP8 matmul for several sibling projections of the same input, split back into their own widths (the
+    reference's _FusedDenseProjection, qwen3_moe.py:233-262).  Every sibling's width is a multiple of 128, so no
+    weight block straddles a seam and each output keeps its own per-row reduction: the split outputs equal the
+    separate calls bit for bit."""
+
+    def __init__(self, parts: list):
+        super().__init__()
+        if not parts or any(not isinstance(p, Fp8Linear) for p in parts):
+            raise AdapterError("FusedDenseProjection needs Fp8Linear parts")
+        if any(p.in_features != parts[0].in_features or p.out_features % 128 for p in parts):
+            raise AdapterError("FusedDenseProjection needs one input width and output widths that are multiples "
+                               "of 128")
+        self.sizes = [p.out_features for p in parts]
+        self.in_features = parts[0].in_features
+        self.out_features = sum(self.sizes)
+        if self.out_features % 256:
+            raise AdapterError("FusedDenseProjection needs a combined output width that is a multiple of 256")
+        self.register_buffer("weight", torch.cat([p.weight.detach() for p in parts], 0).contiguous(),
+                             persistent=False)
+        self.register_buffer("scale", torch.cat([p.scale for p in parts], 0).contiguous(), persistent=False)
+
+    def forward(self, x: torch.Tensor) -> tuple:
+        out = ops.fp8_linear(x.contiguous(), self.weight, self.scale)
+        return torch.split(out, self.sizes, dim=-1)
+
+
 def _swap_children(root: nn.Module, class_name: str, make) -> int:
     count = 0
     for parent in list(root.modules()):

@@ -138,6 +138,30 @@ def _shared_checks(x, w_sg, w13, w13_s, w2, w2_s):
     return T, H, Is
 
 
+def fp8_linear(x: torch.Tensor, w: torch.Tensor, w_s: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """A dense block-FP8 projection x [..., K] bf16 -> [..., N] bf16 with w e4m3 [N, K] and fp32 block multipliers
+    [N/128, K/128] (the reference's Fp8Linear, qwen3_moe.py:211-230)."""
+    _cuda(x, "x", torch.bfloat16)
+    N, K = w.shape
+    _need(x.shape[-1] == K, f"x must end in K={K}")
+    _cuda(w, "w", (FP8, torch.uint8), (N, K))
+    _cuda(w_s, "w_s", torch.float32, (N // 128, K // 128))
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, K)
+    T = x2.shape[0]
+    if out is None:
+        out = torch.empty(*lead, N, dtype=torch.bfloat16, device=x.device)
+    _cuda(out, "out", torch.bfloat16)
+    _need(out.numel() == T * N, f"out must hold {T} x {N} values")
+    if T == 0:
+        return out
+    n = _lib.load().pm_fp8_linear_workspace_bytes(T, K, N)
+    _need(n > 0, f"unsupported projection shape T={T} K={K} N={N} (need K % 128 == 0, N % 256 == 0)")
+    ws = POOL.get(x.device, n, "dense")
+    _lib.call("pm_fp8_linear", _p(x2), _p(_u8(w)), _p(w_s), T, K, N, _p(out), _p(ws), n, _stream(x.device))
+    return out
+
+
 def shared_fp8(x: torch.Tensor, w_sg: torch.Tensor, w13: torch.Tensor, w13_s: torch.Tensor, w2: torch.Tensor,
                w2_s: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """The shared expert on block-FP8 weights: sigmoid(x . w_sg) * down(silu(gate x) * up x) -> bf16 [T, H]
