@@ -3,7 +3,8 @@
 // to bf16 again.  One warp per token: lane l accumulates the 8-column chunks l, l+32, ... in ascending order in
 // fp32, then a fixed xor-shuffle tree adds the 32 lane sums, so a token's gate never depends on the other rows.
 // The same launch writes the one-expert plan the shared expert's grouped GEMMs run on (every 128-row block
-// belongs to expert 0).
+// belongs to expert 0).  A dense block-FP8 projection (the reference's Fp8Linear) runs on the same plan with unit
+// row weights (dense_plan_kernel).
 #include "moe_internal.h"
 #include "ptx.cuh"
 
