@@ -564,7 +564,8 @@ int pm_moe_block_fp8(const void* x, const void* router_w, const void* logits, co
     // leave most SMs idle, and the final sum waits for it.
     SideStream* side = side_stream();
     if (side == nullptr) return PM_ERR_CUDA;
-    if (cudaEventRecord(side->fork, s) != cudaSuccess || cudaStreamWaitEvent(side->stream, side->fork, 0) != cudaSuccess)
+    if (cudaEventRecord(side->fork, s) != cudaSuccess ||
+        cudaStreamWaitEvent(side->stream, side->fork, 0) != cudaSuccess)
         return PM_ERR_CUDA;
     st = shared_fp8_run(x, w_sg, sw13, sw13_s, sw2, sw2_s, T, H, Is, sws + L.out, L, sws, status, d, side->stream);
     if (st != PM_OK) return st;

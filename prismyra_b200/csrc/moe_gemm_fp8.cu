@@ -135,6 +135,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = tail->tmem_base;
+    pdl_wait();
+    pdl_trigger();
 
     const int KB = args.K / kBK;
     const int num_tiles = (*args.num_post_pad / kBM) * args.n_tiles;
@@ -414,10 +416,14 @@ cudaError_t launch_gemm_fp8(int mode, const CUtensorMap& tm_a, const CUtensorMap
     }
     const int grid = args.max_tiles < num_sms ? (args.max_tiles > 0 ? args.max_tiles : 1) : num_sms;
     switch (variant) {
-        case 0: moe_gemm_fp8_kernel<0><<<grid, kThreads, smem_bytes<0>(), s>>>(tm_a, tm_b, args); break;
-        case 1: moe_gemm_fp8_kernel<1><<<grid, kThreads, smem_bytes<1>(), s>>>(tm_a, tm_b, args); break;
-        case 2: moe_gemm_fp8_kernel<1, kEpiRoundFirst><<<grid, kThreads, smem_bytes<1>(), s>>>(tm_a, tm_b, args); break;
-        default: moe_gemm_fp8_kernel<1, kEpiDstRows><<<grid, kThreads, smem_bytes<1>(), s>>>(tm_a, tm_b, args);
+        case 0: PM_TRY(launch_pdl(moe_gemm_fp8_kernel<0>, dim3(grid), dim3(kThreads), smem_bytes<0>(), s, tm_a, tm_b,
+                                  args)); break;
+        case 1: PM_TRY(launch_pdl(moe_gemm_fp8_kernel<1>, dim3(grid), dim3(kThreads), smem_bytes<1>(), s, tm_a, tm_b,
+                                  args)); break;
+        case 2: PM_TRY(launch_pdl(moe_gemm_fp8_kernel<1, kEpiRoundFirst>, dim3(grid), dim3(kThreads), smem_bytes<1>(),
+                                  s, tm_a, tm_b, args)); break;
+        default: PM_TRY(launch_pdl(moe_gemm_fp8_kernel<1, kEpiDstRows>, dim3(grid), dim3(kThreads), smem_bytes<1>(),
+                                   s, tm_a, tm_b, args));
     }
     return cudaGetLastError();
 }

@@ -247,6 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_alloc(smem_u32(&tail->tmem_base), kTmemCols);
         tmem_relinquish();
     }
+    pdl_wait();
     const int blocks = *args.num_post_pad / 128;
     const int num_units = 2 * blocks * args.n_tiles;
     // every thread stages a share of this CTA's unit table (one round of loads in parallel)
@@ -261,6 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = tail->tmem_base;
+    pdl_trigger();  // after this CTA's TMEM allocation (a dependent CTA could otherwise take the columns first)
 
     if (warp < kEpiWarp0) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 40;" ::: "memory");
@@ -417,9 +419,9 @@ cudaError_t launch_gemm_fp8_small(int mode, const CUtensorMap& tm_tok, const CUt
     const int units = 2 * args.max_units;  // two halves per block and column tile
     const int grid = units < num_sms ? (units > 0 ? units : 1) : num_sms;
     if (mode == 0)
-        moe_gemm_fp8_small_kernel<0><<<grid, kThreads, smem, s>>>(tm_tok, tm_w, args);
+        PM_TRY(launch_pdl(moe_gemm_fp8_small_kernel<0>, dim3(grid), dim3(kThreads), smem, s, tm_tok, tm_w, args));
     else
-        moe_gemm_fp8_small_kernel<1><<<grid, kThreads, smem, s>>>(tm_tok, tm_w, args);
+        PM_TRY(launch_pdl(moe_gemm_fp8_small_kernel<1>, dim3(grid), dim3(kThreads), smem, s, tm_tok, tm_w, args));
     return cudaGetLastError();
 }
 

@@ -7,7 +7,35 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace pm {
+
+// Returns a failed cudaError_t from the enclosing function.
+#define PM_TRY(expr)                                 \
+    do {                                             \
+        const cudaError_t pm_err_ = (expr);          \
+        if (pm_err_ != cudaSuccess) return pm_err_;  \
+    } while (0)
+
+// Launches a kernel of the forward chain with programmatic stream serialisation: it may be scheduled while the
+// previous kernel of the stream finishes, and waits for it (pdl_wait) before touching global memory.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 
 constexpr int kBlockM = 128;  // rows of one GEMM tile == the alignment block of the expert permutation
 constexpr int kMaxExperts = 256;

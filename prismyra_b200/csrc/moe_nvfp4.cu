@@ -55,6 +55,8 @@ __device__ __forceinline__ uint8_t nvfp4_group(const float* v, float gs, uint32_
 __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, int T, int H, int k,
                                                           const int32_t* __restrict__ slot_of, float gs,
                                                           uint8_t* __restrict__ a_q, uint8_t* __restrict__ a_sf) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x >> 5);
     const int chunks = H / 64;
@@ -187,6 +189,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tail->tmem_base;
+    pdl_wait();
+    pdl_trigger();
     const int KB = args.K / kBKe;
     const int kchunks = args.K / 64;
     const int nb_total = args.n_total / 128;
@@ -366,8 +370,8 @@ cudaError_t launch_quant_nvfp4(const void* x, int T, int H, int k, const int32_t
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int blocks = min(cdiv(T, 8), sms * 8);
-    quant_nvfp4_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), T, H, k, slot_of, gs, a_q,
-                                               a_sf);
+    PM_TRY(launch_pdl(quant_nvfp4_kernel, dim3(blocks), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(x), T, H,
+                      k, slot_of, gs, a_q, a_sf));
     return cudaGetLastError();
 }
 
@@ -388,9 +392,9 @@ cudaError_t launch_gemm_nvfp4(int mode, const CUtensorMap& tm_a, const CUtensorM
     }
     const int grid = args.max_tiles < num_sms ? (args.max_tiles > 0 ? args.max_tiles : 1) : num_sms;
     if (mode == 0)
-        moe_gemm_nvfp4_kernel<0><<<grid, kThreads, nv_smem<0>(), s>>>(tm_a, tm_b, args);
+        PM_TRY(launch_pdl(moe_gemm_nvfp4_kernel<0>, dim3(grid), dim3(kThreads), nv_smem<0>(), s, tm_a, tm_b, args));
     else
-        moe_gemm_nvfp4_kernel<1><<<grid, kThreads, nv_smem<1>(), s>>>(tm_a, tm_b, args);
+        PM_TRY(launch_pdl(moe_gemm_nvfp4_kernel<1>, dim3(grid), dim3(kThreads), nv_smem<1>(), s, tm_a, tm_b, args));
     return cudaGetLastError();
 }
 

@@ -17,6 +17,8 @@ namespace {
 __global__ void __launch_bounds__(256) quant_fp8_kernel(const __nv_bfloat16* __restrict__ x, int T, int H, int k,
                                                         const int32_t* __restrict__ slot_of,
                                                         uint8_t* __restrict__ x_q, float* __restrict__ x_s) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31, sub = lane & 15;
     const int G = H / 128;
     const long items = (long)T * G;
@@ -68,6 +70,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
                                                       const int32_t* __restrict__ row_of, int T, int k, int H,
                                                       const __nv_bfloat16* __restrict__ add,
                                                       __nv_bfloat16* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const long total = (long)T * (H / 8);
     for (long q = (long)blockIdx.x * blockDim.x + threadIdx.x; q < total; q += (long)gridDim.x * blockDim.x) {
         const long t = q / (H / 8);
@@ -106,7 +110,8 @@ cudaError_t launch_quant_fp8(const void* x, int T, int H, int k, const int32_t* 
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const long pairs = ((long)T * (H / 128) + 1) / 2;  // one warp per two (token, group) items
     const int blocks = (int)min((pairs + 7) / 8, (long)sms * 16);
-    quant_fp8_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), T, H, k, slot_of, x_q, x_s);
+    PM_TRY(launch_pdl(quant_fp8_kernel, dim3(blocks), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(x), T, H, k,
+                      slot_of, x_q, x_s));
     return cudaGetLastError();
 }
 
@@ -150,8 +155,8 @@ cudaError_t launch_combine(const void* c3, const int32_t* row_of, int T, int k, 
     const long total = (long)T * (H / 8);
     const long want = (total + 255) / 256;
     const int blocks = (int)(want < (long)sms * 16 ? want : (long)sms * 16);
-    combine_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(c3), row_of, T, k, H,
-                                          static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out));
+    PM_TRY(launch_pdl(combine_kernel, dim3(blocks), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(c3), row_of, T,
+                      k, H, static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out)));
     return cudaGetLastError();
 }
 

@@ -84,6 +84,8 @@ __device__ __forceinline__ void warp_topk(const float (&v)[kMaxEPT], int E, int 
 __global__ void __launch_bounds__(256) topk_kernel(const __nv_bfloat16* __restrict__ logits,
                                                    const float* __restrict__ bias, int T, int E, int k,
                                                    float* __restrict__ topk_w, int32_t* __restrict__ topk_ids) {
+    pdl_wait();
+    pdl_trigger();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= T) return;
@@ -101,7 +103,10 @@ __global__ void __launch_bounds__(256) topk_kernel(const __nv_bfloat16* __restri
 __global__ void __launch_bounds__(256) topk_partials_kernel(const float* __restrict__ part, int chunks,
                                                             __nv_bfloat16* __restrict__ logits,
                                                             const float* __restrict__ bias, int T, int E, int k,
-                                                            float* __restrict__ topk_w, int32_t* __restrict__ topk_ids) {
+                                                            float* __restrict__ topk_w,
+                                                            int32_t* __restrict__ topk_ids) {
+    pdl_wait();
+    pdl_trigger();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= T) return;
@@ -145,6 +150,8 @@ __global__ void __launch_bounds__(256) topk_partials_kernel(const float* __restr
 // Pass 1: per-chunk expert histogram.
 __global__ void __launch_bounds__(256) align_count_kernel(const int32_t* __restrict__ ids, int n, int E, int chunk,
                                                           int32_t* __restrict__ counts) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ int32_t cnt[];
     for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
@@ -175,6 +182,8 @@ __global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __res
                                                             int32_t* __restrict__ num_post_pad,
                                                             int32_t* __restrict__ expert_off,
                                                             int32_t* __restrict__ slot_of) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ int32_t sm[];
     int32_t* base = sm;            // [E]  next slot of each expert for this chunk
     int32_t* pad = sm + E;         // [E]  padded totals, then padded offsets
@@ -327,7 +336,8 @@ cudaError_t launch_topk(const void* logits, const float* bias, int T, int E, int
                         cudaStream_t s) {
     if (T == 0) return cudaSuccess;
     const int blocks = cdiv((long)T * 32, 256);
-    topk_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(logits), bias, T, E, k, topk_w, topk_ids);
+    PM_TRY(launch_pdl(topk_kernel, dim3(blocks), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(logits), bias, T,
+                      E, k, topk_w, topk_ids));
     return cudaGetLastError();
 }
 
@@ -335,8 +345,8 @@ cudaError_t launch_topk_partials(const float* part, int chunks, void* logits, co
                                  float* topk_w, int32_t* topk_ids, cudaStream_t s) {
     if (T == 0) return cudaSuccess;
     const int blocks = cdiv((long)T * 32, 256);
-    topk_partials_kernel<<<blocks, 256, 0, s>>>(part, chunks, static_cast<__nv_bfloat16*>(logits), bias, T, E, k,
-                                                topk_w, topk_ids);
+    PM_TRY(launch_pdl(topk_partials_kernel, dim3(blocks), dim3(256), 0, s, part, chunks,
+                      static_cast<__nv_bfloat16*>(logits), bias, T, E, k, topk_w, topk_ids));
     return cudaGetLastError();
 }
 
@@ -346,15 +356,16 @@ cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int3
     const int chunk = align_chunk(n);
     const int nchunks = align_chunks(n);
     if (nchunks > 1) {
-        align_count_kernel<<<nchunks, 256, sizeof(int32_t) * E, s>>>(ids, n, E, chunk, counts);
+        PM_TRY(launch_pdl(align_count_kernel, dim3(nchunks), dim3(256), sizeof(int32_t) * E, s, ids, n, E, chunk,
+                          counts));
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     // a single chunk is scattered by CTA 0; the extra CTAs only share the padding writes
     const int grid = nchunks > 1 ? nchunks : max(1, min(16, E / 8));
-    align_scatter_kernel<<<grid, 256, sizeof(int32_t) * 11 * E, s>>>(
-        ids, n, E, chunk, nchunks, nchunks > 1 ? counts : nullptr, sorted, expert_ids, num_post_pad, expert_off,
-        slot_of);
+    PM_TRY(launch_pdl(align_scatter_kernel, dim3(grid), dim3(256), sizeof(int32_t) * 11 * E, s, ids, n, E, chunk,
+                      nchunks, nchunks > 1 ? counts : nullptr, sorted, expert_ids, num_post_pad, expert_off,
+                      slot_of));
     return cudaGetLastError();
 }
 

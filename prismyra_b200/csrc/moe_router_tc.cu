@@ -90,6 +90,8 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tail->tmem_base;
+    pdl_wait();
+    pdl_trigger();
 
     if (warp == 0 && lane == 0) {
         int stage = 0;
@@ -224,19 +226,19 @@ cudaError_t launch_router_topk(const void* x, const void* w, const float* bias, 
     const int chunks = H / kChunkK;
     if (part != nullptr && router_split_bytes(T, H, E) > 0) {
         const dim3 grid(cdiv(T, kTM), cdiv(E, kTN), chunks);
-        router_tc_kernel<kStepsPerChunk, true><<<grid, kRouterThreads, router_smem<kStepsPerChunk>(), s>>>(tx, tw, T, H, E, lg,
-                                                                                              part, err);
+        PM_TRY(launch_pdl(router_tc_kernel<kStepsPerChunk, true>, dim3(grid), dim3(kRouterThreads),
+                          router_smem<kStepsPerChunk>(), s, tx, tw, T, H, E, lg, part, err));
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         return launch_topk_partials(part, chunks, lg, bias, T, E, k, topk_w, topk_ids, s);
     }
     const dim3 grid(cdiv(T, kTM), cdiv(E, kTN));
     if ((long)grid.x * grid.y <= sms)
-        router_tc_kernel<kTStagesDeep, false><<<grid, kRouterThreads, router_smem<kTStagesDeep>(), s>>>(tx, tw, T, H, E, lg,
-                                                                                           nullptr, err);
+        PM_TRY(launch_pdl(router_tc_kernel<kTStagesDeep, false>, dim3(grid), dim3(kRouterThreads),
+                          router_smem<kTStagesDeep>(), s, tx, tw, T, H, E, lg, nullptr, err));
     else
-        router_tc_kernel<kTStagesWide, false><<<grid, kRouterThreads, router_smem<kTStagesWide>(), s>>>(tx, tw, T, H, E, lg,
-                                                                                           nullptr, err);
+        PM_TRY(launch_pdl(router_tc_kernel<kTStagesWide, false>, dim3(grid), dim3(kRouterThreads),
+                          router_smem<kTStagesWide>(), s, tx, tw, T, H, E, lg, nullptr, err));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     return launch_topk(logits, bias, T, E, k, topk_w, topk_ids, s);

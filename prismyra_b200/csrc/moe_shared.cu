@@ -15,6 +15,8 @@ __global__ void __launch_bounds__(256) shared_gate_kernel(const __nv_bfloat16* _
                                                           const __nv_bfloat16* __restrict__ w_sg, int T, int H,
                                                           float* __restrict__ gate, int32_t* __restrict__ expert_ids,
                                                           int32_t* __restrict__ num_post_pad) {
+    pdl_wait();
+    pdl_trigger();
     const long gtid = (long)blockIdx.x * blockDim.x + threadIdx.x;
     const int blocks = (T + kBlockM - 1) / kBlockM;
     for (long b = gtid; b < blocks; b += (long)gridDim.x * blockDim.x) expert_ids[b] = 0;
@@ -47,6 +49,8 @@ __global__ void __launch_bounds__(256) shared_gate_kernel(const __nv_bfloat16* _
 __global__ void __launch_bounds__(256) dense_plan_kernel(int T, float* __restrict__ ones,
                                                          int32_t* __restrict__ expert_ids,
                                                          int32_t* __restrict__ num_post_pad) {
+    pdl_wait();
+    pdl_trigger();
     const long gtid = (long)blockIdx.x * blockDim.x + threadIdx.x;
     const long stride = (long)gridDim.x * blockDim.x;
     const int blocks = (T + kBlockM - 1) / kBlockM;
@@ -60,7 +64,7 @@ __global__ void __launch_bounds__(256) dense_plan_kernel(int T, float* __restric
 cudaError_t launch_dense_plan(int T, float* ones, int32_t* expert_ids, int32_t* num_post_pad, int sms,
                               cudaStream_t s) {
     const int blocks = (int)std::min<long>(((long)T + 255) / 256 + 1, (long)sms * 4);
-    dense_plan_kernel<<<blocks, 256, 0, s>>>(T, ones, expert_ids, num_post_pad);
+    PM_TRY(launch_pdl(dense_plan_kernel, dim3(blocks), dim3(256), 0, s, T, ones, expert_ids, num_post_pad));
     return cudaGetLastError();
 }
 
@@ -68,9 +72,8 @@ cudaError_t launch_shared_gate(const void* x, const void* w_sg, int T, int H, fl
                                int32_t* num_post_pad, int sms, cudaStream_t s) {
     const long warps = T > 0 ? T : 1;
     const int blocks = (int)std::min<long>((warps + 7) / 8, (long)sms * 16);
-    shared_gate_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
-                                              static_cast<const __nv_bfloat16*>(w_sg), T, H, gate, expert_ids,
-                                              num_post_pad);
+    PM_TRY(launch_pdl(shared_gate_kernel, dim3(blocks), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(x),
+                      static_cast<const __nv_bfloat16*>(w_sg), T, H, gate, expert_ids, num_post_pad));
     return cudaGetLastError();
 }
 

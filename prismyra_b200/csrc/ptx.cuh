@@ -60,6 +60,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Wait for the phase with the given parity to complete.  Returns false (and raises *abort) on timeout, or
 // immediately once another thread of the CTA has raised *abort.
+// Programmatic dependent launch: pdl_wait() returns once the previous kernel of the stream has completed and its
+// memory is visible (a no-op when the kernel was launched without the programmatic-serialisation attribute);
+// pdl_trigger() lets the next kernel be scheduled (its own pdl_wait still waits for this kernel to complete).
+// Every kernel of the forward chain calls both before its first global memory access, so no kernel reads or
+// writes global memory while its predecessor runs, and completion stays transitive along the chain.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
