@@ -18,6 +18,8 @@
 // (warps 2-3 idle); warpgroups 1 and 2 (warps 4-11) promote and run the epilogue.  Epilogue warp w reads TMEM
 // lanes 32*(w%4).. and one half of the tile's columns.  Registers are rebalanced with setmaxnreg: 40 for
 // warpgroup 0 and 232 for the epilogue warpgroups (40*128 + 232*256 = 64512 = 168 * 384, the launch's total).
+#include <atomic>
+
 #include "moe_internal.h"
 #include "ptx.cuh"
 
@@ -395,11 +397,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 cudaError_t launch_gemm_fp8(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, const GemmArgs& args,
                             int num_sms, cudaStream_t s) {
     // variant 0: gate_up; 1..3: down with the plain, round-first or per-row-destination epilogue
-    static bool configured[64][4] = {};
+    static std::atomic<bool> configured[64][4];  // zero-initialised: false
     const int variant = mode == 0 ? 0 : (args.dst_rows != nullptr ? 3 : (args.round_first ? 2 : 1));
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !configured[dev][variant]) {
+    if (dev < 64 && !configured[dev][variant].load(std::memory_order_acquire)) {
         cudaError_t e;
         switch (variant) {
             case 0: e = cudaFuncSetAttribute(moe_gemm_fp8_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -412,7 +414,7 @@ cudaError_t launch_gemm_fp8(int mode, const CUtensorMap& tm_a, const CUtensorMap
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<1>());
         }
         if (e != cudaSuccess) return e;
-        configured[dev][variant] = true;
+        configured[dev][variant].store(true, std::memory_order_release);
     }
     const int grid = args.max_tiles < num_sms ? (args.max_tiles > 0 ? args.max_tiles : 1) : num_sms;
     switch (variant) {

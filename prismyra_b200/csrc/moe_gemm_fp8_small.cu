@@ -21,6 +21,8 @@
 // rows) and token columns of half (w-4)/4 of the unit.  TMEM holds a ring of K-block accumulators (4 of 128
 // columns for gate_up: gate at +0, up at +64; 8 of 64 for down), so the MMA runs several K blocks ahead of the
 // promotion and through a unit's epilogue.  Every wait is bounded.
+#include <atomic>
+
 #include "moe_internal.h"
 #include "ptx.cuh"
 
@@ -405,16 +407,16 @@ cudaError_t launch_gemm_fp8_small(int mode, const CUtensorMap& tm_tok, const CUt
     while (stages > 2 && (mode == 0 ? small_smem<0>(stages, KB) : small_smem<1>(stages, KB)) > limit) --stages;
     args.stages = stages;
     const size_t smem = mode == 0 ? small_smem<0>(stages, KB) : small_smem<1>(stages, KB);
-    static bool configured[64][2] = {};
+    static std::atomic<bool> configured[64][2];  // zero-initialised: false
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 64 || !configured[dev][mode]) {
+    if (dev >= 64 || !configured[dev][mode].load(std::memory_order_acquire)) {
         cudaError_t e = mode == 0 ? cudaFuncSetAttribute(moe_gemm_fp8_small_kernel<0>,
                                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)limit)
                                   : cudaFuncSetAttribute(moe_gemm_fp8_small_kernel<1>,
                                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)limit);
         if (e != cudaSuccess) return e;
-        if (dev < 64) configured[dev][mode] = true;
+        if (dev < 64) configured[dev][mode].store(true, std::memory_order_release);
     }
     const int units = 2 * args.max_units;  // two halves per block and column tile
     const int grid = units < num_sms ? (units > 0 ? units : 1) : num_sms;

@@ -15,6 +15,8 @@
 // tcgen05.cp.32x128b.warpx4 moves one block into 4 TMEM columns (replicated over the 4 lane quarters).
 #include <cuda_fp4.h>
 
+#include <atomic>
+
 #include "moe_internal.h"
 #include "ptx.cuh"
 
@@ -377,10 +379,10 @@ cudaError_t launch_quant_nvfp4(const void* x, int T, int H, int k, const int32_t
 
 cudaError_t launch_gemm_nvfp4(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, const NvGemmArgs& args,
                               int num_sms, cudaStream_t s) {
-    static bool configured[64][2] = {};
+    static std::atomic<bool> configured[64][2];  // zero-initialised: false
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !configured[dev][mode]) {
+    if (dev < 64 && !configured[dev][mode].load(std::memory_order_acquire)) {
         cudaError_t e = mode == 0 ? cudaFuncSetAttribute(moe_gemm_nvfp4_kernel<0>,
                                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                          (int)nv_smem<0>())
@@ -388,7 +390,7 @@ cudaError_t launch_gemm_nvfp4(int mode, const CUtensorMap& tm_a, const CUtensorM
                                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                          (int)nv_smem<1>());
         if (e != cudaSuccess) return e;
-        configured[dev][mode] = true;
+        configured[dev][mode].store(true, std::memory_order_release);
     }
     const int grid = args.max_tiles < num_sms ? (args.max_tiles > 0 ? args.max_tiles : 1) : num_sms;
     if (mode == 0)

@@ -14,6 +14,8 @@
 //          SMs: each writes its P_c in fp32 and the top-k kernel adds the chunks in the same order, rounds,
 //          writes the logits and ranks.
 // Either way a row's result never depends on which rows share the call or which shape ran.
+#include <atomic>
+
 #include "moe_internal.h"
 #include "ptx.cuh"
 
@@ -211,16 +213,16 @@ cudaError_t launch_router_topk(const void* x, const void* w, const float* bias, 
         !encode_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H, (uint64_t)E, (uint64_t)H * 2, kTK,
                         kTN))
         return cudaErrorInvalidValue;
-    static bool configured[64] = {false};
+    static std::atomic<bool> configured[64];  // zero-initialised: false
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (dev < 64 && !configured[dev]) {
+    if (dev < 64 && !configured[dev].load(std::memory_order_acquire)) {
         cudaError_t e = configure_router<kTStagesDeep, false>();
         if (e == cudaSuccess) e = configure_router<kTStagesWide, false>();
         if (e == cudaSuccess) e = configure_router<kStepsPerChunk, true>();
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        configured[dev].store(true, std::memory_order_release);
     }
     __nv_bfloat16* lg = static_cast<__nv_bfloat16*>(logits);
     const int chunks = H / kChunkK;

@@ -124,3 +124,70 @@ def test_fp8_model_without_a_device_is_skipped():
                      num_experts_per_tok=4, hidden_size=256, moe_intermediate_size=128)
     applied = kernels.apply(model, cfg)
     assert applied.skipped == ["no CUDA device: the B200 kernels need one"]
+
+
+def _fp8_linear_module(out_f, in_f, scale_shape=None):
+    from transformers.integrations.finegrained_fp8 import FP8Linear
+
+    m = FP8Linear(in_f, out_f, block_size=(128, 128))
+    m.weight = nn.Parameter(torch.zeros(out_f, in_f).to(torch.float8_e4m3fn), requires_grad=False)
+    m.weight_scale_inv = nn.Parameter(torch.ones(scale_shape or (out_f // 128, in_f // 128)), requires_grad=False)
+    return m
+
+
+class _SharedMLP(nn.Module):
+    def __init__(self, H, Is, fp8=True):
+        super().__init__()
+        from transformers.activations import ACT2FN
+
+        if fp8:
+            self.gate_proj, self.up_proj = _fp8_linear_module(Is, H), _fp8_linear_module(Is, H)
+            self.down_proj = _fp8_linear_module(H, Is)
+        else:
+            self.gate_proj, self.up_proj = nn.Linear(H, Is, bias=False), nn.Linear(H, Is, bias=False)
+            self.down_proj = nn.Linear(Is, H, bias=False)
+        self.act_fn = ACT2FN["silu"]
+
+
+def _block_with_shared(fp8_shared=True, Is=128):
+    blk = Qwen3_5MoeSparseMoeBlock()
+    blk.shared_expert = _SharedMLP(256, Is, fp8_shared)
+    blk.shared_expert_gate = nn.Linear(256, 1, bias=False).to(torch.bfloat16)
+    return blk
+
+
+def test_fused_experts_runs_a_block_fp8_shared_expert_in_the_library_and_keeps_others():
+    """FusedExperts takes the shared expert into the library call only when its projections are bias-free
+    block-FP8 with a bf16 one-row gate; anything else stays the framework's module (built on CPU: construction
+    touches no device)."""
+    from prismyra_b200.kernels.qwen3_moe import FusedExperts
+
+    mod = FusedExperts(_block_with_shared(), 4)
+    assert mod.shared_fp8 is not None
+    w_sg, w13, s13, w2, s2 = mod.shared_fp8
+    assert w_sg.shape == (256,) and w13.shape == (256, 256) and s13.shape == (2, 2)
+    assert w2.shape == (256, 128) and s2.shape == (2, 1) and s13.dtype == torch.float32
+    assert FusedExperts(_block_with_shared(fp8_shared=False), 4).shared_fp8 is None
+    odd = _block_with_shared()
+    odd.shared_expert.act_fn = nn.GELU()
+    assert FusedExperts(odd, 4).shared_fp8 is None
+    biased = _block_with_shared()
+    biased.shared_expert.down_proj.bias = nn.Parameter(torch.zeros(256))
+    assert FusedExperts(biased, 4).shared_fp8 is None
+
+
+def test_dense_projection_modules_check_their_shapes():
+    from prismyra_b200.kernels.qwen3_moe import Fp8Linear, FusedDenseProjection
+
+    lin = Fp8Linear(_fp8_linear_module(512, 256))
+    assert (lin.out_features, lin.in_features) == (512, 256) and lin.scale.dtype == torch.float32
+    with pytest.raises(AdapterError):
+        Fp8Linear(_fp8_linear_module(384, 256))  # output width not a multiple of 256
+    with pytest.raises(AdapterError):
+        Fp8Linear(nn.Linear(256, 256, bias=False))  # not FP8
+    with pytest.raises(AdapterError):
+        Fp8Linear(_fp8_linear_module(256, 256, scale_shape=(1, 1)))  # per-tensor scale
+    fused = FusedDenseProjection([lin, Fp8Linear(_fp8_linear_module(256, 256))])
+    assert fused.sizes == [512, 256] and fused.weight.shape == (768, 256) and fused.scale.shape == (6, 2)
+    with pytest.raises(AdapterError):
+        FusedDenseProjection([lin, Fp8Linear(_fp8_linear_module(256, 512))])  # different input widths
