@@ -71,3 +71,38 @@ def test_captured_layer_replays_like_eager_calls(layer, T, which):
     torch.cuda.synchronize()
     assert torch.equal(out, eager2)
     del graph
+
+
+def test_two_lanes_on_two_threads_match_sequential_calls(layer):
+    """Two threads, each on its own stream, call the forward and the block concurrently (the reference's two
+    lanes, prismyra/kernels/qwen3_moe.py:277-279): every result equals the sequential call bit for bit (workspace
+    and side stream are per thread)."""
+    import threading
+
+    xs = [layer["x"][:700].contiguous(), layer["x2"][:900].contiguous()]
+    want = [(_forward(layer, x).clone(), _block(layer, x).clone()) for x in xs]
+    torch.cuda.synchronize()
+    got = [None, None]
+    errors = []
+
+    def lane(i):
+        try:
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                outs = []
+                for _ in range(3):
+                    outs.append((_forward(layer, xs[i]), _block(layer, xs[i])))
+                s.synchronize()
+            got[i] = outs
+        except Exception as e:  # pragma: no cover - reported below
+            errors.append(e)
+
+    threads = [threading.Thread(target=lane, args=(i,)) for i in range(2)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    assert not errors, errors
+    for i in range(2):
+        for f, b in got[i]:
+            assert torch.equal(f, want[i][0]) and torch.equal(b, want[i][1]), i
