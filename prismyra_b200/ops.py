@@ -218,8 +218,11 @@ def block_fp8(x: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch.T
 
 
 class _HostPipe:
-    """Per-(device, thread) copy streams and device row buffers for :func:`forward_fp8_host` (grow-only, never
-    freed, so addresses stay stable across calls)."""
+    """Per-(device, thread) copy streams and two sets of device row buffers for the host-to-host calls (grow-only,
+    never freed, so addresses stay stable across calls).  Calls alternate between the two sets, so that one call's
+    upload can run while the previous call's layer and download are still in flight; each set carries the events
+    after which its input rows may be overwritten (its layer has read them) and its output rows may be overwritten
+    (its download has read them)."""
 
     def __init__(self):
         self._lock = threading.Lock()
@@ -230,13 +233,21 @@ class _HostPipe:
         with self._lock:
             st = self._state.get(key)
             if st is None:
-                st = {"h2d": torch.cuda.Stream(device), "d2h": torch.cuda.Stream(device), "rows": 0, "H": H}
+                st = {"h2d": torch.cuda.Stream(device), "d2h": torch.cuda.Stream(device), "rows": 0, "H": H,
+                      "next": 0, "sets": [{}, {}]}
                 self._state[key] = st
             if st["rows"] < T or st["H"] != H:
-                st["x"] = torch.empty(T, H, dtype=torch.bfloat16, device=device)
-                st["out"] = torch.empty(T, H, dtype=torch.bfloat16, device=device)
+                for bs in st["sets"]:
+                    for ev in ("x_free", "out_free"):  # a grown buffer set waits for the old one's users
+                        if ev in bs:
+                            torch.cuda.current_stream(device).wait_event(bs[ev])
+                    bs.clear()
+                    bs["x"] = torch.empty(T, H, dtype=torch.bfloat16, device=device)
+                    bs["out"] = torch.empty(T, H, dtype=torch.bfloat16, device=device)
                 st["rows"], st["H"] = T, H
-            return st
+            bs = st["sets"][st["next"]]
+            st["next"] ^= 1
+            return st, bs
 
 
 _PIPE = _HostPipe()
@@ -253,47 +264,72 @@ def host_chunks(T: int, edge_rows: int = 1024) -> list[tuple[int, int]]:
     return [(0, edge_rows), (edge_rows, T - edge_rows), (T - edge_rows, T)]
 
 
-def forward_fp8_host(x_host: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch.Tensor,
-                     w2_s: torch.Tensor, top_k: int, router_w: torch.Tensor, out_host: torch.Tensor | None = None,
-                     edge_rows: int = 1024) -> torch.Tensor:
-    """The routed FP8 experts for a host-resident x [T, H] bf16 (pinned, so the copies overlap): rows go to the GPU,
-    through :func:`forward_fp8` and back in the chunks of :func:`host_chunks`, with the host-to-device copies, the
-    layer and the device-to-host copies on three streams so that both PCIe directions overlap the compute.  Every
-    row's result equals :func:`forward_fp8` on the whole batch (rows are independent, and the layer's launch shapes
-    agree bit for bit).  Ordered on the caller's current stream: returns once the work is queued; ``out_host``
-    [T, H] (pinned bf16) holds the result when that stream has reached this point."""
+def _host_args(x_host, out_host):
     _need(x_host.dim() == 2 and x_host.dtype == torch.bfloat16 and x_host.device.type == "cpu",
           "x_host must be a host bf16 [T, H] tensor")
-    dev = w1.device
     T, H = x_host.shape
     if out_host is None:
         out_host = torch.empty(T, H, dtype=torch.bfloat16, pin_memory=True)
     _need(tuple(out_host.shape) == (T, H) and out_host.dtype == torch.bfloat16 and out_host.device.type == "cpu",
           "out_host must be a host bf16 [T, H] tensor")
-    if T == 0:
-        return out_host
-    st = _PIPE.get(dev, T, H)
+    return T, H, out_host
+
+
+def forward_fp8_host_async(x_host: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch.Tensor,
+                           w2_s: torch.Tensor, top_k: int, router_w: torch.Tensor,
+                           out_host: torch.Tensor | None = None, chunks: list[tuple[int, int]] | None = None):
+    """Queue the routed FP8 experts for a host-resident x [T, H] bf16 (pinned) and return (out_host, done): done is
+    a CUDA event after which ``out_host`` holds the result.  The caller's current stream runs the layer; uploads
+    and downloads run on this thread's copy streams, each call on the other of two device buffer sets, so
+    consecutive calls overlap: a call's upload runs during the previous call's layer, its download during the next
+    call's layer.  ``chunks`` (row ranges covering [0, T) in order, default one) splits a call into pieces whose
+    copies overlap its own layer (:func:`host_chunks`).  Every row's result equals :func:`forward_fp8` on the whole
+    batch (rows are independent, and the layer's launch shapes agree bit for bit)."""
+    dev = w1.device
+    T, H, out_host = _host_args(x_host, out_host)
+    done = torch.cuda.Event()
     comp = torch.cuda.current_stream(dev)
-    start = torch.cuda.Event()
-    start.record(comp)
-    st["h2d"].wait_event(start)  # the device row buffers are free once the caller's earlier work is done
-    st["d2h"].wait_event(start)
-    for r0, r1 in host_chunks(T, edge_rows):
-        xs, os_ = st["x"][r0:r1], st["out"][r0:r1]
+    if T == 0:
+        done.record(comp)
+        return out_host, done
+    st, bs = _PIPE.get(dev, T, H)
+    if "x_free" in bs:
+        st["h2d"].wait_event(bs["x_free"])   # this set's input rows: read by its previous layer
+    if "out_free" in bs:
+        comp.wait_event(bs["out_free"])      # this set's output rows: read by its previous download
+    for r0, r1 in (chunks or [(0, T)]):
+        xs, os_ = bs["x"][r0:r1], bs["out"][r0:r1]
         with torch.cuda.stream(st["h2d"]):
             xs.copy_(x_host[r0:r1], non_blocking=True)
             ready = torch.cuda.Event()
             ready.record(st["h2d"])
         comp.wait_event(ready)
         forward_fp8(xs, w1, w1_s, w2, w2_s, top_k, router_w=router_w, out=os_)
-        done = torch.cuda.Event()
-        done.record(comp)
-        st["d2h"].wait_event(done)
+        computed = torch.cuda.Event()
+        computed.record(comp)
+        st["d2h"].wait_event(computed)
         with torch.cuda.stream(st["d2h"]):
             out_host[r0:r1].copy_(os_, non_blocking=True)
-    finished = torch.cuda.Event()
-    finished.record(st["d2h"])
-    comp.wait_event(finished)
+    x_free = torch.cuda.Event()
+    x_free.record(comp)
+    done.record(st["d2h"])
+    bs["x_free"], bs["out_free"] = x_free, done
+    return out_host, done
+
+
+def forward_fp8_host(x_host: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch.Tensor,
+                     w2_s: torch.Tensor, top_k: int, router_w: torch.Tensor, out_host: torch.Tensor | None = None,
+                     edge_rows: int = 1024) -> torch.Tensor:
+    """The routed FP8 experts for a host-resident x [T, H] bf16 (pinned, so the copies overlap): rows go to the GPU,
+    through :func:`forward_fp8` and back in the chunks of :func:`host_chunks`, with the host-to-device copies, the
+    layer and the device-to-host copies on three streams so that both PCIe directions overlap the compute.  Ordered
+    on the caller's current stream: returns once the work is queued; ``out_host`` [T, H] (pinned bf16) holds the
+    result when that stream has reached this point.  For a stream of batches, :func:`forward_fp8_host_async`
+    overlaps consecutive calls instead."""
+    T, H, out_host = _host_args(x_host, out_host)
+    out_host, done = forward_fp8_host_async(x_host, w1, w1_s, w2, w2_s, top_k, router_w, out_host,
+                                            chunks=host_chunks(T, edge_rows))
+    torch.cuda.current_stream(w1.device).wait_event(done)
     return out_host
 
 

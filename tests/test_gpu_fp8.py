@@ -324,6 +324,24 @@ def test_host_pipelined_forward_equals_the_device_forward(layer, T, edge):
     assert torch.equal(out, ref)
 
 
+def test_host_calls_overlapping_each_other_equal_device_forwards(layer):
+    """Consecutive asynchronous host-to-host calls (each upload overlapping the previous call's layer and
+    download, two alternating device buffer sets) with different inputs: every result equals its own device
+    forward bit for bit, also when a later call grows the buffers."""
+    _, gpu = layer
+    args = (gpu["w1"], gpu["w1_s"], gpu["w2"], gpu["w2_s"], K, gpu["router_w"])
+    cases = []
+    for i, T in enumerate((512, 512, 300, 512, 700, 512)):
+        x = gpu["x"][(torch.arange(T, device=DEV) * (i + 3)) % 512].contiguous()
+        cases.append((x.cpu().pin_memory(), ops.forward_fp8(x, *args[:5], router_w=gpu["router_w"]).cpu()))
+    torch.cuda.synchronize()
+    outs = [ops.forward_fp8_host_async(xh, *args, out_host=torch.empty_like(xh).pin_memory()) for xh, _ in cases]
+    for out_host, done in outs:
+        done.synchronize()
+    for (out_host, _), (_, ref) in zip(outs, cases):
+        assert torch.equal(out_host, ref)
+
+
 def test_forward_with_given_logits_equals_in_kernel_router(layer):
     _, gpu = layer
     x = gpu["x"][:256].contiguous()
