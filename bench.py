@@ -342,19 +342,17 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
         ms = float(t.item())
     value = world * T_CTX / (ms * 1e-3)
 
-    # end to end through the public call with host buffers: every step uploads its pinned x and downloads its
-    # result to pinned memory.  One GPU: the asynchronous host-to-host call, consecutive steps overlapping (a
-    # step's upload runs during the previous step's layer, its download during the next step's layer); the timed
-    # region ends when the last download has landed.
+    # end to end through the public calls with host buffers: every step uploads its pinned x and downloads its
+    # result to pinned memory, consecutive steps overlapping (a step's upload runs during the previous step's
+    # layer, its download during the next step's layer): ops.forward_fp8_host_async on one GPU, ops.host_async
+    # around the expert-parallel layer on every rank; the timed region ends when the last download has landed.
     x_host = x.cpu().pin_memory()
     out_hosts = [torch.empty(T_CTX, H, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    x_dev = torch.empty_like(x)
     last = [None]
 
     def e2e_step(i=0):
         if world > 1:
-            x_dev.copy_(x_host, non_blocking=True)
-            out_hosts[0].copy_(ep_layer.forward(x_dev), non_blocking=True)
+            _, last[0] = ops.host_async(lambda xs, _os: ep_layer.forward(xs), x_host, out_hosts[i % 2], device=dev)
         else:
             _, last[0] = ops.forward_fp8_host_async(x_host, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"],
                                                     K, layer["router_w"], out_host=out_hosts[i % 2])
@@ -496,9 +494,9 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
                         "stages_ms": {k: round(v, 4) for k, v in b_st.items() if isinstance(v, float)}},
         "e2e": {"value": world * T_CTX / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": T_CTX * H * 2, "d2h_bytes_per_step": T_CTX * H * 2,
-                "mode": "ops.forward_fp8_host_async per step, consecutive steps overlapping (upload of step i+1 "
-                        "and download of step i-1 during the layer of step i)" if world == 1 else
-                        "per rank: upload, expert-parallel layer, download, in series"},
+                "mode": ("ops.forward_fp8_host_async" if world == 1 else "ops.host_async around the expert-parallel "
+                         "layer on every rank") + " per step, consecutive steps overlapping (upload of step i+1 and "
+                         "download of step i-1 during the layer of step i)"},
         "nvfp4_t5120": {"ms": nv_ms, "tokens_per_s": T_CTX / (nv_ms * 1e-3), "tflops": nv_tflops,
                         "frac_fp4_peak": nv_tflops / fp4_peak, "fp4_peak": fp4_peak,
                         "weights": "NVFP4 from the FP8 layer (reference prepare_layer recipe), synthetic calibration"},

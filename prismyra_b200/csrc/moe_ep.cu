@@ -29,6 +29,8 @@ namespace {
 // ---------------------------------------------------------------------------------------------- count
 __global__ void __launch_bounds__(1024) ep_count_kernel(const int32_t* __restrict__ ids, int n, int E, int G,
                                                         int rank, const uint64_t* __restrict__ peer_cm) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ int cnt[kMaxExperts];
     for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
@@ -46,6 +48,8 @@ __global__ void __launch_bounds__(1024) ep_count_kernel(const int32_t* __restric
 // ---------------------------------------------------------------------------------------------- barrier
 __global__ void ep_barrier_kernel(const uint64_t* __restrict__ peer_flag, unsigned* own_flag, int G,
                                   unsigned target, int32_t* err) {
+    pdl_wait();
+    pdl_trigger();
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     __threadfence_system();
     for (int d = 0; d < G; ++d) atomicAdd_system(reinterpret_cast<unsigned*>(peer_flag[d]), 1u);
@@ -68,6 +72,8 @@ __global__ void __launch_bounds__(kMaxExperts) ep_offsets_kernel(const int32_t* 
                                                                  int32_t* __restrict__ expert_ids,
                                                                  int32_t* __restrict__ npp, int cap_blocks,
                                                                  int32_t* err) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ int padded[kMaxExperts];
     const int e = threadIdx.x;
     int tot = 0, pre = 0;
@@ -109,6 +115,8 @@ __global__ void __launch_bounds__(256) ep_dispatch_quant_kernel(
     const __nv_bfloat16* __restrict__ x, int T, int H, int k, const int32_t* __restrict__ ids,
     const float* __restrict__ topk_w, const int32_t* __restrict__ slot_local, const int32_t* __restrict__ off_local,
     const int32_t* __restrict__ base, int E, int epr, int rank, int cap, PeerPtrs peers, int32_t* err) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31, sub = lane & 15;
     const int G128 = H / 128;
     const long items = (long)T * G128;
@@ -174,6 +182,8 @@ __global__ void __launch_bounds__(256) ep_dispatch_quant_kernel(
 __global__ void ep_local_rows_kernel(const int32_t* __restrict__ meta, const int32_t* __restrict__ npp, int cap,
                                      int H, int G, int n_pairs, const uint64_t* __restrict__ peer_back,
                                      uint64_t* __restrict__ dst_rows, int32_t* err) {
+    pdl_wait();
+    pdl_trigger();
     const int n = *npp;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < cap; i += gridDim.x * blockDim.x) {
         uint64_t d = 0;
@@ -197,20 +207,21 @@ int grid_for(long work_items, int per_block, int sms) {
 
 cudaError_t launch_ep_count(const int32_t* ids, int n, int E, int G, int rank, const uint64_t* peer_cm,
                             cudaStream_t s) {
-    ep_count_kernel<<<1, 1024, 0, s>>>(ids, n, E, G, rank, peer_cm);
+    PM_TRY(launch_pdl(ep_count_kernel, dim3(1), dim3(1024), 0, s, ids, n, E, G, rank, peer_cm));
     return cudaGetLastError();
 }
 
 cudaError_t launch_ep_barrier(const uint64_t* peer_flag, unsigned* own_flag, int G, unsigned target, int32_t* err,
                               cudaStream_t s) {
-    ep_barrier_kernel<<<1, 32, 0, s>>>(peer_flag, own_flag, G, target, err);
+    PM_TRY(launch_pdl(ep_barrier_kernel, dim3(1), dim3(32), 0, s, peer_flag, own_flag, G, target, err));
     return cudaGetLastError();
 }
 
 cudaError_t launch_ep_offsets(const int32_t* cm, int G, int E, int epr, int rank, int32_t* base, int32_t* expert_ids,
                               int32_t* npp, int cap_blocks, int32_t* err, cudaStream_t s) {
     if (E > kMaxExperts) return cudaErrorInvalidValue;
-    ep_offsets_kernel<<<1, kMaxExperts, 0, s>>>(cm, G, E, epr, rank, base, expert_ids, npp, cap_blocks, err);
+    PM_TRY(launch_pdl(ep_offsets_kernel, dim3(1), dim3(kMaxExperts), 0, s, cm, G, E, epr, rank, base, expert_ids,
+                      npp, cap_blocks, err));
     return cudaGetLastError();
 }
 
@@ -222,17 +233,17 @@ cudaError_t launch_ep_dispatch_quant(const void* x, int T, int H, int k, const i
     if (T == 0) return cudaSuccess;
     PeerPtrs p{peer_a1, peer_a1s, peer_meta, peer_wgt};
     const long pairs = ((long)T * (H / 128) + 1) / 2;
-    ep_dispatch_quant_kernel<<<grid_for(pairs, 8, sms * 2), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), T, H,
-                                                                         k, ids, topk_w, slot_local, off_local, base,
-                                                                         E, epr, rank, cap, p, err);
+    PM_TRY(launch_pdl(ep_dispatch_quant_kernel, dim3(grid_for(pairs, 8, sms * 2)), dim3(256), 0, s,
+                      static_cast<const __nv_bfloat16*>(x), T, H, k, ids, topk_w, slot_local, off_local, base, E,
+                      epr, rank, cap, p, err));
     return cudaGetLastError();
 }
 
 cudaError_t launch_ep_local_rows(const int32_t* meta, const int32_t* npp, int cap, int H, int G, int n_pairs,
                                  const uint64_t* peer_back, uint64_t* dst_rows, int32_t* err, int sms,
                                  cudaStream_t s) {
-    ep_local_rows_kernel<<<grid_for(cap, 256, sms), 256, 0, s>>>(meta, npp, cap, H, G, n_pairs, peer_back, dst_rows,
-                                                                  err);
+    PM_TRY(launch_pdl(ep_local_rows_kernel, dim3(grid_for(cap, 256, sms)), dim3(256), 0, s, meta, npp, cap, H, G,
+                      n_pairs, peer_back, dst_rows, err));
     return cudaGetLastError();
 }
 

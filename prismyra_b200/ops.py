@@ -275,17 +275,17 @@ def _host_args(x_host, out_host):
     return T, H, out_host
 
 
-def forward_fp8_host_async(x_host: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch.Tensor,
-                           w2_s: torch.Tensor, top_k: int, router_w: torch.Tensor,
-                           out_host: torch.Tensor | None = None, chunks: list[tuple[int, int]] | None = None):
-    """Queue the routed FP8 experts for a host-resident x [T, H] bf16 (pinned) and return (out_host, done): done is
-    a CUDA event after which ``out_host`` holds the result.  The caller's current stream runs the layer; uploads
-    and downloads run on this thread's copy streams, each call on the other of two device buffer sets, so
-    consecutive calls overlap: a call's upload runs during the previous call's layer, its download during the next
-    call's layer.  ``chunks`` (row ranges covering [0, T) in order, default one) splits a call into pieces whose
-    copies overlap its own layer (:func:`host_chunks`).  Every row's result equals :func:`forward_fp8` on the whole
-    batch (rows are independent, and the layer's launch shapes agree bit for bit)."""
-    dev = w1.device
+def host_async(fn, x_host: torch.Tensor, out_host: torch.Tensor | None = None,
+               chunks: list[tuple[int, int]] | None = None, device: torch.device | None = None):
+    """Run a device function over a host-resident batch: upload x_host [T, H] bf16 (pinned) on this thread's upload
+    stream, call ``fn(x_rows, out_rows)`` on the caller's current stream (it returns the result rows: ``out_rows``
+    itself or a tensor of its own), download on the download stream, and return (out_host, done): done is a CUDA
+    event after which ``out_host`` holds the result.  Calls alternate between two device buffer sets, so
+    consecutive calls overlap: a call's upload runs during the previous call's ``fn``, its download during the
+    next call's.  ``chunks`` (row ranges covering [0, T) in order, default one) splits a call into pieces whose
+    copies overlap its own ``fn``; use it only for a row-wise ``fn``.  Every rank of an expert-parallel layer calls
+    this the same number of times, like the layer itself."""
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
     T, H, out_host = _host_args(x_host, out_host)
     done = torch.cuda.Event()
     comp = torch.cuda.current_stream(dev)
@@ -294,7 +294,7 @@ def forward_fp8_host_async(x_host: torch.Tensor, w1: torch.Tensor, w1_s: torch.T
         return out_host, done
     st, bs = _PIPE.get(dev, T, H)
     if "x_free" in bs:
-        st["h2d"].wait_event(bs["x_free"])   # this set's input rows: read by its previous layer
+        st["h2d"].wait_event(bs["x_free"])   # this set's input rows: read by its previous call
     if "out_free" in bs:
         comp.wait_event(bs["out_free"])      # this set's output rows: read by its previous download
     for r0, r1 in (chunks or [(0, T)]):
@@ -304,17 +304,31 @@ def forward_fp8_host_async(x_host: torch.Tensor, w1: torch.Tensor, w1_s: torch.T
             ready = torch.cuda.Event()
             ready.record(st["h2d"])
         comp.wait_event(ready)
-        forward_fp8(xs, w1, w1_s, w2, w2_s, top_k, router_w=router_w, out=os_)
+        res = fn(xs, os_)
         computed = torch.cuda.Event()
         computed.record(comp)
         st["d2h"].wait_event(computed)
+        if res.data_ptr() != os_.data_ptr():
+            res.record_stream(st["d2h"])     # a tensor of fn's own: kept until its download has read it
         with torch.cuda.stream(st["d2h"]):
-            out_host[r0:r1].copy_(os_, non_blocking=True)
+            out_host[r0:r1].copy_(res, non_blocking=True)
     x_free = torch.cuda.Event()
     x_free.record(comp)
     done.record(st["d2h"])
     bs["x_free"], bs["out_free"] = x_free, done
     return out_host, done
+
+
+def forward_fp8_host_async(x_host: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch.Tensor,
+                           w2_s: torch.Tensor, top_k: int, router_w: torch.Tensor,
+                           out_host: torch.Tensor | None = None, chunks: list[tuple[int, int]] | None = None):
+    """The routed FP8 experts for a host-resident x [T, H] bf16 through :func:`host_async`: returns (out_host,
+    done), consecutive calls overlapping.  Every row's result equals :func:`forward_fp8` on the whole batch (rows
+    are independent, and the layer's launch shapes agree bit for bit)."""
+    def fn(xs, os_):
+        return forward_fp8(xs, w1, w1_s, w2, w2_s, top_k, router_w=router_w, out=os_)
+
+    return host_async(fn, x_host, out_host, chunks, device=w1.device)
 
 
 def forward_fp8_host(x_host: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch.Tensor,
