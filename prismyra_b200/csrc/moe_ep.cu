@@ -213,7 +213,9 @@ cudaError_t launch_ep_count(const int32_t* ids, int n, int E, int G, int rank, c
 
 cudaError_t launch_ep_barrier(const uint64_t* peer_flag, unsigned* own_flag, int G, unsigned target, int32_t* err,
                               cudaStream_t s) {
-    PM_TRY(launch_pdl(ep_barrier_kernel, dim3(1), dim3(32), 0, s, peer_flag, own_flag, G, target, err));
+    // A plain launch: the barrier publishes its predecessor's peer stores to the other ranks, so it starts only
+    // after that kernel has fully completed in stream order.
+    ep_barrier_kernel<<<1, 32, 0, s>>>(peer_flag, own_flag, G, target, err);
     return cudaGetLastError();
 }
 
