@@ -342,6 +342,26 @@ def test_host_calls_overlapping_each_other_equal_device_forwards(layer):
         assert torch.equal(out_host, ref)
 
 
+def test_host_async_around_a_function_with_its_own_output(layer):
+    """ops.host_async around a device function that returns a tensor of its own (as the expert-parallel layer does)
+    rather than filling the given rows: consecutive overlapping calls still return each batch's own result."""
+    _, gpu = layer
+
+    def fn(xs, _rows):
+        return ops.forward_fp8(xs, gpu["w1"], gpu["w1_s"], gpu["w2"], gpu["w2_s"], K, router_w=gpu["router_w"])
+
+    cases = []
+    for i in range(4):
+        x = gpu["x"][(torch.arange(400, device=DEV) * (i + 5)) % 512].contiguous()
+        cases.append((x.cpu().pin_memory(), fn(x, None).cpu()))
+    torch.cuda.synchronize()
+    outs = [ops.host_async(fn, xh, torch.empty_like(xh).pin_memory(), device=torch.device(DEV)) for xh, _ in cases]
+    for out_host, done in outs:
+        done.synchronize()
+    for (out_host, _), (_, ref) in zip(outs, cases):
+        assert torch.equal(out_host, ref)
+
+
 def test_forward_with_given_logits_equals_in_kernel_router(layer):
     _, gpu = layer
     x = gpu["x"][:256].contiguous()
