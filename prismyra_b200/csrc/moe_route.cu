@@ -15,26 +15,36 @@
 namespace pm {
 namespace {
 
-constexpr int kMaxEPT = kMaxExperts / 32;  // logits held per lane
+constexpr int kMaxEPT = kMaxExperts / 32;  // logits held per lane at most (EPT: 4 for E <= 128, else 8)
 
 // One warp ranks one token.  v[i] holds the logit of expert lane + 32 i (or -inf past E).
-__device__ __forceinline__ void warp_topk(const float (&v)[kMaxEPT], int E, int k, float* w_out, int32_t* id_out) {
+template <int EPT>
+__device__ __forceinline__ void warp_topk(const float (&v)[EPT], int E, int k, float* w_out, int32_t* id_out) {
     const int lane = threadIdx.x & 31;
     float mx = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < kMaxEPT; ++i) mx = fmaxf(mx, v[i]);
+    for (int i = 0; i < EPT; ++i) mx = fmaxf(mx, v[i]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float ex[kMaxEPT];
+    float ex[EPT];
 #pragma unroll
-    for (int i = 0; i < kMaxEPT; ++i) ex[i] = (lane + 32 * i < E) ? expf(v[i] - mx) : 0.0f;
-    // The exponent sum in ascending expert order, the same order as the router kernel's epilogue, so both
-    // entry points give bit-identical weights for the same logits.
+    for (int i = 0; i < EPT; ++i) ex[i] = (lane + 32 * i < E) ? expf(v[i] - mx) : 0.0f;
+    // The exponent sum in ascending expert order over whole 32-expert groups (zeros past E), one fp32 add per
+    // term: the row is staged in this warp's shared-memory row and every lane adds it in order from 16-byte
+    // broadcast loads.
+    __shared__ __align__(16) float rows[8][32 * EPT];
+    float* row = rows[(threadIdx.x >> 5) & 7];
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) row[lane + 32 * i] = ex[i];
+    __syncwarp();
     float sum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < kMaxEPT; ++i) {
-        if (32 * i >= E) break;
-        for (int l = 0; l < 32; ++l) sum += __shfl_sync(0xffffffffu, ex[i], l);
+    const int n = 32 * min(EPT, (E + 31) / 32);
+    for (int e = 0; e < n; e += 4) {
+        const float4 q = *reinterpret_cast<const float4*>(row + e);
+        sum += q.x;
+        sum += q.y;
+        sum += q.z;
+        sum += q.w;
     }
 
     uint32_t used = 0;
@@ -44,7 +54,7 @@ __device__ __forceinline__ void warp_topk(const float (&v)[kMaxEPT], int E, int 
         float bv = -INFINITY;
         int bi = 0x7fffffff;
 #pragma unroll
-        for (int i = 0; i < kMaxEPT; ++i) {
+        for (int i = 0; i < EPT; ++i) {
             const int e = lane + 32 * i;
             if (e < E && !((used >> i) & 1u) && (v[i] > bv || bi == 0x7fffffff)) {
                 bv = v[i];
@@ -65,7 +75,7 @@ __device__ __forceinline__ void warp_topk(const float (&v)[kMaxEPT], int E, int 
             const int slot = bi >> 5;
             used |= 1u << slot;
 #pragma unroll
-            for (int i = 0; i < kMaxEPT; ++i)
+            for (int i = 0; i < EPT; ++i)
                 if (i == slot) mine = ex[i];
         }
         const float p = __shfl_sync(0xffffffffu, mine, bi & 31) / sum;
@@ -81,6 +91,7 @@ __device__ __forceinline__ void warp_topk(const float (&v)[kMaxEPT], int E, int 
     }
 }
 
+template <int EPT>
 __global__ void __launch_bounds__(256) topk_kernel(const __nv_bfloat16* __restrict__ logits,
                                                    const float* __restrict__ bias, int T, int E, int k,
                                                    float* __restrict__ topk_w, int32_t* __restrict__ topk_ids) {
@@ -89,9 +100,9 @@ __global__ void __launch_bounds__(256) topk_kernel(const __nv_bfloat16* __restri
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= T) return;
-    float v[kMaxEPT];
+    float v[EPT];
 #pragma unroll
-    for (int i = 0; i < kMaxEPT; ++i) {
+    for (int i = 0; i < EPT; ++i) {
         const int e = lane + 32 * i;
         v[i] = e < E ? __bfloat162float(logits[(size_t)warp * E + e]) + (bias != nullptr ? bias[e] : 0.0f)
                      : -INFINITY;
@@ -100,6 +111,7 @@ __global__ void __launch_bounds__(256) topk_kernel(const __nv_bfloat16* __restri
 }
 
 // The same from the router's fp32 chunk partials: logit = bf16(((P_0 + P_1) + P_2) + ...), written out, then ranked.
+template <int EPT>
 __global__ void __launch_bounds__(256) topk_partials_kernel(const float* __restrict__ part, int chunks,
                                                             __nv_bfloat16* __restrict__ logits,
                                                             const float* __restrict__ bias, int T, int E, int k,
@@ -110,27 +122,27 @@ __global__ void __launch_bounds__(256) topk_partials_kernel(const float* __restr
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= T) return;
-    float v[kMaxEPT];
+    float v[EPT];
     // all of this lane's chunk partials are loaded before any is added (one round trip for up to 8 chunks), then
     // added in chunk order
     constexpr int kC = 8;
     for (int c0 = 0; c0 < chunks; c0 += kC) {
-        float pv[kMaxEPT][kC];
+        float pv[EPT][kC];
 #pragma unroll
-        for (int i = 0; i < kMaxEPT; ++i) {
+        for (int i = 0; i < EPT; ++i) {
             const int e = lane + 32 * i;
 #pragma unroll
             for (int j = 0; j < kC; ++j)
                 pv[i][j] = (e < E && c0 + j < chunks) ? part[((size_t)(c0 + j) * T + warp) * E + e] : 0.0f;
         }
 #pragma unroll
-        for (int i = 0; i < kMaxEPT; ++i)
+        for (int i = 0; i < EPT; ++i)
 #pragma unroll
             for (int j = 0; j < kC; ++j)
                 if (c0 + j < chunks) v[i] = (c0 + j == 0) ? pv[i][j] : v[i] + pv[i][j];
     }
 #pragma unroll
-    for (int i = 0; i < kMaxEPT; ++i) {
+    for (int i = 0; i < EPT; ++i) {
         const int e = lane + 32 * i;
         if (e < E) {
             const __nv_bfloat16 b = __float2bfloat16_rn(v[i]);
@@ -336,8 +348,12 @@ cudaError_t launch_topk(const void* logits, const float* bias, int T, int E, int
                         cudaStream_t s) {
     if (T == 0) return cudaSuccess;
     const int blocks = cdiv((long)T * 32, 256);
-    PM_TRY(launch_pdl(topk_kernel, dim3(blocks), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(logits), bias, T,
-                      E, k, topk_w, topk_ids));
+    if (E <= 128)
+        PM_TRY(launch_pdl(topk_kernel<4>, dim3(blocks), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(logits),
+                          bias, T, E, k, topk_w, topk_ids));
+    else
+        PM_TRY(launch_pdl(topk_kernel<kMaxEPT>, dim3(blocks), dim3(256), 0, s,
+                          static_cast<const __nv_bfloat16*>(logits), bias, T, E, k, topk_w, topk_ids));
     return cudaGetLastError();
 }
 
@@ -345,8 +361,12 @@ cudaError_t launch_topk_partials(const float* part, int chunks, void* logits, co
                                  float* topk_w, int32_t* topk_ids, cudaStream_t s) {
     if (T == 0) return cudaSuccess;
     const int blocks = cdiv((long)T * 32, 256);
-    PM_TRY(launch_pdl(topk_partials_kernel, dim3(blocks), dim3(256), 0, s, part, chunks,
-                      static_cast<__nv_bfloat16*>(logits), bias, T, E, k, topk_w, topk_ids));
+    if (E <= 128)
+        PM_TRY(launch_pdl(topk_partials_kernel<4>, dim3(blocks), dim3(256), 0, s, part, chunks,
+                          static_cast<__nv_bfloat16*>(logits), bias, T, E, k, topk_w, topk_ids));
+    else
+        PM_TRY(launch_pdl(topk_partials_kernel<kMaxEPT>, dim3(blocks), dim3(256), 0, s, part, chunks,
+                          static_cast<__nv_bfloat16*>(logits), bias, T, E, k, topk_w, topk_ids));
     return cudaGetLastError();
 }
 
