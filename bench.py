@@ -8,11 +8,14 @@ quantisation, gate_up GEMM + silu*mul + requantisation, down GEMM + routing weig
 of H=2048 with E=128 experts, top-8, I=768, synthetic seeded data, expert weights 128x128
 block-FP8.  The weights (604 MB) exceed the 126 MB L2, so every step streams them from HBM; no L2 flush is added.
 Under torchrun (N GPUs) the step is the expert-parallel layer: every rank owns E/N experts and its own 5120
-tokens (weak scaling), NCCL all-to-all dispatch and combine; the step time is the max over ranks.
+tokens (weak scaling); the kernels move the rows themselves over NVLink (the dispatching quantisation stores each
+token's rows into the owners' expert slots, the down GEMM's epilogue stores each weighted row back into its source
+rank's result row, device barriers between the phases; no collective library on the data path); the step time is
+the max over ranks.
 
 ``--impl reference`` times the reference's own CPU implementation of the same layer (transformers' fallback
-block, float32, all host threads) on a bounded sample of the workload and prints the same JSON line with
-``"impl": "reference"``.
+block, float32 -- the engine's CPU dtype -- and bfloat16, all host threads, median of >= 5 calls after 2 warm-ups)
+on a bounded sample of the same seeded workload and prints the same JSON line with ``"impl": "reference"``.
 """
 
 from __future__ import annotations
@@ -146,8 +149,9 @@ class Clocks:
                 "samples": len(inside), "power_w_max": max(r[3] for r in inside)}
 
 
-def cpu_baseline(layer_cpu: dict, min_seconds: float = 12.0) -> dict:
-    """The reference's CPU fallback (transformers block, float32) on a 512-token sample of the workload."""
+def cpu_baseline(layer_cpu: dict, max_seconds: float = 12.0) -> dict:
+    """The reference's CPU fallback (transformers block) on a 512-token sample of the workload, in float32 (the
+    engine's CPU dtype: the reported value) and in bfloat16; median of >= 5 calls after 2 warm-ups each."""
     import torch
 
     from oracle import torch_fallback
@@ -155,14 +159,20 @@ def cpu_baseline(layer_cpu: dict, min_seconds: float = 12.0) -> dict:
 
     w1 = synth.dequantize_fp8_blocks(layer_cpu["w1"], layer_cpu["w1_s"])
     w2 = synth.dequantize_fp8_blocks(layer_cpu["w2"], layer_cpu["w2_s"])
-    router, experts = torch_fallback.build_block(layer_cpu["router_w"].float(), w1, w2, K)
-    x = layer_cpu["x"][:T_CPU_SAMPLE].float()
-    r = torch_fallback.time_routed(router, experts, x, min_seconds=min_seconds)
-    del w1, w2, router, experts
+    res = {}
+    for dt in (torch.float32, torch.bfloat16):
+        router, experts = torch_fallback.build_block(layer_cpu["router_w"].float(), w1, w2, K, dtype=dt)
+        x = layer_cpu["x"][:T_CPU_SAMPLE].to(dt)
+        res[dt] = torch_fallback.time_routed(router, experts, x, max_seconds=max_seconds)
+        del router, experts
+    del w1, w2
+    r, rb = res[torch.float32], res[torch.bfloat16]
     return {"value": r["tokens_per_s"], "unit": "tokens/s", "cores": r["threads"], "kind": "reference",
-            "sample": f"{T_CPU_SAMPLE} of the {T_CTX} tokens, {r['calls']} calls in {r['seconds']:.1f} s: "
-                      "transformers Qwen3_5MoeTopKRouter + Qwen3_5MoeExperts (the reference's CPU fallback) in "
-                      f"float32 on dequantised FP8 weights; os.cpu_count()={r['cpu_count']}"}
+            "sample": f"{T_CPU_SAMPLE} of the {T_CTX} tokens (the same seeded tensors as the GPU arm), median of "
+                      f"{r['calls']} calls after {r['warmup']} warm-ups: transformers Qwen3_5MoeTopKRouter + "
+                      "Qwen3_5MoeExperts (the reference's CPU fallback) in float32 on dequantised FP8 weights",
+            "bf16_tokens_per_s": rb["tokens_per_s"], "bf16_calls": rb["calls"],
+            "cpu_model": r["cpu_model"], "os_cpu_count": r["cpu_count"], "torch_threads": r["threads"]}
 
 
 def run_reference(args, rank: int, world: int) -> None:
@@ -174,7 +184,7 @@ def run_reference(args, rank: int, world: int) -> None:
 
     layer = synth.make_fp8_layer(T_CTX, H, I, E, seed=0, device="cpu")
     per_step = max(3.0, min(20.0, 150.0 / max(1, args.steps + args.warmup)))
-    cb = cpu_baseline(layer, min_seconds=per_step * max(1, args.steps))
+    cb = cpu_baseline(layer, max_seconds=min(60.0, per_step * max(1, args.steps)))
     line = {
         "metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": T_CPU_SAMPLE / cb["value"] * 1e3, "higher_is_better": True,
@@ -293,7 +303,13 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
     torch.cuda.set_device(dev)
     pk = peaks()
     fp8_peak = 2.0 * pk["bf16_tflops"]  # B200 FP8 dense rate is twice its BF16 dense rate
-    layer = synth.make_fp8_layer(T_CTX, H, I, E, seed=0, device=dev, gen_device="cuda")
+    # the seeded layer is drawn on the CPU (seed 0) and copied over: the CPU baseline times the
+    # very same tensors
+    layer_cpu = synth.make_fp8_layer(T_CTX, H, I, E, seed=0, device="cpu")
+    layer = {k: v.to(dev) for k, v in layer_cpu.items()}
+    if world > 1 or args.no_cpu_baseline:
+        del layer_cpu
+        layer_cpu = None
     x = layer["x"]
     stream = torch.cuda.current_stream()
     if world > 1:
@@ -468,8 +484,7 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
     if rank != 0:
         return
     cb = None
-    if world == 1 and not args.no_cpu_baseline:
-        layer_cpu = synth.make_fp8_layer(T_CTX, H, I, E, seed=0, device="cpu")
+    if layer_cpu is not None:
         cb = cpu_baseline(layer_cpu)
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,

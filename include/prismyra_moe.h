@@ -233,7 +233,9 @@ int pm_nvfp4_prepare(const uint8_t *w, const float *s, int E, int R, int C, uint
  * inside the library (held on every GPU that loads it until the process exits).  Limits: T*k <= 2^20 and
  * E <= 256, else PM_ERR_TOO_LARGE.  All calls share that array: calls whose kernels overlap on the GPU (e.g. on
  * two streams) race and must be serialised by the caller.  The first call on each device looks up the array's
- * device address (cudaGetSymbolAddress, with that device current); make it before any stream capture begins. */
+ * device address (cudaGetSymbolAddress, with that device current); make it before any stream capture begins.  The
+ * address is kept for the life of the process: it does not survive cudaDeviceReset or the destruction of the
+ * device's primary context, after which this entry point must not be called. */
 int pm_moe_align_noalloc(const int32_t *topk_ids, int T, int k, int E, int32_t *sorted_ids, int32_t *expert_ids,
                          int32_t *num_post_pad, int32_t *expert_off, pm_stream_t stream);
 
@@ -243,8 +245,8 @@ int pm_moe_align_noalloc(const int32_t *topk_ids, int T, int k, int E, int32_t *
  * peer's handle into this process (pm_ep_close / pm_ep_free undo them).  The other calls take device arrays of G
  * addresses (peer_*, one per rank, this rank's own included) and are stream-ordered, without host synchronisation.
  *   pm_ep_count       store this rank's per-expert pair counts into row `rank` of every rank's count matrix [G][E]
- *   pm_ep_barrier     add 1 to every rank's counter and wait (bounded; on timeout *err = 1) until the own counter
- *                     reaches target
+ *   pm_ep_barrier     add 1 to every rank's counter and wait until the own counter reaches target, for at most
+ *                     wait_limit_ns nanoseconds (0: the library's 2 s); on timeout *err = 1 and the kernel returns
  *   pm_ep_offsets     from the full count matrix: for each global expert, where this rank's pairs of it start in
  *                     the owner's slot space (experts padded to 128 slots, sources in rank order), and the block
  *                     table and slot count of this rank's own experts
@@ -259,7 +261,7 @@ int pm_ep_close(void *ptr);
 int pm_ep_free(void *ptr);
 int pm_ep_count(const int32_t *ids, int n, int E, int G, int rank, const uint64_t *peer_cm, pm_stream_t stream);
 int pm_ep_barrier(const uint64_t *peer_flag, unsigned *own_flag, int G, unsigned target, int32_t *err,
-                  pm_stream_t stream);
+                  uint64_t wait_limit_ns, pm_stream_t stream);
 int pm_ep_offsets(const int32_t *cm, int G, int E, int epr, int rank, int32_t *base, int32_t *expert_ids,
                   int32_t *num_post_pad, int cap_slots, int32_t *err, pm_stream_t stream);
 int pm_ep_dispatch_quant(const void *x, int T, int H, int k, const int32_t *topk_ids, const float *topk_w,

@@ -39,20 +39,36 @@ def routed(router, experts, x: torch.Tensor) -> torch.Tensor:
     return experts(x, ids, weights)
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (from /proc/cpuinfo), or the platform's processor string."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.lower().startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
 @torch.no_grad()
-def time_routed(router, experts, x: torch.Tensor, min_seconds: float = 10.0, max_iters: int = 50,
-                warmup: int = 1) -> dict:
-    """Tokens/s of the routed path on this host's cores: warm-up calls, then repeated calls until at least
-    ``min_seconds`` of CPU work (or ``max_iters`` calls) have been timed with ``time.perf_counter``."""
+def time_routed(router, experts, x: torch.Tensor, warmup: int = 2, min_calls: int = 5, max_seconds: float = 30.0,
+                max_calls: int = 50) -> dict:
+    """Tokens/s of the routed path on this host's cores: ``warmup`` untimed calls, then calls timed one by one with
+    ``time.perf_counter`` -- at least ``min_calls``, more while the total stays under ``max_seconds`` (at most
+    ``max_calls``) -- and the median call time."""
     torch.set_num_threads(os.cpu_count() or 1)
     for _ in range(warmup):
         routed(router, experts, x)
-    n, t0 = 0, time.perf_counter()
-    while True:
+    times: list[float] = []
+    t_start = time.perf_counter()
+    while len(times) < min_calls or (time.perf_counter() - t_start < max_seconds and len(times) < max_calls):
+        t0 = time.perf_counter()
         routed(router, experts, x)
-        n += 1
-        el = time.perf_counter() - t0
-        if el >= min_seconds or n >= max_iters:
-            break
-    return {"tokens_per_s": x.shape[0] * n / el, "seconds": el, "calls": n, "threads": torch.get_num_threads(),
-            "cpu_count": os.cpu_count()}
+        times.append(time.perf_counter() - t0)
+    med = sorted(times)[len(times) // 2]
+    return {"tokens_per_s": x.shape[0] / med, "median_s": med, "calls": len(times), "warmup": warmup,
+            "seconds": sum(times), "threads": torch.get_num_threads(), "cpu_count": os.cpu_count(),
+            "cpu_model": cpu_model(), "dtype": str(x.dtype).replace("torch.", "")}

@@ -33,7 +33,8 @@ static __device__ __align__(256) int32_t g_noalloc_counts[kNoallocChunks * kNoal
 int32_t* g_noalloc_ptr[64] = {};
 std::mutex g_noalloc_mu;
 
-// Device address of g_noalloc_counts on the current device (looked up once per device).
+// Device address of g_noalloc_counts on the current device (looked up once per device and kept: a cudaDeviceReset
+// or a destroyed primary context invalidates it, and the entry point's documentation rules calls after either out).
 int noalloc_counts(int32_t** out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PM_ERR_CUDA;

@@ -2,6 +2,7 @@
 // launch sequence of the routed-expert layer.  Nothing here allocates device memory or synchronises, except
 // pm_moe_read_status.
 #include <cudaTypedefs.h>
+#include <limits.h>
 #include <stdint.h>
 #include <string.h>
 
@@ -211,6 +212,7 @@ int pm_moe_topk(const void* logits, const float* bias, int T, int E, int k, floa
 size_t pm_moe_align_workspace_bytes(int T, int k, int E) {
     if (T < 0 || k <= 0 || E <= 0 || E > 1024) return 0;
     const long n = (long)T * k;
+    if (n > INT_MAX) return 0;  // the kernels index the flat pairs with 32-bit integers
     return (size_t)(n > 0 ? align_chunks(n) : 1) * E * 4;
 }
 
@@ -220,6 +222,7 @@ int pm_moe_align(const int32_t* topk_ids, int T, int k, int E, int32_t* sorted_i
     if (T < 0 || k <= 0 || E <= 0 || E > 1024) return PM_ERR_INVALID;
     if (!sorted_ids || !expert_ids || !num_post_pad || !workspace || (T > 0 && !topk_ids)) return PM_ERR_INVALID;
     const long n = (long)T * k;
+    if (n > INT_MAX) return PM_ERR_SHAPE;
     if (workspace_bytes < pm_moe_align_workspace_bytes(T, k, E)) return PM_ERR_WORKSPACE;
     DeviceInfo d;
     const int st = current_device_info(&d);
@@ -838,9 +841,9 @@ int pm_ep_count(const int32_t* ids, int n, int E, int G, int rank, const uint64_
 }
 
 int pm_ep_barrier(const uint64_t* peer_flag, unsigned* own_flag, int G, unsigned target, int32_t* err,
-                  pm_stream_t stream) {
+                  uint64_t wait_limit_ns, pm_stream_t stream) {
     if (!peer_flag || !own_flag || G <= 0) return PM_ERR_INVALID;
-    return cuda_status(launch_ep_barrier(peer_flag, own_flag, G, target, err, (cudaStream_t)stream));
+    return cuda_status(launch_ep_barrier(peer_flag, own_flag, G, target, err, wait_limit_ns, (cudaStream_t)stream));
 }
 
 int pm_ep_offsets(const int32_t* cm, int G, int E, int epr, int rank, int32_t* base, int32_t* expert_ids,

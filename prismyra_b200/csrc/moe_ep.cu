@@ -18,7 +18,7 @@
 // The rows, their arithmetic and the combine order are those of one GPU, so the result is bit-identical.
 //
 // Barrier: a one-thread kernel adds 1 to every rank's counter (system-scope atomics after a system fence) and
-// waits, bounded by PM_WAIT_TIMEOUT_NS, until its own counter reaches the call's target; on timeout it sets the
+// waits, bounded by the call's limit (PM_WAIT_TIMEOUT_NS when it gives 0), until its own counter reaches the call's target; on timeout it sets the
 // error word and returns.  Only plain peer loads/stores/atomics are used (no multicast).
 #include "moe_internal.h"
 #include "ptx.cuh"
@@ -47,7 +47,7 @@ __global__ void __launch_bounds__(1024) ep_count_kernel(const int32_t* __restric
 
 // ---------------------------------------------------------------------------------------------- barrier
 __global__ void ep_barrier_kernel(const uint64_t* __restrict__ peer_flag, unsigned* own_flag, int G,
-                                  unsigned target, int32_t* err) {
+                                  unsigned target, int32_t* err, uint64_t limit_ns) {
     pdl_wait();
     pdl_trigger();
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
@@ -57,7 +57,7 @@ __global__ void ep_barrier_kernel(const uint64_t* __restrict__ peer_flag, unsign
     while (true) {
         const unsigned v = *reinterpret_cast<volatile unsigned*>(own_flag);
         if ((int)(v - target) >= 0) break;  // counters only grow (wrap-safe comparison)
-        if (globaltimer() - t0 > PM_WAIT_TIMEOUT_NS) {
+        if (globaltimer() - t0 > limit_ns) {
             if (err != nullptr) atomicExch(err, 1);
             return;
         }
@@ -212,10 +212,11 @@ cudaError_t launch_ep_count(const int32_t* ids, int n, int E, int G, int rank, c
 }
 
 cudaError_t launch_ep_barrier(const uint64_t* peer_flag, unsigned* own_flag, int G, unsigned target, int32_t* err,
-                              cudaStream_t s) {
+                              uint64_t limit_ns, cudaStream_t s) {
     // A plain launch: the barrier publishes its predecessor's peer stores to the other ranks, so it starts only
     // after that kernel has fully completed in stream order.
-    ep_barrier_kernel<<<1, 32, 0, s>>>(peer_flag, own_flag, G, target, err);
+    ep_barrier_kernel<<<1, 32, 0, s>>>(peer_flag, own_flag, G, target, err,
+                                       limit_ns != 0 ? limit_ns : (uint64_t)PM_WAIT_TIMEOUT_NS);
     return cudaGetLastError();
 }
 

@@ -186,7 +186,7 @@ inline bool encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner
 cudaError_t launch_ep_count(const int32_t* ids, int n, int E, int G, int rank, const uint64_t* peer_cm,
                             cudaStream_t s);
 cudaError_t launch_ep_barrier(const uint64_t* peer_flag, unsigned* own_flag, int G, unsigned target, int32_t* err,
-                              cudaStream_t s);
+                              uint64_t limit_ns, cudaStream_t s);
 cudaError_t launch_ep_offsets(const int32_t* cm, int G, int E, int epr, int rank, int32_t* base, int32_t* expert_ids,
                               int32_t* npp, int cap_blocks, int32_t* err, cudaStream_t s);
 cudaError_t launch_ep_dispatch_quant(const void* x, int T, int H, int k, const int32_t* ids, const float* topk_w,

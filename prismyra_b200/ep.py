@@ -255,13 +255,14 @@ class PeerExchange:
         torch.cuda.synchronize(device)
         dist.barrier(group=group)  # every rank has mapped every region
 
-    def barrier(self, stream: int) -> None:
-        """Device barrier over the ranks (stream-ordered, bounded wait; on timeout the error word is set)."""
+    def barrier(self, stream: int, wait_limit_ns: int = 0) -> None:
+        """Device barrier over the ranks (stream-ordered; the wait gives up after ``wait_limit_ns``, 0 = the
+        library's 2 s, and then sets the error word)."""
         from . import _lib
 
         self.epoch += 1
         _lib.call("pm_ep_barrier", self.peer["flag"].data_ptr(), self.flag.data_ptr(), self.world,
-                  (self.epoch * self.world) & 0xFFFFFFFF, self.err.data_ptr(), stream)
+                  (self.epoch * self.world) & 0xFFFFFFFF, self.err.data_ptr(), wait_limit_ns, stream)
 
     def errors(self) -> int:
         """Non-zero if any kernel gave up on a bounded wait or met an out-of-range slot (synchronises)."""

@@ -35,7 +35,7 @@ def _group_scales(amax: torch.Tensor, g: torch.Tensor, frac: float = 1.0) -> tor
 
 def _encode(groups: torch.Tensor, scale: torch.Tensor, g: torch.Tensor):
     """Nearest e2m1 magnitude index (the first of equals, i.e. the smaller magnitude), sign and step of each value
-    of groups [rows, G, 16] under e4m3 group scales [rows, G]."""
+    of groups [..., G, 16] under e4m3 group scales [..., G] and global scales g broadcastable to [..., G]."""
     step = (scale.float() / g).unsqueeze(-1)
     x = torch.where(step > 0, groups / step, torch.zeros_like(groups)).clamp(-6, 6)
     grid = torch.tensor(E2M1_VALUES, device=groups.device)
@@ -43,88 +43,79 @@ def _encode(groups: torch.Tensor, scale: torch.Tensor, g: torch.Tensor):
     return mag, x < 0, step
 
 
-def _pack(mag: torch.Tensor, neg: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
-    code = (mag | (neg.long() << 3)).to(torch.uint8).reshape(rows, cols)
-    return (code[:, 0::2] | (code[:, 1::2] << 4)).contiguous()
+def _pack(mag: torch.Tensor, neg: torch.Tensor) -> torch.Tensor:
+    """Codes [..., G, 16] -> bytes [..., G*8]: two codes per byte, the even column in the low nibble."""
+    code = (mag | (neg.long() << 3)).to(torch.uint8).flatten(-2)
+    return (code[..., 0::2] | (code[..., 1::2] << 4)).contiguous()
+
+
+SEARCH = (1.0, 0.95, 0.9, 0.85, 0.8, 0.75, 0.7)
+
+
+def _quantize_groups(groups: torch.Tensor, g: torch.Tensor, imp: torch.Tensor | None = None, search: bool = False):
+    """groups [..., G, 16] fp32 under global scales g (broadcastable to [..., G]) -> (packed bytes, e4m3 scales).
+
+    Without ``search`` every 16-group gets the plain scale e4m3(min(amax/6*g, 448)).  With it, the scale is chosen
+    among SEARCH fractions of the plain one: the fraction whose decoded group has the smallest importance-weighted
+    squared error (imp broadcastable to groups; None weighs every value 1), the earliest fraction among equals."""
+    amax = groups.abs().amax(-1)
+    if not search:
+        scale = _group_scales(amax, g)
+    else:
+        w = imp if imp is not None else torch.ones((), device=groups.device)
+        grid = torch.tensor(E2M1_VALUES, device=groups.device)
+        cand, errs = [], []
+        for frac in SEARCH:
+            sc = _group_scales(amax, g, frac)
+            mag, neg, step = _encode(groups, sc, g)
+            back = grid[mag] * torch.where(neg, -1.0, 1.0) * step
+            errs.append((w * (back - groups) ** 2).sum(-1))
+            cand.append(sc.view(torch.uint8))
+        pick = torch.stack(errs).argmin(0, keepdim=True)
+        scale = torch.stack(cand).gather(0, pick)[0].view(FP8)
+    mag, neg, _ = _encode(groups, scale, g)
+    return _pack(mag, neg), scale.contiguous()
 
 
 def quantize(w: torch.Tensor, global_scale) -> tuple[torch.Tensor, torch.Tensor]:
     """fp32 [rows, cols] and a global scale -> packed uint8 [rows, cols/2] and e4m3 scales [rows, cols/16]."""
     rows, cols = w.shape
-    groups = w.reshape(rows, cols // 16, 16)
     g = torch.as_tensor(global_scale, dtype=torch.float32, device=w.device)
-    scale = _group_scales(groups.abs().amax(-1), g)
-    mag, neg, _ = _encode(groups, scale, g)
-    return _pack(mag, neg, rows, cols), scale.contiguous()
-
-
-SEARCH = (1.0, 0.95, 0.9, 0.85, 0.8, 0.75, 0.7)
+    return _quantize_groups(w.reshape(rows, cols // 16, 16), g)
 
 
 def quantize_search(w: torch.Tensor, global_scale, importance: torch.Tensor | None):
-    """:func:`quantize` with each 16-group's scale chosen among SEARCH fractions of its plain scale: the fraction
-    whose decoded group has the smallest importance-weighted squared error, the earliest fraction among equals
-    (the reference's nvfp4.py:57-94).  importance is per input column; None weighs every column 1."""
+    """:func:`quantize` with each 16-group's scale searched among SEARCH fractions of its plain scale (the
+    reference's nvfp4.py:57-94).  importance is per input column; None weighs every column 1."""
     rows, cols = w.shape
-    groups = w.reshape(rows, cols // 16, 16)
     g = torch.as_tensor(global_scale, dtype=torch.float32, device=w.device)
-    imp = (importance.float().reshape(1, cols // 16, 16) if importance is not None
-           else torch.ones(1, cols // 16, 16, device=w.device))
-    amax = groups.abs().amax(-1)
-    grid = torch.tensor(E2M1_VALUES, device=w.device)
-    cand, errs = [], []
-    for frac in SEARCH:
-        scale = _group_scales(amax, g, frac)
-        mag, neg, step = _encode(groups, scale, g)
-        back = grid[mag] * torch.where(neg, -1.0, 1.0) * step
-        errs.append((imp * (back - groups) ** 2).sum(-1))
-        cand.append(scale.view(torch.uint8))
-    pick = torch.stack(errs).argmin(0, keepdim=True)
-    scale = torch.stack(cand).gather(0, pick)[0].view(FP8)
-    mag, neg, _ = _encode(groups, scale, g)
-    return _pack(mag, neg, rows, cols), scale.contiguous()
+    imp = importance.float().reshape(cols // 16, 16) if importance is not None else None
+    return _quantize_groups(w.reshape(rows, cols // 16, 16), g, imp, search=True)
 
 
 def dequant_fp8(w: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
-    """128x128 block FP8 -> fp32 (the stored value times its block's multiplier)."""
-    o, i = w.shape
-    return (w.float().reshape(o // 128, 128, i // 128, 128) * s.float().reshape(o // 128, 1, i // 128, 1)).reshape(o, i)
+    """128x128 block FP8 [..., R, C] -> fp32 (each stored value times its block's multiplier)."""
+    *lead, o, i = w.shape
+    v = w.float().reshape(-1, o // 128, 128, i // 128, 128) * s.float().reshape(-1, o // 128, 1, i // 128, 1)
+    return v.reshape(*lead, o, i)
 
 
-SEARCH = (1.0, 0.95, 0.9, 0.85, 0.8, 0.75, 0.7)
-
-
-def quantize_search(w: torch.Tensor, global_scale, importance: torch.Tensor | None):
-    """:func:`quantize` with each 16-group's scale picked among SEARCH fractions of its maximum by the smallest
-    importance-weighted squared error (earlier fraction on ties); importance is per input column, None = plain
-    squared error (the reference's nvfp4.py:57-94)."""
-    rows, cols = w.shape
-    groups = w.reshape(rows, cols // 16, 16)
-    g = torch.as_tensor(global_scale, dtype=torch.float32, device=w.device)
-    imp = (importance.float().reshape(1, cols // 16, 16) if importance is not None
-           else torch.ones(1, cols // 16, 16, device=w.device))
-    amax = groups.abs().amax(-1)
-    grid = torch.tensor(E2M1_VALUES, device=w.device)
-    best_err = best = None
-    for frac in SEARCH:
-        scale = (amax / 6.0 * g * frac).clamp(max=448.0).to(FP8)
-        step = (scale.float() / g).unsqueeze(-1)
-        x = torch.where(step > 0, groups / step, torch.zeros_like(groups)).clamp(-6, 6)
-        idx = (x.abs().unsqueeze(-1) - grid).abs().argmin(-1)
-        back = grid[idx] * torch.where(x < 0, -1.0, 1.0) * step
-        err = (imp * (back - groups) ** 2).sum(-1)
-        if best_err is None:
-            best_err, best = err, scale.float()
-        else:
-            better = err < best_err
-            best_err = torch.where(better, err, best_err)
-            best = torch.where(better, scale.float(), best)
-    scale = best.to(FP8)
-    step = (scale.float() / g).unsqueeze(-1)
-    x = torch.where(step > 0, groups / step, torch.zeros_like(groups)).clamp(-6, 6)
-    code = (x.abs().unsqueeze(-1) - grid).abs().argmin(-1)
-    code = (code | ((x < 0).long() << 3)).to(torch.uint8).reshape(rows, cols)
-    return (code[:, 0::2] | (code[:, 1::2] << 4)).contiguous(), scale.contiguous()
+def _prepare_stack(w: torch.Tensor, s: torch.Tensor, device, imp: torch.Tensor | None, chunk: int = 4):
+    """An FP8 expert stack [E, R, C] -> (packed [E, R, C/2], scales [E, R, C/16], g [E]), ``chunk`` experts at a
+    time: every matrix is restored to fp32, g = 448*6/max(amax, 1e-12) per matrix (torch evaluates the quotient as
+    reciprocal(amax) * 2688), then its groups are quantised (searched when ``imp`` [E, C] is given)."""
+    E, R, C = w.shape
+    packed, scales, gs = [], [], []
+    for e0 in range(0, E, chunk):
+        d = dequant_fp8(w[e0:e0 + chunk].to(device), s[e0:e0 + chunk].to(device))
+        n = d.shape[0]
+        g = 448.0 * 6.0 / d.abs().amax((1, 2)).clamp_min(1e-12)
+        im = imp[e0:e0 + n].to(device).float().reshape(n, 1, C // 16, 16) if imp is not None else None
+        p, sc = _quantize_groups(d.reshape(n, R, C // 16, 16), g.view(n, 1, 1), im, search=imp is not None)
+        packed.append(p.cpu())
+        scales.append(sc.cpu())
+        gs.append(g.float().cpu())
+    return torch.cat(packed), torch.cat(scales), torch.cat(gs)
 
 
 def prepare_layer(w13, s13, w2, s2, device, imp_in=None, imp_mid=None, tok=None) -> dict:
@@ -132,9 +123,9 @@ def prepare_layer(w13, s13, w2, s2, device, imp_in=None, imp_mid=None, tok=None)
     (the reference's nvfp4.py:315-331, same arguments and results).
 
     On a CUDA device without importance weights the whole stack goes through the library's preparation kernels
-    (:func:`prismyra_b200.ops.nvfp4_prepare`, bit-identical to the per-expert torch arithmetic below); with
-    importance weights (imp_in for w13's input columns, imp_mid for w2's; experts whose token count ``tok`` is 0
-    fall back to plain squared error) each 16-group's scale is searched as in the reference."""
+    (:func:`prismyra_b200.ops.nvfp4_prepare`, bit-identical to the torch arithmetic of :func:`_prepare_stack`);
+    with importance weights (imp_in for w13's input columns, imp_mid for w2's) each 16-group's scale is searched,
+    experts whose token count ``tok`` is 0 weighing every column 1."""
     dev = torch.device(device)
     if dev.type == "cuda" and imp_in is None:
         out = {}
@@ -142,21 +133,14 @@ def prepare_layer(w13, s13, w2, s2, device, imp_in=None, imp_mid=None, tok=None)
             packed, scale, g = ops.nvfp4_prepare(w.to(dev).contiguous(), s.to(dev, torch.float32).contiguous())
             out["w" + tag], out["s" + tag], out["g" + tag] = packed, scale, g
         return {k: v.cpu() for k, v in out.items()}
-    out = {k: [] for k in ("w1", "s1", "g1", "w2", "s2", "g2")}
-    for e in range(w13.shape[0]):
-        for w, s, tag in ((w13, s13, "1"), (w2, s2, "2")):
-            d = dequant_fp8(w[e].to(device), s[e].to(device))
-            g = 448.0 * 6.0 / d.abs().amax().clamp_min(1e-12)  # torch: d_max.reciprocal() * 2688
-            if imp_in is not None:
-                imp = (imp_in if tag == "1" else imp_mid)[e].to(device)
-                imp = imp if (tok is None or tok[e] > 0) else None
-                packed, scale = quantize_search(d, g, imp)
-            else:
-                packed, scale = quantize(d, g)
-            out["w" + tag].append(packed)
-            out["s" + tag].append(scale)
-            out["g" + tag].append(g.float())
-    return {k: torch.stack(v).cpu() for k, v in out.items()}
+    out = {}
+    for w, s, imp, tag in ((w13, s13, imp_in, "1"), (w2, s2, imp_mid, "2")):
+        if imp is not None:
+            imp = imp.float().clone()
+            if tok is not None:
+                imp[torch.as_tensor(tok) <= 0] = 1.0  # experts without tokens: plain squared error
+        out["w" + tag], out["s" + tag], out["g" + tag] = _prepare_stack(w, s, dev, imp)
+    return out
 
 
 def block_scales(sf: torch.Tensor) -> torch.Tensor:

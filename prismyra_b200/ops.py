@@ -222,11 +222,17 @@ class _HostPipe:
     never freed, so addresses stay stable across calls).  Calls alternate between the two sets, so that one call's
     upload can run while the previous call's layer and download are still in flight; each set carries the events
     after which its input rows may be overwritten (its layer has read them) and its output rows may be overwritten
-    (its download has read them)."""
+    (its download has read them).
+
+    Growing replaces both sets.  The superseded buffers may still be read or written by copies queued on the upload
+    and download streams (and by the layer on the caller's stream), so they are retired -- kept referenced for the
+    life of the process, never handed back to the caching allocator -- rather than dropped: no later allocation on
+    any stream can reuse their memory while those copies run."""
 
     def __init__(self):
         self._lock = threading.Lock()
         self._state = {}
+        self._retired: list = []
 
     def get(self, device: torch.device, T: int, H: int):
         key = (device.index, threading.get_ident())
@@ -238,9 +244,7 @@ class _HostPipe:
                 self._state[key] = st
             if st["rows"] < T or st["H"] != H:
                 for bs in st["sets"]:
-                    for ev in ("x_free", "out_free"):  # a grown buffer set waits for the old one's users
-                        if ev in bs:
-                            torch.cuda.current_stream(device).wait_event(bs[ev])
+                    self._retired.extend(bs[name] for name in ("x", "out") if name in bs)
                     bs.clear()
                     bs["x"] = torch.empty(T, H, dtype=torch.bfloat16, device=device)
                     bs["out"] = torch.empty(T, H, dtype=torch.bfloat16, device=device)

@@ -26,6 +26,14 @@ the code that actually defines it, run on the CPU:
   ``prepare_layer`` with importance weights (one expert with no tokens), and the global scale ``448.0 * 6.0 / t``
   over many maxima (torch evaluates it as ``t.reciprocal() * 2688``, which a true division misses about one time
   in four).
+* ``nvfp4_layer.npz`` -- the whole NVFP4 routed layer as vLLM's NVFP4 emulation MoE computes it
+  (``vllm/model_executor/layers/fused_moe/experts/nvfp4_emulation_moe.py:83-160``): weights prepared by the
+  reference's own ``prepare_layer`` and dequantised by vLLM's ``dequantize_to_dtype`` (times 1/g per expert, bf16),
+  activations quantise-dequantised by vLLM's Triton ``_nvfp4_quant_dequant_kernel`` (global scales
+  448*6/(1.25*amax), the reference's nvfp4.py:125-126), then vLLM's ``fused_moe_kernel`` in bf16 for both GEMMs,
+  ``SiluAndMul.forward_native`` between them and the top-k sum.  The reference itself runs FlashInfer's closed
+  CUTLASS MoE here; this chain is the readable restatement of the same quantised arithmetic (it rounds the
+  dequantised operands to bf16, which the real FP4 GEMM does not, so it pins the layer within the bf16 tolerance).
 """
 
 from __future__ import annotations
@@ -276,6 +284,91 @@ def make_nvfp4_search():
     )
 
 
+def _triton_gemm_bf16(a, w, c, weights, sorted_ids, expert_ids, npp, top_k, mul_routed_weight, bm):
+    """vLLM's fused_moe_kernel with bf16 operands (no quantisation), as TritonExperts runs it after the NVFP4
+    emulation has dequantised the weights.  The Triton CPU interpreter's dot multiplies bf16 operands as their raw
+    16-bit patterns, so the operands are handed over as fp32 copies of the same bf16 values: every product of two
+    bf16 values is exact in fp32 and the sum is an fp32 accumulation, which is what the compiled kernel's bf16
+    tensor-core dot computes.  This corrects the tool, not the kernel being interpreted."""
+    import triton
+    import triton.language as tl
+    from vllm.model_executor.layers.fused_moe import fused_moe as fm
+
+    E, N, K = w.shape
+    a, w = a.float().contiguous(), w.float().contiguous()
+    em = sorted_ids.numel()
+    bn = 64
+    grid = (triton.cdiv(em, bm) * triton.cdiv(N, bn),)
+    fm.fused_moe_kernel[grid](
+        a, w, c, None, None, None, weights, sorted_ids, expert_ids, npp,
+        N, K, em, weights.numel(),
+        a.stride(0), a.stride(1), w.stride(0), w.stride(2), w.stride(1), c.stride(-2), c.stride(-1),
+        0, 0, 0, 0, 0, 0, 0,
+        group_n=0, group_k=0, naive_block_assignment=False,
+        BLOCK_SIZE_M=bm, BLOCK_SIZE_N=bn, BLOCK_SIZE_K=64, GROUP_SIZE_M=1, SPLIT_K=1,
+        MUL_ROUTED_WEIGHT=mul_routed_weight, top_k=top_k, compute_type=tl.bfloat16, use_fp8_w8a8=False,
+        use_int8_w8a8=False, use_int8_w8a16=False, per_channel_quant=False, HAS_BIAS=False,
+    )
+
+
+def make_nvfp4_layer(seed: int = 13, T: int = 24, H: int = 256, I: int = 256, E: int = 8, k: int = 4):
+    from prismyra.kernels.nvfp4 import prepare_layer
+    from vllm.model_executor.layers.activation import SiluAndMul
+    from vllm.model_executor.layers.quantization.utils.nvfp4_emulation_utils import (
+        _triton_nvfp4_quant_dequant, dequantize_to_dtype)
+
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    x[4] = 0.0  # an all-zero token: every group scale is 0
+    logits = torch.randn(T, E, generator=g)
+    logits[:, 2] -= 40.0  # expert 2 receives no token
+    logits = logits.to(torch.bfloat16)
+    w13, s13 = _fp8_blocks(torch.randn(E, 2 * I, H, generator=g) * 0.02)
+    w2f, s2f = _fp8_blocks(torch.randn(E, H, I, generator=g) * 0.02)
+    prep = prepare_layer(w13, s13, w2f, s2f, "cpu")
+
+    probs = torch.softmax(logits.float(), dim=-1)
+    top_w, top_i = torch.topk(probs, k, dim=-1)
+    top_w = top_w / top_w.sum(-1, keepdim=True)
+    top_i = top_i.to(torch.int32)
+
+    # synthetic calibration: the activation maxima the reference reads from its calibration file
+    a1_amax = float(x.float().abs().max())
+    w1d = _fp8_deq(w13, s13)
+    h = torch.einsum("th,tkih->tki", x.float(), w1d[top_i.long()])
+    a2_amax = float((torch.nn.functional.silu(h[..., :I]) * h[..., I:]).abs().max())
+    a1_gs = torch.tensor([448.0 * 6.0 / (1.25 * a1_amax)], dtype=torch.float32)
+    a2_gs = torch.tensor([448.0 * 6.0 / (1.25 * a2_amax)], dtype=torch.float32)
+
+    w1_dq = dequantize_to_dtype(prep["w1"], prep["s1"].view(torch.uint8), 1.0 / prep["g1"], torch.bfloat16,
+                                16, swizzle=False)
+    w2_dq = dequantize_to_dtype(prep["w2"], prep["s2"].view(torch.uint8), 1.0 / prep["g2"], torch.bfloat16,
+                                16, swizzle=False)
+    bm = 16
+    sorted_ids, expert_ids, npp = _align(top_i.flatten(), E, bm)
+    x_dq = _triton_nvfp4_quant_dequant(x, a1_gs, 16)
+    c1 = torch.zeros(T, k, 2 * I, dtype=torch.bfloat16)
+    _triton_gemm_bf16(x_dq, w1_dq, c1, top_w.flatten().contiguous(), sorted_ids, expert_ids, npp, k, False, bm)
+    c2 = SiluAndMul.forward_native(c1.view(-1, 2 * I))
+    c2_dq = _triton_nvfp4_quant_dequant(c2.contiguous(), a2_gs, 16)
+    c3 = torch.zeros(T * k, H, dtype=torch.bfloat16)
+    _triton_gemm_bf16(c2_dq, w2_dq, c3, top_w.flatten().contiguous(), sorted_ids, expert_ids, npp, 1, True, bm)
+    out = c3.view(T, k, H).sum(dim=1)
+
+    np.savez_compressed(
+        OUT / "nvfp4_layer.npz",
+        x=_bits(x), logits=_bits(logits), w1=_bits(prep["w1"]), s1=_bits(prep["s1"]), g1=_bits(prep["g1"]),
+        w2=_bits(prep["w2"]), s2=_bits(prep["s2"]), g2=_bits(prep["g2"]), a1_gs=_bits(a1_gs), a2_gs=_bits(a2_gs),
+        top_w=_bits(top_w.float()), top_i=_bits(top_i), x_dq=_bits(x_dq), c1=_bits(c1), c2=_bits(c2),
+        c2_dq=_bits(c2_dq), c3=_bits(c3), out=_bits(out), k=np.int32(k),
+    )
+
+
+def _fp8_deq(q: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+    e, r, c = q.shape
+    return (q.float().view(e, r // 128, 128, c // 128, 128) * s.view(e, r // 128, 1, c // 128, 1)).view(e, r, c)
+
+
 if __name__ == "__main__":
     if not any("reference" in p for p in sys.path):
         print("note: PYTHONPATH should hold the reference checkout for the NVFP4 fixtures", file=sys.stderr)
@@ -283,11 +376,15 @@ if __name__ == "__main__":
         make_nvfp4_search()
         sys.exit(0)
     _patch_interpreter_rounding()
+    if sys.argv[1:] == ["nvfp4_layer"]:
+        make_nvfp4_layer()
+        sys.exit(0)
     make_align_kat()
     make_router()
     make_quant_edges()
     make_fp8_layer()
     make_nvfp4()
     make_nvfp4_search()
+    make_nvfp4_layer()
     for f in sorted(OUT.glob("*.npz")):
         print(f.name, f.stat().st_size)

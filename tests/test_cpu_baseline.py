@@ -23,5 +23,9 @@ def test_fallback_runs_and_agrees_with_the_oracle():
     r = O.bf16_to_f32(ref).astype(np.float64)
     rel = np.linalg.norm(y.double().numpy() - r) / np.linalg.norm(r)
     assert rel < 8e-2  # FP8 activation quantisation (e4m3, 3 mantissa bits) is the only difference
-    t = torch_fallback.time_routed(router, experts, L["x"].float(), min_seconds=0.05, max_iters=3)
-    assert t["tokens_per_s"] > 0 and t["calls"] >= 1
+    t = torch_fallback.time_routed(router, experts, L["x"].float(), max_seconds=0.05, max_calls=6)
+    assert t["tokens_per_s"] > 0 and 5 <= t["calls"] <= 6 and t["warmup"] == 2
+    assert t["tokens_per_s"] == L["x"].shape[0] / t["median_s"] and t["cpu_model"]
+    rb, eb = torch_fallback.build_block(L["router_w"].float(), w1, w2, 4, dtype=torch.bfloat16)
+    tb = torch_fallback.time_routed(rb, eb, L["x"], max_seconds=0.05)
+    assert tb["dtype"] == "bfloat16" and tb["tokens_per_s"] > 0

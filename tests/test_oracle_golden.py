@@ -205,6 +205,58 @@ def test_nvfp4_act_quant_matches_vllm_emulation(golden):
     assert np.array_equal(deq.astype(np.float32), g["act_dequant"])
 
 
+def _nvfp4_layer_case(golden):
+    g = golden("nvfp4_layer")
+    a1, a2 = float(g["a1_gs"][0]), float(g["a2_gs"][0])
+    # alpha = 1/(g_w * a_gs) per expert, fp32 (reference prismyra/kernels/nvfp4.py:141-142)
+    al1 = (np.float32(1.0) / (g["g1"] * np.float32(a1)).astype(np.float32)).astype(np.float32)
+    al2 = (np.float32(1.0) / (g["g2"] * np.float32(a2)).astype(np.float32)).astype(np.float32)
+    return g, a1, a2, al1, al2
+
+
+def _rel(got_bits, ref_bits):
+    a = O.bf16_to_f32(got_bits).astype(np.float64)
+    b = O.bf16_to_f32(ref_bits).astype(np.float64)
+    return np.linalg.norm(a - b) / np.linalg.norm(b), np.abs(a - b).max() / np.abs(b).max()
+
+
+def test_nvfp4_layer_stages_match_vllm_emulation(golden):
+    """The oracle's NVFP4 layer against vLLM's NVFP4 emulation MoE (nvfp4_emulation_moe.py:83-160) stage by stage:
+    the activation quantise-dequantise bit-exact, the gate_up GEMM within 1e-2, the requantisation of the same
+    silu*mul rows bit-exact, and the down GEMM times the routing weight on vLLM's own requantised rows within 1e-2.
+    The emulation rounds its dequantised operands to bf16 (2^-9 relative), which the FP4 GEMM does not."""
+    g, a1, a2, al1, al2 = _nvfp4_layer_case(golden)
+    k = int(g["k"])
+    T, H = g["x"].shape
+    rows = np.repeat(np.arange(T), k)
+    re = g["top_i"].reshape(-1)
+    w, ids = O.route_topk(g["logits"], k)
+    assert np.array_equal(ids, g["top_i"])
+    np.testing.assert_allclose(w, g["top_w"], rtol=1e-6)
+    xq, xsf = O.nvfp4_quant_act(g["x"], a1)
+    assert np.array_equal(O.f32_to_bf16(O.nvfp4_dequant(xq, xsf, a1)), g["x_dq"])
+    c1 = O.f32_to_bf16(O.gemm_nvfp4_rows(xq[rows], xsf[rows], re, g["w1"], g["s1"], al1))
+    l2, mx = _rel(c1, g["c1"].reshape(T * k, -1))
+    assert l2 < 1e-2 and mx < 1e-2, (l2, mx)
+    c2 = g["c2"].reshape(T * k, -1)
+    q2, s2 = O.nvfp4_quant_act(c2, a2)
+    assert np.array_equal(O.f32_to_bf16(O.nvfp4_dequant(q2, s2, a2)), g["c2_dq"].reshape(T * k, -1))
+    c3 = O.gemm_nvfp4_rows(q2, s2, re, g["w2"], g["s2"], al2) * g["top_w"].reshape(-1)[:, None]
+    l2, mx = _rel(O.f32_to_bf16(c3), g["c3"])
+    assert l2 < 1e-2 and mx < 1e-2, (l2, mx)
+
+
+def test_nvfp4_layer_end_to_end_matches_vllm_emulation(golden):
+    """The whole oracle NVFP4 layer against the emulation's output.  The two chains differ before the requantisation
+    of the silu*mul rows only by the emulation's bf16 operand rounding, but that requantisation is discontinuous: a
+    1-ulp difference in a row moves about 1% of its e2m1 codes by a whole step and about 3% of its group scales by
+    an e4m3 step, so the end-to-end bound is 5e-2 (each stage is within 1e-2, test above)."""
+    g, a1, a2, al1, al2 = _nvfp4_layer_case(golden)
+    r = O.moe_forward_nvfp4(g["x"], g["logits"], g["w1"], g["s1"], g["w2"], g["s2"], al1, al2, a1, a2, int(g["k"]))
+    l2, mx = _rel(r["out"], g["out"])
+    assert l2 < 5e-2 and mx < 5e-2, (l2, mx)
+
+
 @pytest.mark.parametrize("n", [0, 1, 37])
 def test_conversions_round_to_nearest_even(n):
     rng = np.random.default_rng(n)
