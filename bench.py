@@ -213,6 +213,54 @@ def time_region(fn, steps: int, stream) -> float:
     return a.elapsed_time(b) / steps
 
 
+def vllm_gpu_path(layer: dict, tokens: list, steps: int, ours: dict) -> dict:
+    """The reference's own GPU path for the routed layer on this box (prismyra/kernels/qwen3_moe.py:184-197): vLLM's
+    batch-invariant router matmul, fused_topk and fused_experts (FP8 w8a8, 128x128 block scales) on the same seeded
+    tensors, timed with CUDA events like the layer; ``ours`` maps a token count to this repository's ms per call
+    for the same shape.  Also the relative L2 difference of the two outputs (each with its own router)."""
+    import torch
+
+    from prismyra_b200 import ops
+
+    try:
+        from vllm.model_executor.layers.fused_moe import fused_experts, fused_topk
+        from vllm.model_executor.layers.fused_moe.config import FusedMoEQuantConfig
+        try:
+            from vllm.model_executor.layers.batch_invariant import linear_batch_invariant as router_linear
+        except ImportError:
+            router_linear = torch.nn.functional.linear
+        quant = FusedMoEQuantConfig.make(quant_dtype=torch.float8_e4m3fn, block_shape=[128, 128],
+                                         w1_scale=layer["w1_s"], w2_scale=layer["w2_s"])
+    except Exception as e:  # noqa: BLE001 - reported, not fatal: the comparison is optional
+        return {"unavailable": f"vllm does not import here: {type(e).__name__}: {e}"[:300]}
+    stream = torch.cuda.current_stream()
+    res = {"path": "vllm " + __import__("vllm").__version__ + ": linear_batch_invariant + fused_topk + "
+                   "fused_experts (FP8 w8a8 block 128x128)"}
+    for T in tokens:
+        x = layer["x"][:T].contiguous()
+
+        def step():
+            logits = router_linear(x, layer["router_w"])
+            w, ids = fused_topk(x, logits, K, renormalize=True)[:2]
+            return fused_experts(x, layer["w1"], layer["w2"], w, ids, quant_config=quant)
+
+        try:
+            ref_out = step()
+            for _ in range(3):
+                step()
+            ms = time_region(step, 20, stream)
+        except Exception as e:  # noqa: BLE001
+            res[f"t{T}"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+            continue
+        mine = ops.forward_fp8(x, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K,
+                               router_w=layer["router_w"]).float()
+        rel = float((mine - ref_out.float()).norm() / ref_out.float().norm().clamp_min(1e-30))
+        res[f"t{T}"] = {"ms": ms, "tokens_per_s": T / (ms * 1e-3), "ours_ms": ours.get(T),
+                        "speedup_ours_over_vllm": (ms / ours[T]) if ours.get(T) else None,
+                        "rel_l2_ours_vs_vllm": rel}
+    return res
+
+
 def stage_times(layer: dict, T: int, reps: int = 20) -> dict:
     """Per-stage device time (ms) of one forward, each stage re-run alone on preallocated buffers and timed with
     CUDA events on the launching stream."""
@@ -477,6 +525,10 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
                  "shared_ms_over_routed": blk_ms - ms,
                  "tflops": (fl["total"] + shared_flops) / (blk_ms * 1e-3) / 1e12}
 
+    vllm_ref = None
+    if world == 1 and not args.no_vllm:
+        vllm_ref = vllm_gpu_path(layer, [T_CTX, T_BRANCH], args.steps, {T_CTX: ms, T_BRANCH: b_ms})
+
     if world > 1:
         ep_layer.close()  # every rank together: frees this layer's exchange before the stack makes its own
     stack_ms, stack_peak = ep_stack(dev, rank, world, args.stack_layers, 4096, max(2, args.steps // 20))
@@ -525,6 +577,8 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
     line["nvfp4_prepare"] = prep
     if block is not None:
         line["block_t5120"] = block
+    if vllm_ref is not None:
+        line["vllm_gpu_same_box"] = vllm_ref
     if cb is not None:
         line["cpu_baseline"] = cb
     print(json.dumps(line), flush=True)
@@ -537,6 +591,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-vllm", action="store_true", help="skip timing the reference's vLLM GPU path")
     ap.add_argument("--stack-layers", type=int, default=36)
     args = ap.parse_args()
     if args.impl == "reference":

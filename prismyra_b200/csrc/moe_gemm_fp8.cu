@@ -3,21 +3,31 @@
 // Arithmetic (vLLM fused_moe_kernel, fused_moe.py:483-548, the kernel the reference's FusedExperts calls):
 //   acc = sum over 128-wide K blocks kb of  (A_q[row, kb] . B_q[n, kb]) * a_scale[row, kb] * b_scale[n/128, kb]
 // The block scales are fp32 (not powers of two), so the tensor core cannot apply them: every K block is one
-// tcgen05 MMA chain into a fresh TMEM accumulator, and the epilogue warps promote it into fp32 registers with the
+// tcgen05 MMA chain into a fresh TMEM accumulator, and the promotion warps add it into fp32 registers with the
 // block's scale ("software promotion").  Two TMEM accumulators alternate so the MMA of block kb+1 runs while
 // block kb is being promoted.
 //
 // Tiles: 128 rows (one alignment block, one expert) x 256 columns x 128 K per pipeline stage.
 //   mode 0 (gate_up, K = H): A is the expert-ordered FP8 copy of x written by the quantisation kernel.  The 256
-//           columns are 128 gate rows n0.. and the matching 128 up rows I+n0..,
-//           the epilogue applies bf16 -> silu(gate)*up -> bf16 and re-quantises to e4m3 with one scale per
-//           128 output columns (exactly one tile), writing the down GEMM's A operand in slot order.
+//           columns are 128 gate rows n0.. and the matching 128 up rows I+n0..; the epilogue applies
+//           bf16 -> silu(gate)*up -> bf16 and re-quantises to e4m3 with one scale per 128 output columns (exactly one
+//           tile), writing the down GEMM's A operand in slot order.
 //   mode 1 (down, K = I): the 256 columns are hidden columns n0..n0+255; the epilogue multiplies by the routing
-//           weight in fp32, rounds to bf16 and scatters the row to c3[flat index].
-// Warp roles (384 threads, three warpgroups): warp 0 issues TMA loads, warp 1 owns TMEM and issues the MMAs
-// (warps 2-3 idle); warpgroups 1 and 2 (warps 4-11) promote and run the epilogue.  Epilogue warp w reads TMEM
-// lanes 32*(w%4).. and one half of the tile's columns.  Registers are rebalanced with setmaxnreg: 40 for
-// warpgroup 0 and 232 for the epilogue warpgroups (40*128 + 232*256 = 64512 = 168 * 384, the launch's total).
+//           weight in fp32, rounds to bf16 and writes the row to c3[flat index] (or to a per-row destination).
+//
+// Warp roles (384 threads, three warpgroups):
+//   warp 0       TMA producer (A and B tiles of each K block into the stage ring);
+//   warp 1       TMEM owner and MMA issuer (one elected lane);
+//   warps 2-3    scale loaders: for every tile, in chunks of 16 K blocks, the 128 rows' activation scales and the
+//                tile's two weight-scale rows go into a double-buffered shared-memory ring, transposed to
+//                [K block][row] so that a promotion warp reads its 32 rows' scales of one K block without bank
+//                conflicts.  The scales are thus loaded well ahead of use, off the promotion warps' critical path;
+//   warps 4-11   promotion and epilogue: warp w reads TMEM lanes 32*(w%4).. and one half of the tile's columns
+//                (two 32-column TMEM loads per wait; the accumulator goes back to the MMA once the last loads have
+//                landed), adds each K block into 128 fp32 registers per thread, then runs the tile's epilogue.
+// Registers are rebalanced with setmaxnreg: 64 for warpgroup 0 (the scale loaders hold a chunk's 32 scales) and
+// 216 for the promotion warpgroups (64*128 + 216*256 = 63488 <= 168*384, the launch's total).
+// Every wait is bounded (ptx.cuh): on timeout the kernel raises its abort flag, unwinds and reports through err.
 #include <atomic>
 
 #include "moe_internal.h"
@@ -28,9 +38,9 @@ namespace {
 
 constexpr int kBM = 128, kBN = 256, kBK = 128;
 template <int MODE> struct Cfg {
-    // gate_up keeps four pipeline stages; down gives one up for the 64 KB bf16 staging of its output rows.
+    // gate_up keeps four pipeline stages; down gives one up for the bf16 staging of its output rows.
     static constexpr int kStages = MODE == 0 ? 4 : 3;
-    static constexpr int kStageRowBytes = 272;  // 128 bf16 + 16 B pad: conflict-free row-per-thread writes
+    static constexpr int kStageRowBytes = 144;  // 64 bf16 + 16 B pad: conflict-free row-per-thread writes
     static constexpr int kStagingBytes = MODE == 0 ? 0 : 8 * 32 * kStageRowBytes;
 };
 constexpr int kMaxStages = 4;
@@ -38,23 +48,32 @@ constexpr int kABytes = kBM * kBK;          // 16 KB
 constexpr int kBBytes = kBN * kBK;          // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kThreads = 384;
-constexpr int kEpiWarp0 = 4;          // first epilogue warp
+constexpr int kLoadWarp0 = 2;               // scale loader warps 2-3
+constexpr int kLoadThreads = 64;
+constexpr int kEpiWarp0 = 4;                // first promotion / epilogue warp
 constexpr int kEpiWarps = 8;
-constexpr uint32_t kTmemCols = 512;
-constexpr int kEidCache = 512;              // tiles per CTA whose expert ids are staged in shared memory         // two 256-column fp32 accumulators
+constexpr int kChunk = 16;                  // K blocks per scale chunk
+constexpr uint32_t kTmemCols = 512;         // two 256-column fp32 accumulators
 constexpr uint32_t kIdesc = idesc_f32acc(0 /*e4m3*/, 0 /*e4m3*/, kBM, kBN);
+
+struct ScaleSlot {
+    float a[kChunk][kBM];   // activation scale of row r for K block c0 + j, at a[j][r]
+    float b[2][kChunk];     // the tile's two weight-scale rows (gate / up groups, or the two column halves)
+};
 
 struct SmemTail {
     uint64_t full[kMaxStages];
     uint64_t empty[kMaxStages];
     uint64_t tfull[2];
     uint64_t tempty[2];
+    uint64_t sc_full[2];    // scale slot filled (arrived by the 64 loader threads)
+    uint64_t sc_empty[2];   // scale slot read (arrived by the 8 promotion warps)
     uint64_t drain;
-    uint64_t xbar[2];         // epilogue amax exchange, one per tile parity
+    uint64_t xbar[2];       // epilogue amax exchange, one per tile parity
     uint32_t tmem_base;
     int abort;
-    int eid[kEidCache];  // expert of this CTA's j-th tile, j < kEidCache
     float amax_x[2][2][kBM];  // [tile parity][column half][row]
+    ScaleSlot sc[2];
 };
 
 template <int MODE>
@@ -62,30 +81,37 @@ constexpr size_t smem_bytes() {
     return 1024 /*alignment slack*/ + (size_t)Cfg<MODE>::kStages * kStageBytes + Cfg<MODE>::kStagingBytes +
            sizeof(SmemTail);
 }
+static_assert(smem_bytes<0>() <= 227 * 1024 && smem_bytes<1>() <= 227 * 1024, "shared memory per CTA");
 
 // silu(g) * u on bf16 values with bf16 rounding after each step (vLLM silu_and_mul semantics) is computed pairwise
 // in the gate_up epilogue.  The sigmoid comes from the hardware tanh (relative error below 2^-11): the result is
 // rounded to bf16 (8 significant bits) right after, so the error changes an output only when it straddles a bf16
 // rounding boundary, and then by one bf16 unit before the e4m3 requantisation.
 
-// acc[c] += scale * TMEM[lane, col + c] for 32 consecutive columns, as packed fp32x2 FMAs when PACKED.
+// acc[c] += scale * r[c] for two runs of 32 values (r0 -> acc0, r1 -> acc1) just loaded from TMEM: packed fp32x2
+// FMAs when PACKED.
 template <bool PACKED>
-__device__ __forceinline__ void promote32(uint32_t taddr, float scale, float* acc) {
-    uint32_t r[32];
-    tmem_ld32(taddr, r);
-    tmem_ld_wait();
+__device__ __forceinline__ void fma2x32(const uint32_t (&r0)[32], const uint32_t (&r1)[32], float scale, float* acc0,
+                                        float* acc1) {
     if (PACKED) {
         const float2 s2 = make_float2(scale, scale);
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-            const float2 v = __ffma2_rn(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), s2,
-                                        make_float2(acc[i], acc[i + 1]));
-            acc[i] = v.x;
-            acc[i + 1] = v.y;
+            const float2 v0 = __ffma2_rn(make_float2(__uint_as_float(r0[i]), __uint_as_float(r0[i + 1])), s2,
+                                         make_float2(acc0[i], acc0[i + 1]));
+            const float2 v1 = __ffma2_rn(make_float2(__uint_as_float(r1[i]), __uint_as_float(r1[i + 1])), s2,
+                                         make_float2(acc1[i], acc1[i + 1]));
+            acc0[i] = v0.x;
+            acc0[i + 1] = v0.y;
+            acc1[i] = v1.x;
+            acc1[i + 1] = v1.y;
         }
     } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = fmaf(__uint_as_float(r[i]), scale, acc[i]);
+        for (int i = 0; i < 32; ++i) {
+            acc0[i] = fmaf(__uint_as_float(r0[i]), scale, acc0[i]);
+            acc1[i] = fmaf(__uint_as_float(r1[i]), scale, acc1[i]);
+        }
     }
 }
 
@@ -110,6 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t bar_full = smem_u32(tail->full), bar_empty = smem_u32(tail->empty);
     const uint32_t bar_tfull = smem_u32(tail->tfull), bar_tempty = smem_u32(tail->tempty);
+    const uint32_t bar_scf = smem_u32(tail->sc_full), bar_sce = smem_u32(tail->sc_empty);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -119,6 +146,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int b = 0; b < 2; ++b) {
             mbar_init(bar_tfull + 8 * b, 1);
             mbar_init(bar_tempty + 8 * b, kEpiWarps);
+            mbar_init(bar_scf + 8 * b, kLoadThreads);
+            mbar_init(bar_sce + 8 * b, kEpiWarps);
         }
         mbar_init(smem_u32(&tail->drain), 1);
         mbar_init(smem_u32(&tail->xbar[0]), kEpiWarps * 32);
@@ -144,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int num_tiles = (*args.num_post_pad / kBM) * args.n_tiles;
 
     if (warp < kEpiWarp0) {
-      asm volatile("setmaxnreg.dec.sync.aligned.u32 40;" ::: "memory");
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 64;" ::: "memory");
       if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer
         int stage = 0;
@@ -163,13 +192,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t a_dst = sbase + stage * kStageBytes;
                 const uint32_t b_dst = a_dst + kABytes;
                 const uint32_t fb = bar_full + 8 * stage;
-                if (lane == 0) mbar_arrive_expect_tx(fb, kStageBytes);
-                __syncwarp();
                 if (lane == 0) {
+                    mbar_arrive_expect_tx(fb, kStageBytes);
                     tma_load_2d(a_dst, &tm_a, fb, kb * kBK, mb * kBM);
                     tma_load_2d(b_dst, &tm_b, fb, kb * kBK, row0);
                     tma_load_2d(b_dst + kBBytes / 2, &tm_b, fb, kb * kBK, row1);
                 }
+                __syncwarp();
                 if (++stage == kStages) { stage = 0; phase ^= 1u; }
             }
         }
@@ -213,90 +242,115 @@ __global__ void __launch_bounds__(kThreads, 1)
             while (!mbar_try_wait(smem_u32(&tail->drain), 0) && globaltimer() - t0 < PM_WAIT_TIMEOUT_NS) {
             }
         }
+      } else {
+        // ------------------------------------------------------------------ scale loaders (warps 2-3)
+        // Thread t fills rows t and t+64 of a chunk; threads 0..15 also the two weight-scale rows.
+        const int t = threadIdx.x - kLoadWarp0 * 32;
+        const int nb_total = args.n_total / 128;
+        uint32_t chunk = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+            const int mb = tile / args.n_tiles, nt = tile % args.n_tiles;
+            const int e = args.expert_ids[mb];
+            const float* bs = args.b_scale + (size_t)e * nb_total * KB;
+            const float* brow0 = bs + (size_t)(MODE == 0 ? nt : nt * 2) * KB;
+            const float* brow1 = bs + (size_t)(MODE == 0 ? args.inter / 128 + nt : nt * 2 + 1) * KB;
+            const float* as0 = args.a_scale + (size_t)(mb * kBM + t) * KB;
+            const float* as1 = as0 + (size_t)64 * KB;
+            for (int c0 = 0; c0 < KB; c0 += kChunk, ++chunk) {
+                const uint32_t slot = chunk & 1u, use = chunk >> 1;
+                const int n = KB - c0 < kChunk ? KB - c0 : kChunk;
+                float v0[kChunk], v1[kChunk];
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) {  // the loads are issued before the slot is waited for
+                    v0[j] = j < n ? as0[c0 + j] : 0.0f;
+                    v1[j] = j < n ? as1[c0 + j] : 0.0f;
+                }
+                float b0 = 0.0f, b1 = 0.0f;
+                if (t < n) {
+                    b0 = brow0[c0 + t];
+                    b1 = brow1[c0 + t];
+                }
+                if (!mbar_wait(bar_sce + 8 * slot, (use & 1u) ^ 1u, abort)) { ok = false; break; }
+                ScaleSlot& S = tail->sc[slot];
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) {
+                    S.a[j][t] = v0[j];
+                    S.a[j][t + 64] = v1[j];
+                }
+                if (t < kChunk) {
+                    S.b[0][t] = b0;
+                    S.b[1][t] = b1;
+                }
+                mbar_arrive(bar_scf + 8 * slot);
+            }
+        }
       }
     } else {
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 232;" ::: "memory");
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 216;" ::: "memory");
         // ------------------------------------------------------------------ promotion + epilogue
         const int q = warp & 3;                    // TMEM lane quarter
         const int half = (warp - kEpiWarp0) >> 2;  // column half
         const int row = q * 32 + lane;
         const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
-        const int nb_total = args.n_total / 128;
         // Packed FMAs halve the promotion's issue slots; in the down GEMM they cost spills, so it stays scalar.
         constexpr bool kPackedPromote = MODE == 0;
-        uint32_t it = 0;
+        uint32_t it = 0, chunk = 0;
         int local = 0;
         float acc[128];
-        // Per-tile inputs are fetched ahead so that no tile starts on a dependent chain of global loads: the
-        // experts of this CTA's tiles are staged in shared memory once, the next tile's first K block scales are
-        // loaded during the last K block, and (down) the row's flat index at the start of the tile and its routing
-        // weight during the second K block.  Later tiles than the staged ones read their expert from global memory.
-        const int ptid = threadIdx.x - kEpiWarp0 * 32;
-        for (int j = ptid; j < kEidCache; j += kEpiWarps * 32) {
-            const long long t = blockIdx.x + (long long)j * gridDim.x;
-            tail->eid[j] = t < num_tiles ? args.expert_ids[t / args.n_tiles] : 0;
-        }
-        named_bar_sync(1, kEpiWarps * 32);
-        float sa_n = 0.0f, b0_n = 0.0f, b1_n = 0.0f;  // scales of the next K block to promote
-        if (blockIdx.x < num_tiles) {
-            const int e = tail->eid[0], nt = blockIdx.x % args.n_tiles;
-            const float* bs = args.b_scale + (size_t)e * nb_total * KB;
-            sa_n = args.a_scale[(size_t)((blockIdx.x / args.n_tiles) * kBM + row) * KB];
-            b0_n = bs[(size_t)(MODE == 0 ? nt : nt * 2 + half) * KB];
-            b1_n = bs[(size_t)(MODE == 0 ? args.inter / 128 + nt : nt * 2 + half) * KB];
-        }
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
             const int mb = tile / args.n_tiles, nt = tile % args.n_tiles;
-            const int e = local < kEidCache ? tail->eid[local] : args.expert_ids[mb];
             const int grow = mb * kBM + row;
-            const float* bs = args.b_scale + (size_t)e * nb_total * KB;
-            const float* as = args.a_scale + (size_t)grow * KB;
-            // the two block-scale rows this thread multiplies by (gate/up halves, or its column half)
-            const float* bs0 = bs + (size_t)(MODE == 0 ? nt : nt * 2 + half) * KB;
-            const float* bs1 = bs + (size_t)(MODE == 0 ? args.inter / 128 + nt : nt * 2 + half) * KB;
-            // down: the row's flat index (the slot itself when there is no row map) and, with a destination table,
-            // the address its weighted row is stored to (0: the slot holds no row)
+            // down: the row's flat index (the slot itself when there is no row map), its routing weight and, with a
+            // destination table, the address its weighted row is stored to (0: the slot holds no row)
             const int flat = MODE == 1 ? (args.sorted_ids != nullptr ? args.sorted_ids[grow] : grow) : 0;
             const uint64_t drow = (MODE == 1 && EPI == kEpiDstRows) ? args.dst_rows[grow] : 0;
             float w = 0.0f;
 #pragma unroll
             for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
             bool ok = true;
+            const ScaleSlot* S = nullptr;
             for (int kb = 0; kb < KB; ++kb, ++it) {
                 const uint32_t buf = it & 1u, use = it >> 1;
-                const float s0 = sa_n * b0_n, s1 = sa_n * b1_n;
-                if (kb + 1 < KB) {
-                    sa_n = as[kb + 1];
-                    b0_n = bs0[kb + 1];
-                    b1_n = bs1[kb + 1];
-                } else if (tile + (int)gridDim.x < num_tiles) {
-                    const int t2 = tile + gridDim.x, j2 = local + 1;
-                    const int m2 = t2 / args.n_tiles, n2 = t2 % args.n_tiles;
-                    const int e2 = j2 < kEidCache ? tail->eid[j2] : args.expert_ids[m2];
-                    const float* bs2 = args.b_scale + (size_t)e2 * nb_total * KB;
-                    sa_n = args.a_scale[(size_t)(m2 * kBM + row) * KB];
-                    b0_n = bs2[(size_t)(MODE == 0 ? n2 : n2 * 2 + half) * KB];
-                    b1_n = bs2[(size_t)(MODE == 0 ? args.inter / 128 + n2 : n2 * 2 + half) * KB];
+                const int j = kb % kChunk;
+                if (j == 0) {
+                    if (!mbar_wait(bar_scf + 8 * (chunk & 1u), (chunk >> 1) & 1u, abort)) { ok = false; break; }
+                    S = &tail->sc[chunk & 1u];
+                }
+                const float sa = S->a[j][row];
+                const float s0 = sa * S->b[MODE == 0 ? 0 : half][j];
+                const float s1 = sa * S->b[MODE == 0 ? 1 : half][j];
+                if (j == kChunk - 1 || kb == KB - 1) {  // this chunk's scales have been read
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar_sce + 8 * (chunk & 1u));
+                    ++chunk;
                 }
                 if (MODE == 1 && kb == (KB > 1 ? 1 : 0)) w = flat < args.n_valid ? args.topk_w[flat] : 0.0f;
                 if (!mbar_wait(bar_tfull + 8 * buf, use & 1u, abort)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t tb = t_lane + buf * kBN;
-                if (MODE == 0) {
-                    // gate columns [64*half, 64*half+64) and up columns [128+64*half, ...+64) of the tile
-                    promote32<kPackedPromote>(tb + 64 * half, s0, acc);
-                    promote32<kPackedPromote>(tb + 64 * half + 32, s0, acc + 32);
-                    promote32<kPackedPromote>(tb + 128 + 64 * half, s1, acc + 64);
-                    promote32<kPackedPromote>(tb + 128 + 64 * half + 32, s1, acc + 96);
-                } else {
-                    promote32<kPackedPromote>(tb + 128 * half, s0, acc);
-                    promote32<kPackedPromote>(tb + 128 * half + 32, s0, acc + 32);
-                    promote32<kPackedPromote>(tb + 128 * half + 64, s0, acc + 64);
-                    promote32<kPackedPromote>(tb + 128 * half + 96, s0, acc + 96);
+                // this thread's 128 columns: mode 0 gate columns [64*half, +64) then up columns [128+64*half, +64);
+                // mode 1 columns [128*half, +128).  Two 32-column TMEM loads per wait; the accumulator is handed
+                // back to the MMA as soon as the last load has landed, before that pair's FMAs.
+                const uint32_t c0 = MODE == 0 ? 64 * half : 128 * half;
+                const uint32_t c1 = MODE == 0 ? 128 + 64 * half : 128 * half + 64;
+                {
+                    uint32_t r0[32], r1[32];
+                    tmem_ld32(tb + c0, r0);
+                    tmem_ld32(tb + c0 + 32, r1);
+                    tmem_ld_wait();
+                    fma2x32<kPackedPromote>(r0, r1, s0, acc, acc + 32);
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar_tempty + 8 * buf);
+                {
+                    uint32_t r0[32], r1[32];
+                    tmem_ld32(tb + c1, r0);
+                    tmem_ld32(tb + c1 + 32, r1);
+                    tmem_ld_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar_tempty + 8 * buf);
+                    fma2x32<kPackedPromote>(r0, r1, MODE == 0 ? s1 : s0, acc + 64, acc + 96);
+                }
             }
             if (!ok) break;
 
@@ -342,43 +396,45 @@ __global__ void __launch_bounds__(kThreads, 1)
                     dst[u] = make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
                 if (half == 0) args.out_s[(size_t)grow * (args.inter / 128) + nt] = sc;
             } else {
-                // Weight, round, and stage this warp's 32 rows x 128 columns in shared memory (one row per
-                // thread), then write the rows out as coalesced 256-byte segments, two rows per instruction.
+                // Weight, round, and stage this warp's 32 rows in shared memory 64 columns at a time (one row per
+                // thread), writing each pass out as coalesced 128-byte row segments, four rows per instruction.
                 constexpr int RB = Cfg<MODE>::kStageRowBytes;
                 uint8_t* wst = staging + (size_t)(warp - kEpiWarp0) * 32 * RB;
                 if constexpr (EPI == kEpiRoundFirst) {
 #pragma unroll
                     for (int i = 0; i < 128; ++i) acc[i] = __bfloat162float(__float2bfloat16_rn(acc[i]));
                 }
-#pragma unroll
-                for (int u = 0; u < 16; ++u) {
-                    uint4 o;
-                    __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        ob[i] = __floats2bfloat162_rn(acc[8 * u + 2 * i] * w, acc[8 * u + 2 * i + 1] * w);
-                    *reinterpret_cast<uint4*>(wst + lane * RB + u * 16) = o;
-                }
-                __syncwarp();
-                // A row's half is 128 bf16 = 256 bytes = 16 lanes x 16 bytes: lanes 0-15 write row r,
-                // lanes 16-31 row r+1.  Columns stay within [nt*256, nt*256 + 256) of an H-wide row.
                 const int H = args.n_total;
-                const int sub = lane >> 4, chunk = lane & 15;
-                for (int r = 0; r < 32; r += 2) {
-                    const int f = __shfl_sync(0xffffffffu, flat, r + sub);
-                    if constexpr (EPI == kEpiDstRows) {
-                        const uint64_t dr = __shfl_sync(0xffffffffu, drow, r + sub);
-                        if (f < args.n_valid && dr != 0) {
-                            const uint4 v = *reinterpret_cast<const uint4*>(wst + (r + sub) * RB + chunk * 16);
-                            __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(dr);
-                            *reinterpret_cast<uint4*>(row + nt * kBN + 128 * half + chunk * 8) = v;
-                        }
-                    } else if (f < args.n_valid) {
-                        const uint4 v = *reinterpret_cast<const uint4*>(wst + (r + sub) * RB + chunk * 16);
-                        *reinterpret_cast<uint4*>(args.c3 + (size_t)f * H + nt * kBN + 128 * half + chunk * 8) = v;
+                const int sub = lane >> 3, chunk8 = lane & 7;
+#pragma unroll
+                for (int p = 0; p < 2; ++p) {
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        uint4 o;
+                        __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            ob[i] = __floats2bfloat162_rn(acc[64 * p + 8 * u + 2 * i] * w,
+                                                          acc[64 * p + 8 * u + 2 * i + 1] * w);
+                        *reinterpret_cast<uint4*>(wst + lane * RB + u * 16) = o;
                     }
+                    __syncwarp();
+                    // Columns [nt*256 + 128*half + 64*p, +64) of an H-wide row: 128 bytes = 8 lanes x 16 bytes.
+                    const int col = nt * kBN + 128 * half + 64 * p + chunk8 * 8;
+#pragma unroll 4
+                    for (int r = 0; r < 32; r += 4) {
+                        const int f = __shfl_sync(0xffffffffu, flat, r + sub);
+                        const uint4 v = *reinterpret_cast<const uint4*>(wst + (r + sub) * RB + chunk8 * 16);
+                        if constexpr (EPI == kEpiDstRows) {
+                            const uint64_t dr = __shfl_sync(0xffffffffu, drow, r + sub);
+                            if (f < args.n_valid && dr != 0)
+                                *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(dr) + col) = v;
+                        } else if (f < args.n_valid) {
+                            *reinterpret_cast<uint4*>(args.c3 + (size_t)f * H + col) = v;
+                        }
+                    }
+                    __syncwarp();
                 }
-                __syncwarp();
             }
         }
     }

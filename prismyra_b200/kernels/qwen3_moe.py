@@ -13,6 +13,8 @@ the framework's own modules, as in the reference.
 
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.nn.functional as F
 from torch import nn
@@ -183,6 +185,60 @@ class FusedDenseProjection(nn.Module):
         return torch.split(out, self.sizes, dim=-1)
 
 
+#: How many times the construction-time self-check calls one installed FusedExperts on the same input (the
+#: reference's FP8 determinism probe, prismyra/kernels/qwen3_moe.py:1677-1683).
+FP8_DETERMINISM_PROBES = 8
+
+
+def _withheld() -> set[str]:
+    """Checks a caller switched off with PRISMYRA_WITHOUT (a comma-separated list), as in the reference."""
+    return {w.strip() for w in os.environ.get("PRISMYRA_WITHOUT", "").split(",") if w.strip()}
+
+
+def _raise_if_out_of_resources(e: Exception, context: str) -> None:
+    """A self-check that could not run because the device ran out of memory says nothing about the kernel; it is
+    raised as AdapterError instead of silently choosing a slower path (the reference's qwen3_moe.py:29-65, whose
+    other resource case, a Triton shared-memory limit, has no counterpart here: these kernels' shared memory is
+    fixed at build time)."""
+    if isinstance(e, torch.OutOfMemoryError):
+        raise AdapterError(
+            f"{context}: ran out of GPU memory while self-checking the installed kernel ({type(e).__name__}: {e}); "
+            "retry with more free memory on this device") from e
+
+
+def _check_fp8_determinism(applied: Applied, root: nn.Module) -> None:
+    """Call one installed FusedExperts on a fixed input FP8_DETERMINISM_PROBES times and refuse to start when the
+    bits ever differ (the reference's _check_fp8_determinism, qwen3_moe.py:1683-1761, pointed at the FP8 module this
+    adapter installs).  The kernels have no atomics in any reduction, so a difference is a device fault; there is
+    nothing to retry.  Running out of memory raises AdapterError; any other failure to run the probe is recorded as a
+    skip of this check."""
+    probe = next((m for m in root.modules() if type(m).__name__ == "FusedExperts"), None)
+    if probe is None:
+        applied.notes.append("fp8_determinism: nothing matched (no FusedExperts installed)")
+        return
+    width = probe.hidden
+    g = torch.Generator(device="cpu").manual_seed(width)
+    x = (torch.randn(64, width, generator=g) * 0.1).to(device=probe.w1.device, dtype=torch.bfloat16)
+    try:
+        with torch.inference_mode():
+            first = probe(x).clone()
+            repeats = [probe(x).clone() for _ in range(FP8_DETERMINISM_PROBES - 1)]
+    except Exception as e:  # noqa: BLE001 - a probe that cannot run is a resource question, not a finding
+        _raise_if_out_of_resources(e, "fp8_determinism")
+        applied.skipped.append(f"fp8_determinism: the probe raised {type(e).__name__}: {e} -- not checked")
+        return
+    bad = [i for i, r in enumerate(repeats) if not torch.equal(first, r)]
+    if bad:
+        moved = max((first.float() - repeats[i].float()).abs().max().item() for i in bad)
+        raise AdapterError(
+            f"fp8_determinism: the installed FP8 experts answered the same input differently in {len(bad)} of "
+            f"{FP8_DETERMINISM_PROBES - 1} repeated calls (max difference {moved:.3e}); this device does not give "
+            "the same bits back twice -- move to another GPU, or set PRISMYRA_WITHOUT=fp8_determinism to serve "
+            "from it anyway")
+    applied.notes.append(f"fp8_determinism: {FP8_DETERMINISM_PROBES} calls to the installed FP8 experts agreed "
+                         "bit for bit")
+
+
 def _swap_children(root: nn.Module, class_name: str, make) -> int:
     count = 0
     for parent in list(root.modules()):
@@ -231,6 +287,8 @@ class Qwen3MoeAdapter:
         applied.swaps.append(Swap("routed_experts", n, d.num_hidden_layers))
         applied.notes.append("only the routed experts are replaced; attention, norms and dense projections keep "
                              "the framework's modules")
+        if "fp8_determinism" not in _withheld():
+            _check_fp8_determinism(applied, text)
         return applied
 
 

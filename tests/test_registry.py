@@ -191,3 +191,69 @@ def test_dense_projection_modules_check_their_shapes():
     assert fused.sizes == [512, 256] and fused.weight.shape == (768, 256) and fused.scale.shape == (6, 2)
     with pytest.raises(AdapterError):
         FusedDenseProjection([lin, Fp8Linear(_fp8_linear_module(256, 512))])  # different input widths
+
+
+class FusedExperts(nn.Module):  # matched by class name, like the adapter's installed module
+    """A stand-in for the installed routed-expert module whose repeat behaviour the test chooses."""
+
+    def __init__(self, behaviour: str):
+        super().__init__()
+        self.hidden = 256
+        self.w1 = torch.zeros(1)
+        self.behaviour = behaviour
+        self.calls = 0
+
+    def forward(self, x):
+        self.calls += 1
+        if self.behaviour == "oom":
+            raise torch.OutOfMemoryError("CUDA out of memory. Tried to allocate 2.00 GiB")
+        if self.behaviour == "error":
+            raise RuntimeError("launch failed")
+        out = x * 2
+        if self.behaviour == "flaky" and self.calls == 5:
+            out = out + 1e-2
+        return out
+
+
+def test_fp8_determinism_probe_accepts_a_kernel_that_repeats_itself():
+    from prismyra_b200.kernels import qwen3_moe as q
+
+    m = FusedExperts("stable")
+    applied = Applied(adapter="t")
+    q._check_fp8_determinism(applied, nn.Sequential(m))
+    assert m.calls == q.FP8_DETERMINISM_PROBES == 8
+    assert any("agreed bit for bit" in n for n in applied.notes) and not applied.skipped
+
+
+def test_fp8_determinism_probe_refuses_a_device_that_does_not():
+    from prismyra_b200.kernels import qwen3_moe as q
+
+    with pytest.raises(AdapterError, match="differently in 1 of 7"):
+        q._check_fp8_determinism(Applied(adapter="t"), nn.Sequential(FusedExperts("flaky")))
+
+
+def test_fp8_determinism_probe_out_of_memory_is_an_adapter_error_not_a_fallback():
+    from prismyra_b200.kernels import qwen3_moe as q
+
+    with pytest.raises(AdapterError, match="ran out of GPU memory"):
+        q._check_fp8_determinism(Applied(adapter="t"), nn.Sequential(FusedExperts("oom")))
+
+
+def test_fp8_determinism_probe_that_cannot_run_is_recorded_as_a_skip():
+    from prismyra_b200.kernels import qwen3_moe as q
+
+    applied = Applied(adapter="t")
+    q._check_fp8_determinism(applied, nn.Sequential(FusedExperts("error")))
+    assert applied.skipped == ["fp8_determinism: the probe raised RuntimeError: launch failed -- not checked"]
+    applied = Applied(adapter="t")
+    q._check_fp8_determinism(applied, nn.Sequential(nn.Identity()))
+    assert applied.notes == ["fp8_determinism: nothing matched (no FusedExperts installed)"]
+
+
+def test_the_probe_can_be_withheld_like_the_reference(monkeypatch):
+    from prismyra_b200.kernels import qwen3_moe as q
+
+    monkeypatch.setenv("PRISMYRA_WITHOUT", "dense_fusion, fp8_determinism")
+    assert q._withheld() == {"dense_fusion", "fp8_determinism"}
+    monkeypatch.delenv("PRISMYRA_WITHOUT")
+    assert q._withheld() == set()
