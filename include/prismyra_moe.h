@@ -149,6 +149,26 @@ int pm_moe_forward_fp8(const void *x, const void *router_w, const void *logits, 
                        const float *w1_s, const uint8_t *w2, const float *w2_s, int T, int H, int I, int E, int k,
                        void *out, void *workspace, size_t workspace_bytes, pm_stream_t stream);
 
+/* pm_moe_quant_fp8 and pm_moe_forward_fp8 with a choice of activation-scale rule (flags; 0 gives exactly those
+ * calls).  Every FP8 activation quantisation -- the input's, and the gate_up epilogue's requantisation of
+ * silu(gate)*up -- divides a 128-value group by one fp32 scale derived from its maximum magnitude amax, as vLLM's
+ * per_token_group_quant_fp8 does (vllm/model_executor/layers/quantization/utils/fp8_utils.py:510-640):
+ *   0                        s = max(amax, 1e-10) / 448, correctly rounded: vLLM's compiled CUDA quantiser, the op the
+ *                            reference's fused_experts call (prismyra/kernels/qwen3_moe.py:197) runs on a GPU;
+ *   PM_FLAG_ACT_SCALE_UE8M0  that s rounded up to a power of two, 2^ceil(log2(s)) (fp8_utils.py:145): vLLM's mode when
+ *                            it runs DeepGEMM with E8M0 scales (VLLM_USE_DEEP_GEMM_E8M0, on by default where DeepGEMM
+ *                            is installed);
+ *   PM_FLAG_ACT_SCALE_RCP    s = max(amax, 1e-10) * fl(1/448): vLLM's Triton quantiser (fp8_utils.py:143-144), one ulp
+ *                            away from the quotient for about half of all values.
+ * Each value's code is the correctly rounded quotient x / s, clamped to +-448, rounded to e4m3. */
+#define PM_FLAG_ACT_SCALE_UE8M0 1
+#define PM_FLAG_ACT_SCALE_RCP 2
+int pm_moe_quant_fp8_ex(const void *x, int T, int H, int k, const int32_t *slot_of, uint8_t *a_q, float *a_s,
+                        int flags, pm_stream_t stream);
+int pm_moe_forward_fp8_ex(const void *x, const void *router_w, const void *logits, const uint8_t *w1,
+                          const float *w1_s, const uint8_t *w2, const float *w2_s, int T, int H, int I, int E, int k,
+                          int flags, void *out, void *workspace, size_t workspace_bytes, pm_stream_t stream);
+
 /* The shared expert, `torch.sigmoid(self._gate(x)) * self.shared_expert(x)` (prismyra/kernels/qwen3_moe.py:198):
  * gate = bf16(sigmoid(bf16(x . w_sg))) (w_sg bf16 [H], the shared_expert_gate weight, qwen3_moe.py:172-183), and
  * the MLP down(bf16(silu(gate_proj x)) * up_proj x) on 128x128 block-FP8 weights with the reference's Fp8Linear

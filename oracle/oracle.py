@@ -121,12 +121,18 @@ def align(ids, num_experts: int, block_m: int):
     return sorted_ids[: int(npp[0])].copy(), expert_ids[:nb].copy(), int(npp[0])
 
 
-def quant_fp8_groups(x_bits):
+#: Activation-scale rules, numbered as the library's flags (include/prismyra_moe.h PM_FLAG_ACT_SCALE_*): "fp32" the
+#: correctly rounded max(amax, 1e-10)/448 (vLLM's compiled quantiser), "ue8m0" that rounded up to a power of two,
+#: "fp32_rcp" max(amax, 1e-10) * fl(1/448) (vLLM's Triton kernel, what the golden fixtures were made with).
+SCALE_RULES = {"fp32": 0, "ue8m0": 1, "fp32_rcp": 2}
+
+
+def quant_fp8_groups(x_bits, scale: str = "fp32"):
     x = _c(x_bits, np.uint16)
     R, C = x.shape
     q = np.empty((R, C), np.uint8)
     s = np.empty((R, C // 128), np.float32)
-    lib().or_quant_fp8_groups(_p(x), R, C, _p(q), _p(s))
+    lib().or_quant_fp8_groups_ex(_p(x), R, C, _p(q), _p(s), SCALE_RULES[scale])
     return q, s
 
 
@@ -161,9 +167,11 @@ def router_logits(x_bits, w_bits) -> np.ndarray:
     return out
 
 
-def moe_forward_fp8(x_bits, logits_bits, w1, w1_s, w2, w2_s, k: int, want_intermediates: bool = False):
+def moe_forward_fp8(x_bits, logits_bits, w1, w1_s, w2, w2_s, k: int, want_intermediates: bool = False,
+                    scale: str = "fp32"):
     """The whole routed FP8 layer; returns a dict with ``out`` (bf16 bits [T,H]) and, on request, the
-    routing and the intermediates the CUDA stages produce (x_q, x_s, c2q, c2s, c3)."""
+    routing and the intermediates the CUDA stages produce (x_q, x_s, c2q, c2s, c3).  ``scale``: the activation-scale
+    rule of both quantisations (:data:`SCALE_RULES`)."""
     x = _c(x_bits, np.uint16)
     lg = _c(logits_bits, np.uint16)
     w1 = _c(w1, np.uint8)
@@ -186,9 +194,10 @@ def moe_forward_fp8(x_bits, logits_bits, w1, w1_s, w2, w2_s, k: int, want_interm
             c3=np.empty((T * k, H), np.uint16),
         )
     g = r.get
-    lib().or_moe_forward_fp8(
+    lib().or_moe_forward_fp8_ex(
         _p(x), _p(lg), _p(w1), _p(w1_s), _p(w2), _p(w2_s), T, H, I, E, k, _p(out),
         _p(g("weights")), _p(g("ids")), _p(g("x_q")), _p(g("x_s")), _p(g("c2q")), _p(g("c2s")), _p(g("c3")),
+        SCALE_RULES[scale],
     )
     return r
 

@@ -125,6 +125,16 @@ static int check_dims(int T, int H, int I, int E, int k) {
 
 static int cuda_status(cudaError_t e) { return e == cudaSuccess ? PM_OK : PM_ERR_CUDA; }
 
+// The activation-scale rule (e4m3_group_scale) a flags word selects, or -1 for an invalid word.
+static int scale_rule_of(int flags) {
+    switch (flags) {
+        case 0: return kScaleDiv;
+        case PM_FLAG_ACT_SCALE_UE8M0: return kScaleUe8m0;
+        case PM_FLAG_ACT_SCALE_RCP: return kScaleRcp;
+        default: return -1;
+    }
+}
+
 static GemmArgs gemm_args_common(const float* a_s, const float* b_s, const int32_t* expert_ids,
                                  const int32_t* npp, int n_total, int K, int n_tiles, int max_slots, int inter,
                                  int32_t* err) {
@@ -233,7 +243,12 @@ int pm_moe_align(const int32_t* topk_ids, int T, int k, int E, int32_t* sorted_i
 
 int pm_moe_quant_fp8(const void* x, int T, int H, int k, const int32_t* slot_of, uint8_t* a_q, float* a_s,
                      pm_stream_t stream) {
-    if (T < 0 || H <= 0 || (slot_of != nullptr && k <= 0)) return PM_ERR_INVALID;
+    return pm_moe_quant_fp8_ex(x, T, H, k, slot_of, a_q, a_s, 0, stream);
+}
+
+int pm_moe_quant_fp8_ex(const void* x, int T, int H, int k, const int32_t* slot_of, uint8_t* a_q, float* a_s,
+                        int flags, pm_stream_t stream) {
+    if (T < 0 || H <= 0 || (slot_of != nullptr && k <= 0) || scale_rule_of(flags) < 0) return PM_ERR_INVALID;
     if (H % 128 != 0) return PM_ERR_SHAPE;
     if (T == 0) return PM_OK;
     if (!x || !a_q || !a_s) return PM_ERR_INVALID;
@@ -241,7 +256,7 @@ int pm_moe_quant_fp8(const void* x, int T, int H, int k, const int32_t* slot_of,
     DeviceInfo d;
     const int st = current_device_info(&d);
     if (st != PM_OK) return st;
-    return cuda_status(launch_quant_fp8(x, T, H, k, slot_of, a_q, a_s, (cudaStream_t)stream));
+    return cuda_status(launch_quant_fp8(x, T, H, k, slot_of, a_q, a_s, (cudaStream_t)stream, scale_rule_of(flags)));
 }
 
 // The few-tokens-per-expert GEMMs (weights as the 128-row MMA operand): used when T*k <= 32 E.
@@ -252,7 +267,7 @@ static bool use_small_gemm(long n_valid, int H, int I, int E) {
 static int small_gemm_fp8(int mode, const uint8_t* a_q, const float* a_s, const uint8_t* w, const float* w_s,
                           const int32_t* expert_ids, const int32_t* npp, const int32_t* sorted_ids,
                           const float* topk_w, int max_slots, int n_valid, int H, int I, int E, uint8_t* out_q,
-                          float* out_s, void* c3, int32_t* err, int sms, cudaStream_t s) {
+                          float* out_s, void* c3, int32_t* err, int sms, cudaStream_t s, int scale_rule = 0) {
     const int K = mode == 0 ? H : I, n_total = mode == 0 ? 2 * I : H;
     CUtensorMap tt, tw;
     if (!encode_tmap_2d_u8(&tt, a_q, (uint64_t)K, (uint64_t)max_slots, (uint64_t)K, 128, 32) ||
@@ -275,13 +290,25 @@ static int small_gemm_fp8(int mode, const uint8_t* a_q, const float* a_s, const 
     g.out_s = out_s;
     g.topk_w = topk_w;
     g.c3 = static_cast<__nv_bfloat16*>(c3);
+    g.scale_rule = scale_rule;
     g.err = err;
     return cuda_status(launch_gemm_fp8_small(mode, tt, tw, g, sms, s));
 }
 
+static int gemm1_fp8_run(const uint8_t* a_q, const float* a_s, const uint8_t* w1, const float* w1_s,
+                         const int32_t* expert_ids, const int32_t* num_post_pad, int max_slots, int H, int I, int E,
+                         uint8_t* out_q, float* out_s, int32_t* err, pm_stream_t stream, int scale_rule);
+
 int pm_moe_gemm1_fp8(const uint8_t* a_q, const float* a_s, const uint8_t* w1, const float* w1_s,
                      const int32_t* expert_ids, const int32_t* num_post_pad, int max_slots, int H, int I, int E,
                      uint8_t* out_q, float* out_s, int32_t* err, pm_stream_t stream) {
+    return gemm1_fp8_run(a_q, a_s, w1, w1_s, expert_ids, num_post_pad, max_slots, H, I, E, out_q, out_s, err, stream,
+                         0);
+}
+
+static int gemm1_fp8_run(const uint8_t* a_q, const float* a_s, const uint8_t* w1, const float* w1_s,
+                         const int32_t* expert_ids, const int32_t* num_post_pad, int max_slots, int H, int I, int E,
+                         uint8_t* out_q, float* out_s, int32_t* err, pm_stream_t stream, int scale_rule) {
     int st = check_dims(0, H, I, E, 1);
     if (st != PM_OK) return st;
     if (max_slots < 0 || max_slots % kBlockM != 0) return PM_ERR_SHAPE;
@@ -298,6 +325,7 @@ int pm_moe_gemm1_fp8(const uint8_t* a_q, const float* a_s, const uint8_t* w1, co
     GemmArgs g = gemm_args_common(a_s, w1_s, expert_ids, num_post_pad, 2 * I, H, I / 128, max_slots, I, err);
     g.out_q = out_q;
     g.out_s = out_s;
+    g.scale_rule = scale_rule;
     return cuda_status(launch_gemm_fp8(0, ta, tb, g, d.sms, (cudaStream_t)stream));
 }
 
@@ -361,7 +389,7 @@ int pm_moe_combine(const void* c3, const int32_t* row_of, int T, int k, int H, v
 static int forward_fp8_impl(const void* x, const void* router_w, const void* logits, const uint8_t* w1,
                             const float* w1_s, const uint8_t* w2, const float* w2_s, int T, int H, int I, int E,
                             int k, const void* add, cudaEvent_t add_ready, void* out, void* workspace,
-                            size_t workspace_bytes, pm_stream_t stream, bool clear_status) {
+                            size_t workspace_bytes, pm_stream_t stream, bool clear_status, int scale_rule = 0) {
     int st = check_dims(T, H, I, E, k);
     if (st != PM_OK) return st;
     if (T == 0) return PM_OK;
@@ -401,13 +429,14 @@ static int forward_fp8_impl(const void* x, const void* router_w, const void* log
     e = launch_align(topk_ids, T * k, E, reinterpret_cast<int32_t*>(R(PM_WS_COUNTS)), sorted, expert_ids, npp,
                      reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_OFF)), slot_of, s);
     if (e != cudaSuccess) return PM_ERR_CUDA;
-    e = launch_quant_fp8(x, T, H, k, slot_of, a1, a1s, s);
+    e = launch_quant_fp8(x, T, H, k, slot_of, a1, a1s, s, scale_rule);
     if (e != cudaSuccess) return PM_ERR_CUDA;
     if (use_small_gemm((long)T * k, H, I, E))
         st = small_gemm_fp8(0, a1, a1s, w1, w1_s, expert_ids, npp, sorted, nullptr, L.max_slots, T * k, H, I, E, a2,
-                            a2s, nullptr, status, d.sms, s);
+                            a2s, nullptr, status, d.sms, s, scale_rule);
     else
-        st = pm_moe_gemm1_fp8(a1, a1s, w1, w1_s, expert_ids, npp, L.max_slots, H, I, E, a2, a2s, status, stream);
+        st = gemm1_fp8_run(a1, a1s, w1, w1_s, expert_ids, npp, L.max_slots, H, I, E, a2, a2s, status, stream,
+                           scale_rule);
     if (st != PM_OK) return st;
     st = pm_moe_gemm2_fp8(a2, a2s, w2, w2_s, expert_ids, npp, sorted, topk_w, L.max_slots, T, k, H, I, E, c3,
                           status, stream);
@@ -421,6 +450,15 @@ int pm_moe_forward_fp8(const void* x, const void* router_w, const void* logits, 
                        void* out, void* workspace, size_t workspace_bytes, pm_stream_t stream) {
     return forward_fp8_impl(x, router_w, logits, w1, w1_s, w2, w2_s, T, H, I, E, k, nullptr, nullptr, out,
                             workspace, workspace_bytes, stream, true);
+}
+
+int pm_moe_forward_fp8_ex(const void* x, const void* router_w, const void* logits, const uint8_t* w1,
+                          const float* w1_s, const uint8_t* w2, const float* w2_s, int T, int H, int I, int E, int k,
+                          int flags, void* out, void* workspace, size_t workspace_bytes, pm_stream_t stream) {
+    const int rule = scale_rule_of(flags);
+    if (rule < 0) return PM_ERR_INVALID;
+    return forward_fp8_impl(x, router_w, logits, w1, w1_s, w2, w2_s, T, H, I, E, k, nullptr, nullptr, out,
+                            workspace, workspace_bytes, stream, true, rule);
 }
 
 // ------------------------------------------------------------------------------------------- shared expert

@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_quant_kernel(
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         if (!valid) continue;
-        const float sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
+        const float sc = e4m3_group_scale(amax, kScaleDiv);
         uint32_t packed[2];
 #pragma unroll
         for (int i = 0; i < 2; ++i) {

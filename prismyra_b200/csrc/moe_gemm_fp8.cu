@@ -377,17 +377,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(xb);
                 if (!mbar_wait(xb, (uint32_t)(local >> 1) & 1u, abort)) break;
                 amax = fmaxf(tail->amax_x[local & 1][0][row], tail->amax_x[local & 1][1][row]);
-                const float sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
-                // y * (1/s) instead of y / s: the e4m3 code keeps 3 significand bits, so the quotient's last-bit
-                // difference moves a code only when it lies on an e4m3 rounding midpoint.
-                // The saturating conversion clamps to +-448 exactly as clamp-then-round does.
+                const float sc = e4m3_group_scale(amax, args.scale_rule);
+                // Codes are the correctly rounded quotients y / s (quot2), as vLLM's quantiser computes them; the
+                // saturating conversion clamps to +-448 exactly as clamp-then-round does.
                 const float inv = __frcp_rn(sc);
-                const float2 inv2 = make_float2(inv, inv);
+                const float2 inv2 = make_float2(inv, inv), nsc2 = make_float2(-sc, -sc);
                 uint32_t packed[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float2 q01 = __fmul2_rn(make_float2(acc[4 * i + 0], acc[4 * i + 1]), inv2);
-                    const float2 q23 = __fmul2_rn(make_float2(acc[4 * i + 2], acc[4 * i + 3]), inv2);
+                    const float2 q01 = quot2(make_float2(acc[4 * i + 0], acc[4 * i + 1]), inv2, nsc2);
+                    const float2 q23 = quot2(make_float2(acc[4 * i + 2], acc[4 * i + 3]), inv2, nsc2);
                     packed[i] = (uint32_t)e4m3x2(q01.x, q01.y) | ((uint32_t)e4m3x2(q23.x, q23.y) << 16);
                 }
                 uint4* dst = reinterpret_cast<uint4*>(args.out_q + (size_t)grow * args.inter + nt * 128 + 64 * half);

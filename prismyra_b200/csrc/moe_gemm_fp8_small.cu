@@ -186,9 +186,10 @@ __device__ __forceinline__ bool run_unit(const SmallGemmArgs& a, SmallTail* tail
 #pragma unroll
         for (int i = 0; i < C; ++i) {
             const float amax = fmaxf(fmaxf(ax[0][i], ax[1][i]), fmaxf(ax[2][i], ax[3][i]));
-            const float sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
-            // y * (1/s): see the gate_up epilogue of moe_gemm_fp8.cu (identical codes but on e4m3 midpoints)
-            const float qv = accg[i] * __frcp_rn(sc);
+            const float sc = e4m3_group_scale(amax, a.scale_rule);
+            // the correctly rounded quotient y / s (quot2 in ptx.cuh), as in the gate_up epilogue of moe_gemm_fp8.cu
+            const float rs = __frcp_rn(sc);
+            const float qv = quot2(make_float2(accg[i], 0.0f), make_float2(rs, rs), make_float2(-sc, -sc)).x;
             const size_t slot = (size_t)un.mb * 128 + row0 + i;
             a.out_q[slot * I + un.nt * 128 + r] = (uint8_t)__nv_cvt_float_to_fp8(qv, __NV_SATFINITE, __NV_E4M3);
             if (q == 0 && lane == i) a.out_s[slot * (I / 128) + un.nt] = sc;

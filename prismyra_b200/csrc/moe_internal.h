@@ -38,6 +38,8 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 
 
 constexpr int kBlockM = 128;  // rows of one GEMM tile == the alignment block of the expert permutation
+// Activation-scale rules of the FP8 quantisations (e4m3_group_scale in ptx.cuh).
+constexpr int kScaleDiv = 0, kScaleUe8m0 = 1, kScaleRcp = 2;
 constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 16;
 // The alignment kernels split the n flat (token, slot) indices into at most kAlignMaxChunks chunks of
@@ -74,8 +76,9 @@ cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int3
                          int32_t* num_post_pad, int32_t* expert_off, int32_t* slot_of, cudaStream_t s);
 // Quantise every token row of x to e4m3 with one fp32 scale per 128 columns.  With slot_of, each quantised row
 // is written to the k slots of its token (a_q [slots, H], a_s [slots, H/128]) instead of to row t.
+// scale_rule: how each group's scale is formed (e4m3_group_scale in ptx.cuh; 0 = the correctly rounded quotient).
 cudaError_t launch_quant_fp8(const void* x, int T, int H, int k, const int32_t* slot_of, uint8_t* x_q, float* x_s,
-                             cudaStream_t s);
+                             cudaStream_t s, int scale_rule = 0);
 // out[t] = bf16(sum_j c3[row(t*k + j)]) in fp32, j ascending; row = identity or row_of.
 cudaError_t launch_combine(const void* c3, const int32_t* row_of, int T, int k, int H, void* out, cudaStream_t s,
                            const void* add = nullptr);
@@ -111,6 +114,7 @@ struct GemmArgs {
                               // instead of c3 -- e.g. another GPU's memory over NVLink
     int n_valid;
     int round_first;          // down epilogue: bf16(bf16(acc) * w) instead of bf16(acc * w) (a bf16 product)
+    int scale_rule;           // gate_up epilogue: how requantisation scales are formed (e4m3_group_scale)
     int* err;                 // set to 1 when a wait timed out
 };
 
@@ -136,6 +140,7 @@ struct SmallGemmArgs {
     float* out_s;                // gate_up: [rows, I/128]
     const float* topk_w;         // down: [n_valid]
     __nv_bfloat16* c3;           // down: [n_valid, H]
+    int scale_rule;              // gate_up: how requantisation scales are formed (e4m3_group_scale)
     int* err;
 };
 // The small-token path is used when T*k <= kSmallTokensPerExpert * E and the K-block scale table fits.

@@ -16,7 +16,8 @@ namespace {
 // stored.  Without slot_of the single copy goes to row t.
 __global__ void __launch_bounds__(256) quant_fp8_kernel(const __nv_bfloat16* __restrict__ x, int T, int H, int k,
                                                         const int32_t* __restrict__ slot_of,
-                                                        uint8_t* __restrict__ x_q, float* __restrict__ x_s) {
+                                                        uint8_t* __restrict__ x_q, float* __restrict__ x_s,
+                                                        int scale_rule) {
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x & 31, sub = lane & 15;
@@ -44,7 +45,7 @@ __global__ void __launch_bounds__(256) quant_fp8_kernel(const __nv_bfloat16* __r
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         if (!valid) continue;
-        const float sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
+        const float sc = e4m3_group_scale(amax, scale_rule);
         uint32_t packed[2];
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
@@ -103,7 +104,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
 }  // namespace
 
 cudaError_t launch_quant_fp8(const void* x, int T, int H, int k, const int32_t* slot_of, uint8_t* x_q, float* x_s,
-                             cudaStream_t s) {
+                             cudaStream_t s, int scale_rule) {
     if (T == 0) return cudaSuccess;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
@@ -111,7 +112,7 @@ cudaError_t launch_quant_fp8(const void* x, int T, int H, int k, const int32_t* 
     const long pairs = ((long)T * (H / 128) + 1) / 2;  // one warp per two (token, group) items
     const int blocks = (int)min((pairs + 7) / 8, (long)sms * 16);
     PM_TRY(launch_pdl(quant_fp8_kernel, dim3(blocks), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(x), T, H, k,
-                      slot_of, x_q, x_s));
+                      slot_of, x_q, x_s, scale_rule));
     return cudaGetLastError();
 }
 

@@ -217,6 +217,36 @@ __device__ __forceinline__ float2 silu2(float2 g) {
     return __ffma2_rn(h, make_float2(tanh_approx(h.x), tanh_approx(h.y)), h);
 }
 
+// How an activation group's e4m3 scale is formed from its maximum magnitude amax (vLLM's per_token_group_quant_fp8,
+// vllm/model_executor/layers/quantization/utils/fp8_utils.py:510-640):
+//   kScaleDiv   the correctly rounded quotient max(amax, 1e-10) / 448 -- what vLLM's compiled CUDA quantiser, the
+//               op the reference's fused_experts runs on a GPU, computes (matched bit for bit on B200);
+//   kScaleRcp   max(amax, 1e-10) * fl(1/448) -- vLLM's Triton kernel (fp8_utils.py:143-144), 1 ulp apart from the
+//               quotient for about half of all values;
+//   kScaleUe8m0 the quotient rounded up to a power of two, 2^ceil(log2(s)) (fp8_utils.py:145), vLLM's mode when
+//               DeepGEMM runs with E8M0 scales.  The power of two is taken from the float's own bits: s is a positive
+//               normal number (at least 1e-10/448), so ceil(log2(s)) is its exponent, plus one unless its
+//               significand is exactly 1.
+__device__ __forceinline__ float e4m3_group_scale(float amax, int rule) {
+    const float a = fmaxf(amax, 1e-10f);
+    if (rule == kScaleRcp) return a * (1.0f / 448.0f);
+    const float s = __fdiv_rn(a, 448.0f);
+    if (rule != kScaleUe8m0) return s;
+    const uint32_t u = __float_as_uint(s);
+    return __uint_as_float(((u >> 23) + ((u & 0x7FFFFFu) != 0u)) << 23);
+}
+
+// The correctly rounded quotients y / s of a pair by one divisor s, given r = RN(1/s) and ns = -s: the reciprocal
+// product q0 = RN(y * r) followed by one correction step, q = RN(q0 + RN(y - q0 * s) * r), the residual being exact
+// in an FMA (P. Markstein, "Computation of elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
+// Dev. 34(1), 1990).  Used where every quotient of a group shares its divisor and must equal the IEEE quotient:
+// the requantisation reproduces vLLM's compiled quantiser code for code, ties to even on e4m3 midpoints included.
+__device__ __forceinline__ float2 quot2(float2 y, float2 r, float2 ns) {
+    const float2 q0 = __fmul2_rn(y, r);
+    const float2 e = __ffma2_rn(q0, ns, y);
+    return __ffma2_rn(e, r, q0);
+}
+
 // Two values rounded to bf16 with one packed conversion (cvt.rn.bf16x2.f32) and widened back.
 __device__ __forceinline__ float2 bf16x2_round(float a, float b) {
     return __bfloat1622float2(__floats2bfloat162_rn(a, b));

@@ -87,10 +87,19 @@ def _fp8_shared_tensors(block: nn.Module, hidden: int):
 
 
 class FusedExperts(nn.Module):
-    """Routed experts through the B200 kernels; router and shared expert kept as in the framework block."""
+    """Routed experts through the B200 kernels; router and shared expert kept as in the framework block.
 
-    def __init__(self, block: nn.Module, top_k: int):
+    ``act_scale`` (default: the PRISMYRA_B200_ACT_SCALE environment variable, else "fp32") picks how activations are
+    quantised: "fp32" scales max(amax, 1e-10)/448, the reference's arithmetic (vLLM's per_token_group_quant_fp8); or
+    "ue8m0", those scales rounded up to powers of two, which is what the reference's vLLM call computes on a host
+    where vLLM runs DeepGEMM with E8M0 scales (VLLM_USE_DEEP_GEMM_E8M0, on by default wherever DeepGEMM is
+    installed).  In the "ue8m0" mode a block-FP8 shared expert stays the framework's module."""
+
+    def __init__(self, block: nn.Module, top_k: int, act_scale: str | None = None):
         super().__init__()
+        self.act_scale = act_scale or os.environ.get("PRISMYRA_B200_ACT_SCALE", "fp32")
+        if self.act_scale not in ops.ACT_SCALES:
+            raise AdapterError(f"act_scale must be one of {sorted(ops.ACT_SCALES)}, got {self.act_scale!r}")
         tensors = _fp8_expert_tensors(block.experts)
         if tensors is None:
             raise AdapterError("FusedExperts needs 128x128 block-FP8 expert weights (gate_up_proj[_scale_inv], "
@@ -110,7 +119,7 @@ class FusedExperts(nn.Module):
                 or H % LIMITS["hidden_multiple"] or self.inter % LIMITS["intermediate_multiple"]):
             raise AdapterError(f"shape outside the kernel's range: E={E} k={self.top_k} H={H} I={self.inter}")
         #: (w_sg, w13, w13_s, w2, w2_s) when the shared expert runs in the library, else None
-        self.shared_fp8 = _fp8_shared_tensors(block, H)
+        self.shared_fp8 = _fp8_shared_tensors(block, H) if self.act_scale == "fp32" else None
 
     def _route(self, x: torch.Tensor) -> torch.Tensor:
         """Router logits (bf16 [T, E]), row-count invariant: each logit is reduced over H in a fixed order."""
@@ -121,7 +130,7 @@ class FusedExperts(nn.Module):
         """The routed-expert output for x [T, H] (no shared expert)."""
         return ops.forward_fp8(x.contiguous(), self.w1, self.w1_scale, self.w2, self.w2_scale, self.top_k,
                                router_w=None if logits is not None else self.gate.weight.contiguous(),
-                               logits=logits)
+                               logits=logits, act_scale=self.act_scale)
 
     def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
         shape = hidden_states.shape

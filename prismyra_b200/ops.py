@@ -91,10 +91,22 @@ def region(ws: torch.Tensor, T, H, I, E, k, fmt, name: str, dtype, shape) -> tor
 
 
 # ------------------------------------------------------------------------------------------- the layer
+#: Activation-scale rules of the FP8 quantisations (include/prismyra_moe.h, PM_FLAG_ACT_SCALE_*): "fp32" the correctly
+#: rounded max(amax, 1e-10)/448 (vLLM's compiled quantiser, what the reference runs on a GPU); "ue8m0" that scale
+#: rounded up to a power of two (vLLM with DeepGEMM E8M0 scales); "fp32_rcp" max(amax, 1e-10) * fl(1/448) (vLLM's
+#: Triton quantiser).
+ACT_SCALES = {"fp32": 0, "ue8m0": _lib.FLAG_ACT_SCALE_UE8M0, "fp32_rcp": _lib.FLAG_ACT_SCALE_RCP}
+
+
 def forward_fp8(x: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch.Tensor, w2_s: torch.Tensor,
                 top_k: int, router_w: torch.Tensor | None = None, logits: torch.Tensor | None = None,
-                out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """Routed FP8 experts for x [T, H] bf16; give ``router_w`` [E, H] bf16 or ``logits`` [T, E] bf16."""
+                out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                act_scale: str = "fp32") -> torch.Tensor:
+    """Routed FP8 experts for x [T, H] bf16; give ``router_w`` [E, H] bf16 or ``logits`` [T, E] bf16.
+    ``act_scale`` picks the activation-scale rule (:data:`ACT_SCALES`): "fp32" (default) the correctly rounded
+    max(amax, 1e-10)/448, as the reference's fused_experts computes on a GPU; "ue8m0" those scales rounded up to
+    powers of two, as vLLM does when it runs DeepGEMM with E8M0 scales; "fp32_rcp" vLLM's Triton rule."""
+    _need(act_scale in ACT_SCALES, f"act_scale must be one of {sorted(ACT_SCALES)}")
     _need(x.dim() == 2, "x must be [T, H]")
     T, H = x.shape
     E, I2, H1 = w1.shape
@@ -119,8 +131,8 @@ def forward_fp8(x: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch
     else:
         nbytes = workspace.numel()
     _lib.call(
-        "pm_moe_forward_fp8", _p(x), _p(router_w), _p(logits), _p(_u8(w1)), _p(w1_s), _p(_u8(w2)), _p(w2_s),
-        T, H, I, E, top_k, _p(out), _p(workspace), nbytes, _stream(x.device),
+        "pm_moe_forward_fp8_ex", _p(x), _p(router_w), _p(logits), _p(_u8(w1)), _p(w1_s), _p(_u8(w2)), _p(w2_s),
+        T, H, I, E, top_k, ACT_SCALES[act_scale], _p(out), _p(workspace), nbytes, _stream(x.device),
     )
     return out
 
@@ -416,9 +428,12 @@ def scatter_rows(src: torch.Tensor, dst_index: torch.Tensor, dst: torch.Tensor) 
     return dst
 
 
-def quant_fp8(x: torch.Tensor, slot_of: torch.Tensor | None = None, k: int = 1, max_slots: int = 0, out=None):
+def quant_fp8(x: torch.Tensor, slot_of: torch.Tensor | None = None, k: int = 1, max_slots: int = 0, out=None,
+              act_scale: str = "fp32"):
     """Per-token, per-128-column e4m3 quantisation of x [T, H] bf16.  Without ``slot_of``: (x_q [T, H] u8,
-    x_s [T, H/128] f32).  With it: the rows land in the k slots of each token (a_q [max_slots, H], a_s)."""
+    x_s [T, H/128] f32).  With it: the rows land in the k slots of each token (a_q [max_slots, H], a_s).
+    ``act_scale`` as in :func:`forward_fp8`."""
+    _need(act_scale in ACT_SCALES, f"act_scale must be one of {sorted(ACT_SCALES)}")
     T, H = x.shape
     _cuda(x, "x", torch.bfloat16)
     rows = T if slot_of is None else max_slots
@@ -426,7 +441,8 @@ def quant_fp8(x: torch.Tensor, slot_of: torch.Tensor | None = None, k: int = 1, 
         out = (torch.zeros(rows, H, dtype=torch.uint8, device=x.device),
                torch.zeros(rows, H // 128, dtype=torch.float32, device=x.device))
     x_q, x_s = out
-    _lib.call("pm_moe_quant_fp8", _p(x), T, H, k, _p(slot_of), _p(x_q), _p(x_s), _stream(x.device))
+    _lib.call("pm_moe_quant_fp8_ex", _p(x), T, H, k, _p(slot_of), _p(x_q), _p(x_s), ACT_SCALES[act_scale],
+              _stream(x.device))
     return x_q, x_s
 
 

@@ -14,6 +14,10 @@ the code that actually defines it, run on the CPU:
   ``SiluAndMul.forward_native`` and the top-k sum is ``torch.sum`` over the top-k axis (the fallback
   ``moe_sum`` takes for top_k > 4).  The compiled ``moe_align_block_size`` cannot run here; its documented
   semantics are restated below (``_align``) and pinned separately by ``align_kat.npz``.
+* ``fp8_layer_ue8m0.npz`` -- the same layer with both activation quantisations in vLLM's power-of-two (UE8M0)
+  scale mode, ``use_ue8m0=True`` (``fp8_utils.py:145``), which vLLM takes when it runs DeepGEMM with E8M0 scales
+  (``VLLM_USE_DEEP_GEMM_E8M0``, on by default where DeepGEMM is installed, as on the B200 hosts of this build);
+  ``act_quant.npz`` holds the edge rows in both modes.
 * ``align_kat.npz`` -- the worked example of the ``moe_align_block_size`` docstring
   (``vllm/model_executor/layers/fused_moe/moe_align_block_size.py:60-69``).  The docstring numbers its experts
   1..4, so the fixture uses ``num_experts=5`` with expert 0 empty.
@@ -109,14 +113,14 @@ def _align(flat_ids: torch.Tensor, num_experts: int, bm: int):
     )
 
 
-def _triton_group_quant(x: torch.Tensor):
+def _triton_group_quant(x: torch.Tensor, ue8m0: bool = False):
     from vllm.model_executor.layers.quantization.utils import fp8_utils
 
     rows, cols = x.shape
     q = torch.empty(rows, cols, dtype=FP8)
     s = torch.empty(rows, cols // 128, dtype=torch.float32)
     fp8_utils._per_token_group_quant_fp8[(rows * cols // 128,)](
-        x, q, s, 128, cols, cols, 1e-10, -448.0, 448.0, False, BLOCK=128
+        x, q, s, 128, cols, cols, 1e-10, -448.0, 448.0, ue8m0, BLOCK=128
     )
     return q, s
 
@@ -142,7 +146,10 @@ def _triton_gemm(a, a_s, w, w_s, c, weights, sorted_ids, expert_ids, npp, top_k,
     )
 
 
-def make_fp8_layer(seed: int = 7, T: int = 24, H: int = 256, I: int = 128, E: int = 8, k: int = 4):
+def make_fp8_layer(seed: int = 7, T: int = 24, H: int = 256, I: int = 128, E: int = 8, k: int = 4,
+                   ue8m0: bool = False):
+    """With ue8m0 both activation quantisations take power-of-two scales (vLLM's DeepGEMM-E8M0 mode, the default
+    where DeepGEMM is installed) and the fixture is fp8_layer_ue8m0.npz."""
     from vllm.model_executor.layers.activation import SiluAndMul
 
     g = torch.Generator().manual_seed(seed)
@@ -162,17 +169,17 @@ def make_fp8_layer(seed: int = 7, T: int = 24, H: int = 256, I: int = 128, E: in
 
     bm = 16
     sorted_ids, expert_ids, npp = _align(top_i.flatten(), E, bm)
-    xq, xs = _triton_group_quant(x)
+    xq, xs = _triton_group_quant(x, ue8m0)
     c1 = torch.zeros(T, k, 2 * I, dtype=torch.bfloat16)
     _triton_gemm(xq, xs, w1, w1_s, c1, top_w.flatten().contiguous(), sorted_ids, expert_ids, npp, k, False, bm)
     c2 = SiluAndMul.forward_native(c1.view(-1, 2 * I))
-    c2q, c2s = _triton_group_quant(c2.contiguous())
+    c2q, c2s = _triton_group_quant(c2.contiguous(), ue8m0)
     c3 = torch.zeros(T * k, H, dtype=torch.bfloat16)
     _triton_gemm(c2q, c2s, w2, w2_s, c3, top_w.flatten().contiguous(), sorted_ids, expert_ids, npp, 1, True, bm)
     out = c3.view(T, k, H).sum(dim=1)
 
     np.savez_compressed(
-        OUT / "fp8_layer.npz",
+        OUT / ("fp8_layer_ue8m0.npz" if ue8m0 else "fp8_layer.npz"),
         x=_bits(x), logits=_bits(logits), w1=_bits(w1), w1_s=_bits(w1_s), w2=_bits(w2), w2_s=_bits(w2_s),
         top_w=_bits(top_w.float()), top_i=_bits(top_i), sorted_ids=_bits(sorted_ids), expert_ids=_bits(expert_ids),
         x_q=_bits(xq), x_s=_bits(xs), c1=_bits(c1), c2=_bits(c2), c2q=_bits(c2q), c2s=_bits(c2s), c3=_bits(c3),
@@ -193,7 +200,9 @@ def make_quant_edges():
     rows.append(ties)
     x = torch.stack(rows).to(torch.bfloat16)
     q, s = _triton_group_quant(x)
-    np.savez_compressed(OUT / "act_quant.npz", x=_bits(x), q=_bits(q), s=_bits(s))
+    qe, se = _triton_group_quant(x, ue8m0=True)
+    np.savez_compressed(OUT / "act_quant.npz", x=_bits(x), q=_bits(q), s=_bits(s), q_ue8m0=_bits(qe),
+                        s_ue8m0=_bits(se))
 
 
 def make_align_kat():
@@ -379,10 +388,15 @@ if __name__ == "__main__":
     if sys.argv[1:] == ["nvfp4_layer"]:
         make_nvfp4_layer()
         sys.exit(0)
+    if sys.argv[1:] == ["ue8m0"]:
+        make_quant_edges()
+        make_fp8_layer(ue8m0=True)
+        sys.exit(0)
     make_align_kat()
     make_router()
     make_quant_edges()
     make_fp8_layer()
+    make_fp8_layer(ue8m0=True)
     make_nvfp4()
     make_nvfp4_search()
     make_nvfp4_layer()

@@ -196,7 +196,7 @@ def test_quant_matches_oracle(layer):
 
 def test_quant_edge_rows_match_vllm_golden(golden):
     g = golden("act_quant")
-    x_q, x_s = ops.quant_fp8(from_bits_bf16(g["x"]).to(DEV))
+    x_q, x_s = ops.quant_fp8(from_bits_bf16(g["x"]).to(DEV), act_scale="fp32_rcp")  # vLLM's Triton rule
     assert np.array_equal(bits(x_q), g["q"])
     assert np.array_equal(bits(x_s), g["s"])
 
@@ -396,7 +396,7 @@ def test_golden_fp8_layer_through_gpu(golden):
     w2 = torch.from_numpy(g["w2"]).view(torch.float8_e4m3fn).to(DEV)
     w1_s = torch.from_numpy(g["w1_s"]).to(DEV)
     w2_s = torch.from_numpy(g["w2_s"]).to(DEV)
-    out = ops.forward_fp8(x, w1, w1_s, w2, w2_s, k, logits=logits)
+    out = ops.forward_fp8(x, w1, w1_s, w2, w2_s, k, logits=logits, act_scale="fp32_rcp")  # the fixture's rule
     l2, mx = rel_err(bits(out), g["out"])
     assert l2 < 1e-2 and mx < 1e-2, (l2, mx)
     w, ids = ops.topk(logits, k)

@@ -129,6 +129,33 @@ def test_fp8_large_tile_thresholds_match_oracle(layer, T):
     assert l2 < 1e-2 and mx < 1e-2, (l2, mx)
 
 
+def test_fp8_t5120_ue8m0_mode_matches_oracle(layer):
+    """The power-of-two activation-scale mode (vLLM's DeepGEMM-E8M0 arithmetic) at BASELINE configs[1]: routing and
+    permutation as in the fp32 mode, output against the oracle in the same mode on a spread 1,024-token subset."""
+    cpu, gpu = layer
+    x = gpu["x"]
+    out = ops.forward_fp8(x, gpu["w1"], gpu["w1_s"], gpu["w2"], gpu["w2_s"], K, router_w=gpu["router_w"],
+                          act_scale="ue8m0").clone()
+    logits, _ = _check_routing_and_permutation(gpu, x, 5120)
+    sub = np.linspace(0, 5119, 1024).astype(np.int64)
+    ref = O.moe_forward_fp8(cpu["x"][sub], bits(logits)[sub], cpu["w1"], cpu["w1_s"], cpu["w2"], cpu["w2_s"], K,
+                            scale="ue8m0")["out"]
+    l2, mx = rel_err(bits(out)[sub], ref)
+    assert l2 < 1e-2 and mx < 1e-2, (l2, mx)
+
+
+def test_golden_fp8_layer_ue8m0_through_gpu(golden):
+    """vLLM's Triton chain in its power-of-two scale mode (tests/golden/fp8_layer_ue8m0.npz) through the CUDA path."""
+    g = golden("fp8_layer_ue8m0")
+    k = int(g["k"])
+    bf = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16).to(DEV)
+    f8 = lambda a: torch.from_numpy(a).view(torch.float8_e4m3fn).to(DEV)
+    out = ops.forward_fp8(bf(g["x"]), f8(g["w1"]), torch.from_numpy(g["w1_s"]).to(DEV), f8(g["w2"]),
+                          torch.from_numpy(g["w2_s"]).to(DEV), k, logits=bf(g["logits"]), act_scale="ue8m0")
+    l2, mx = rel_err(bits(out), g["out"])
+    assert l2 < 1e-2 and mx < 1e-2, (l2, mx)
+
+
 def test_nvfp4_t5120_matches_oracle(layer):
     """NVFP4 weights prepared from the seed-0 FP8 layer on the GPU (bit-exact with the
     reference's prepare_layer, tested elsewhere), synthetic calibration; a spread 1,024-token subset."""

@@ -62,12 +62,15 @@ def _block(gpu, x):
 
 @pytest.mark.parametrize("T", [1, 37, 300])
 def test_shared_expert_matches_oracle(block, T):
+    """Relative L2 <= 1e-2; the maximum error may add one bf16 ulp (2^-7 relative) on top of 1e-2: every row is
+    scaled by its bf16 gate, which is allowed to differ from the oracle's exactly rounded sigmoid by one ulp (pinned
+    on its own by test_shared_gate_within_one_ulp)."""
     L, gpu = block
     out = _shared(gpu, gpu["x"][:T].contiguous())
     ref = O.shared_expert_fp8(bits(L["x"][:T]), bits(L["w_sg"]), bits(L["sw13"]), bits(L["sw13_s"]),
                               bits(L["sw2"]), bits(L["sw2_s"]))
     l2, mx = rel_err(bits(out), ref)
-    assert l2 < 1e-2 and mx < 1e-2, (l2, mx)
+    assert l2 < 1e-2 and mx < 1e-2 + 2.0 ** -7, (l2, mx)
 
 
 def test_shared_gate_within_one_ulp(block):
@@ -111,7 +114,7 @@ def test_block_matches_oracle(block):
     shared = O.shared_expert_fp8(bits(L["x"][:T]), bits(L["w_sg"]), bits(L["sw13"]), bits(L["sw13_s"]),
                                  bits(L["sw2"]), bits(L["sw2_s"]))
     l2, mx = rel_err(bits(out), O.add_bf16(routed, shared))
-    assert l2 < 1e-2 and mx < 1e-2, (l2, mx)
+    assert l2 < 1e-2 and mx < 1e-2 + 2.0 ** -7, (l2, mx)  # the shared part's gate: one bf16 ulp, as above
 
 
 def test_block_row_count_invariant_and_deterministic(block):

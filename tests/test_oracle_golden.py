@@ -102,13 +102,27 @@ def test_router_tie_rule_prefers_lower_expert_index():
 
 def test_act_quant_matches_vllm_triton(golden):
     g = golden("act_quant")
-    q, s = O.quant_fp8_groups(g["x"])
+    q, s = O.quant_fp8_groups(g["x"], scale="fp32_rcp")  # the fixture ran vLLM's Triton kernel
     assert np.array_equal(s, g["s"])
     assert np.array_equal(q, g["q"])
+    # the library's default rule, the correctly rounded quotient, is at most one ulp away from it
+    q2, s2 = O.quant_fp8_groups(g["x"])
+    assert np.all(np.abs(s2.view(np.int32) - s.view(np.int32)) <= 1) and np.mean(q2 == q) > 0.99
 
 
-def test_fp8_layer_intermediates_match_vllm_triton(golden):
-    g = golden("fp8_layer")
+def test_act_quant_ue8m0_matches_vllm_triton(golden):
+    """vLLM's power-of-two scale mode (use_ue8m0, fp8_utils.py:145) on the same edge rows: bit-exact, every scale a
+    power of two no smaller than the fp32 scale."""
+    g = golden("act_quant")
+    q, s = O.quant_fp8_groups(g["x"], scale="ue8m0")
+    assert np.array_equal(s, g["s_ue8m0"]) and np.array_equal(q, g["q_ue8m0"])
+    m, _ = np.frexp(s)
+    assert np.all(m == 0.5) and np.all(s >= g["s"])
+
+
+@pytest.mark.parametrize("fixture,scale", [("fp8_layer", "fp32_rcp"), ("fp8_layer_ue8m0", "ue8m0")])
+def test_fp8_layer_intermediates_match_vllm_triton(golden, fixture, scale):
+    g = golden(fixture)
     k = int(g["k"])
     T, H = g["x"].shape
     E = g["w1"].shape[0]
@@ -120,11 +134,12 @@ def test_fp8_layer_intermediates_match_vllm_triton(golden):
     assert np.array_equal(s, g["sorted_ids"]) and np.array_equal(e, g["expert_ids"])
     assert E - 1 not in e.tolist()  # the starved expert owns no block
     # the whole layer with intermediates
-    r = O.moe_forward_fp8(g["x"], g["logits"], g["w1"], g["w1_s"], g["w2"], g["w2_s"], k, want_intermediates=True)
+    r = O.moe_forward_fp8(g["x"], g["logits"], g["w1"], g["w1_s"], g["w2"], g["w2_s"], k, want_intermediates=True,
+                          scale=scale)
     assert np.array_equal(r["x_q"], g["x_q"]) and np.array_equal(r["x_s"], g["x_s"])
     # GEMM1 + silu: c2 is the bf16 activation the Triton chain fed to its requantisation
     c2 = g["c2"].reshape(T * k, -1)
-    c2q_ref, c2s_ref = O.quant_fp8_groups(c2)
+    c2q_ref, c2s_ref = O.quant_fp8_groups(c2, scale=scale)
     assert np.array_equal(c2q_ref, g["c2q"]) and np.array_equal(c2s_ref, g["c2s"])
     assert np.mean(r["c2q"] == g["c2q"]) > 0.99
     np.testing.assert_allclose(r["c2s"], g["c2s"], rtol=2 ** -7)

@@ -257,3 +257,16 @@ def test_the_probe_can_be_withheld_like_the_reference(monkeypatch):
     assert q._withheld() == {"dense_fusion", "fp8_determinism"}
     monkeypatch.delenv("PRISMYRA_WITHOUT")
     assert q._withheld() == set()
+
+
+def test_fused_experts_act_scale_option(monkeypatch):
+    from prismyra_b200.kernels.qwen3_moe import FusedExperts as FE
+
+    blk = Qwen3_5MoeSparseMoeBlock()
+    assert FE(blk, 4).act_scale == "fp32"
+    assert FE(Qwen3_5MoeSparseMoeBlock(), 4, act_scale="ue8m0").act_scale == "ue8m0"
+    monkeypatch.setenv("PRISMYRA_B200_ACT_SCALE", "ue8m0")
+    assert FE(Qwen3_5MoeSparseMoeBlock(), 4).act_scale == "ue8m0"
+    monkeypatch.setenv("PRISMYRA_B200_ACT_SCALE", "fp16")
+    with pytest.raises(AdapterError, match="act_scale"):
+        FE(Qwen3_5MoeSparseMoeBlock(), 4)
