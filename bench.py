@@ -213,11 +213,12 @@ def time_region(fn, steps: int, stream) -> float:
     return a.elapsed_time(b) / steps
 
 
-def vllm_gpu_path(layer: dict, tokens: list, steps: int, ours: dict) -> dict:
+def vllm_gpu_path(layer: dict, tokens: list, steps: int) -> dict:
     """The reference's own GPU path for the routed layer on this box (prismyra/kernels/qwen3_moe.py:184-197): vLLM's
     batch-invariant router matmul, fused_topk and fused_experts (FP8 w8a8, 128x128 block scales) on the same seeded
-    tensors, timed with CUDA events like the layer; ``ours`` maps a token count to this repository's ms per call
-    for the same shape.  Also the relative L2 difference of the two outputs (each with its own router)."""
+    tensors, timed with CUDA events like the layer, beside this repository's layer in the activation-scale rule vLLM
+    uses here (power-of-two scales when vLLM runs DeepGEMM with E8M0 scales, its default where DeepGEMM is installed;
+    else the correctly rounded fp32 scales), and the relative L2 difference of the two outputs (same logits)."""
     import torch
 
     from prismyra_b200 import ops
@@ -231,11 +232,16 @@ def vllm_gpu_path(layer: dict, tokens: list, steps: int, ours: dict) -> dict:
             router_linear = torch.nn.functional.linear
         quant = FusedMoEQuantConfig.make(quant_dtype=torch.float8_e4m3fn, block_shape=[128, 128],
                                          w1_scale=layer["w1_s"], w2_scale=layer["w2_s"])
+        try:
+            from vllm.utils import deep_gemm
+            act_scale = "ue8m0" if deep_gemm.is_deep_gemm_e8m0_used() else "fp32"
+        except Exception:  # noqa: BLE001
+            act_scale = "fp32"
     except Exception as e:  # noqa: BLE001 - reported, not fatal: the comparison is optional
         return {"unavailable": f"vllm does not import here: {type(e).__name__}: {e}"[:300]}
     stream = torch.cuda.current_stream()
     res = {"path": "vllm " + __import__("vllm").__version__ + ": linear_batch_invariant + fused_topk + "
-                   "fused_experts (FP8 w8a8 block 128x128)"}
+                   "fused_experts (FP8 w8a8 block 128x128)", "act_scale": act_scale}
     for T in tokens:
         x = layer["x"][:T].contiguous()
 
@@ -252,12 +258,22 @@ def vllm_gpu_path(layer: dict, tokens: list, steps: int, ours: dict) -> dict:
         except Exception as e:  # noqa: BLE001
             res[f"t{T}"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
             continue
-        mine = ops.forward_fp8(x, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K,
-                               router_w=layer["router_w"]).float()
-        rel = float((mine - ref_out.float()).norm() / ref_out.float().norm().clamp_min(1e-30))
-        res[f"t{T}"] = {"ms": ms, "tokens_per_s": T / (ms * 1e-3), "ours_ms": ours.get(T),
-                        "speedup_ours_over_vllm": (ms / ours[T]) if ours.get(T) else None,
-                        "rel_l2_ours_vs_vllm": rel}
+        logits = router_linear(x, layer["router_w"])
+
+        def mine():
+            return ops.forward_fp8(x, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K,
+                                   router_w=layer["router_w"], act_scale=act_scale)
+
+        for _ in range(3):
+            mine()
+        ours_ms = time_region(mine, 20, stream)
+        same = ops.forward_fp8(x, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K, logits=logits,
+                               act_scale=act_scale).float()
+        w, ids = fused_topk(x, logits, K, renormalize=True)[:2]
+        ref_same = fused_experts(x, layer["w1"], layer["w2"], w, ids, quant_config=quant).float()
+        rel = float((same - ref_same).norm() / ref_same.norm().clamp_min(1e-30))
+        res[f"t{T}"] = {"ms": ms, "tokens_per_s": T / (ms * 1e-3), "ours_ms": ours_ms,
+                        "speedup_ours_over_vllm": ms / ours_ms, "rel_l2_ours_vs_vllm_same_logits": rel}
     return res
 
 
@@ -304,23 +320,33 @@ def ep_stack(dev, rank: int, world: int, layers: int, tokens: int, steps: int):
     epr = E // world
     lo, hi = rank * epr, (rank + 1) * epr
     bias = synth.zipf_bias(E).to(dev)
+    from prismyra_b200 import ops
+
     stack = []
     # one peer exchange shared by all layers (a layer's exchange buffers are live only during its forward)
     exchange = ep.PeerExchange(E, K, H, I, rank, world, tokens, dev) if world > 1 else None
     for li in range(layers):
         L = synth.make_fp8_layer(8, H, I, E, seed=li, device=dev, gen_device="cuda")
-        b = ep.CudaBackend(L["w1"][lo:hi].contiguous(), L["w1_s"][lo:hi].contiguous(), L["w2"][lo:hi].contiguous(),
-                           L["w2_s"][lo:hi].contiguous(), L["router_w"], K, bias=bias)
-        stack.append(ep.PeerExpertParallelLayer(b, E, K, rank, world, exchange=exchange) if world > 1
-                     else ep.ExpertParallelLayer(b, E, K, rank, world))
+        if world > 1:
+            b = ep.CudaBackend(L["w1"][lo:hi].contiguous(), L["w1_s"][lo:hi].contiguous(),
+                               L["w2"][lo:hi].contiguous(), L["w2_s"][lo:hi].contiguous(), L["router_w"], K,
+                               bias=bias)
+            stack.append(ep.PeerExpertParallelLayer(b, E, K, rank, world, exchange=exchange))
+        else:  # one GPU holds every expert: the single-GPU layer itself (no dispatch to plan)
+            stack.append({k: L[k] for k in ("w1", "w1_s", "w2", "w2_s", "router_w")})
         del L
     g = torch.Generator("cuda").manual_seed(1000 + rank)
     x = torch.randn(tokens, H, generator=g, device=dev).to(torch.bfloat16)
+    bufs = [torch.empty_like(x), torch.empty_like(x)]
 
     def run():
         h = x
-        for layer in stack:
-            h = layer.forward(h)
+        for i, layer in enumerate(stack):
+            if world > 1:
+                h = layer.forward(h)
+            else:
+                h = ops.forward_fp8(h, layer["w1"], layer["w1_s"], layer["w2"], layer["w2_s"], K,
+                                    router_w=layer["router_w"], bias=bias, out=bufs[i % 2])
         return h
 
     for _ in range(2):
@@ -332,9 +358,7 @@ def ep_stack(dev, rank: int, world: int, layers: int, tokens: int, steps: int):
         t = torch.tensor([ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
-    from prismyra_b200 import ops
-
-    _, _, ids = ops.router_topk(x, stack[0].b.router_w, K, bias=bias)
+    _, _, ids = ops.router_topk(x, stack[0].b.router_w if world > 1 else stack[0]["router_w"], K, bias=bias)
     load = torch.bincount(ids.reshape(-1).long(), minlength=E).float()
     del stack
     if exchange is not None:
@@ -527,7 +551,7 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
 
     vllm_ref = None
     if world == 1 and not args.no_vllm:
-        vllm_ref = vllm_gpu_path(layer, [T_CTX, T_BRANCH], args.steps, {T_CTX: ms, T_BRANCH: b_ms})
+        vllm_ref = vllm_gpu_path(layer, [T_CTX, T_BRANCH], args.steps)
 
     if world > 1:
         ep_layer.close()  # every rank together: frees this layer's exchange before the stack makes its own

@@ -160,14 +160,17 @@ int pm_moe_forward_fp8(const void *x, const void *router_w, const void *logits, 
  *                            is installed);
  *   PM_FLAG_ACT_SCALE_RCP    s = max(amax, 1e-10) * fl(1/448): vLLM's Triton quantiser (fp8_utils.py:143-144), one ulp
  *                            away from the quotient for about half of all values.
- * Each value's code is the correctly rounded quotient x / s, clamped to +-448, rounded to e4m3. */
+ * Each value's code is the correctly rounded quotient x / s, clamped to +-448, rounded to e4m3.  bias (fp32 [E], may
+ * be NULL) is added to every logit before the ranking, as for pm_moe_router_topk (no counterpart in the reference:
+ * a benchmark's expert-load skew). */
 #define PM_FLAG_ACT_SCALE_UE8M0 1
 #define PM_FLAG_ACT_SCALE_RCP 2
 int pm_moe_quant_fp8_ex(const void *x, int T, int H, int k, const int32_t *slot_of, uint8_t *a_q, float *a_s,
                         int flags, pm_stream_t stream);
-int pm_moe_forward_fp8_ex(const void *x, const void *router_w, const void *logits, const uint8_t *w1,
-                          const float *w1_s, const uint8_t *w2, const float *w2_s, int T, int H, int I, int E, int k,
-                          int flags, void *out, void *workspace, size_t workspace_bytes, pm_stream_t stream);
+int pm_moe_forward_fp8_ex(const void *x, const void *router_w, const void *logits, const float *bias,
+                          const uint8_t *w1, const float *w1_s, const uint8_t *w2, const float *w2_s, int T, int H,
+                          int I, int E, int k, int flags, void *out, void *workspace, size_t workspace_bytes,
+                          pm_stream_t stream);
 
 /* The shared expert, `torch.sigmoid(self._gate(x)) * self.shared_expert(x)` (prismyra/kernels/qwen3_moe.py:198):
  * gate = bf16(sigmoid(bf16(x . w_sg))) (w_sg bf16 [H], the shared_expert_gate weight, qwen3_moe.py:172-183), and

@@ -50,7 +50,7 @@ SIGNATURES: dict[str, tuple] = {
     "pm_moe_scatter_rows": (_I, [_P, _I, _I, _I, _P, _P, _I, _P]),
     "pm_moe_forward_fp8": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _Z, _P]),
     "pm_moe_quant_fp8_ex": (_I, [_P, _I, _I, _I, _P, _P, _P, _I, _P]),
-    "pm_moe_forward_fp8_ex": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _Z, _P]),
+    "pm_moe_forward_fp8_ex": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _Z, _P]),
     "pm_moe_read_status": (_I, [_P, _P]),
     "pm_moe_align_noalloc": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P]),
     "pm_moe_quant_nvfp4": (_I, [_P, _I, _I, _I, _P, ctypes.c_float, _P, _P, _P]),

@@ -389,7 +389,8 @@ int pm_moe_combine(const void* c3, const int32_t* row_of, int T, int k, int H, v
 static int forward_fp8_impl(const void* x, const void* router_w, const void* logits, const uint8_t* w1,
                             const float* w1_s, const uint8_t* w2, const float* w2_s, int T, int H, int I, int E,
                             int k, const void* add, cudaEvent_t add_ready, void* out, void* workspace,
-                            size_t workspace_bytes, pm_stream_t stream, bool clear_status, int scale_rule = 0) {
+                            size_t workspace_bytes, pm_stream_t stream, bool clear_status, int scale_rule = 0,
+                            const float* bias = nullptr) {
     int st = check_dims(T, H, I, E, k);
     if (st != PM_OK) return st;
     if (T == 0) return PM_OK;
@@ -420,9 +421,9 @@ static int forward_fp8_impl(const void* x, const void* router_w, const void* log
     if (clear_status && cudaMemsetAsync(status, 0, L.len[PM_WS_STATUS], s) != cudaSuccess) return PM_ERR_CUDA;
     cudaError_t e;
     if (logits != nullptr)
-        e = launch_topk(logits, nullptr, T, E, k, topk_w, topk_ids, s);
+        e = launch_topk(logits, bias, T, E, k, topk_w, topk_ids, s);
     else
-        e = launch_router_topk(x, router_w, nullptr, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s,
+        e = launch_router_topk(x, router_w, bias, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s,
                                router_part);
     if (e != cudaSuccess) return PM_ERR_CUDA;
     int32_t* slot_of = reinterpret_cast<int32_t*>(R(PM_WS_SLOT_OF));
@@ -452,13 +453,14 @@ int pm_moe_forward_fp8(const void* x, const void* router_w, const void* logits, 
                             workspace, workspace_bytes, stream, true);
 }
 
-int pm_moe_forward_fp8_ex(const void* x, const void* router_w, const void* logits, const uint8_t* w1,
-                          const float* w1_s, const uint8_t* w2, const float* w2_s, int T, int H, int I, int E, int k,
-                          int flags, void* out, void* workspace, size_t workspace_bytes, pm_stream_t stream) {
+int pm_moe_forward_fp8_ex(const void* x, const void* router_w, const void* logits, const float* bias,
+                          const uint8_t* w1, const float* w1_s, const uint8_t* w2, const float* w2_s, int T, int H,
+                          int I, int E, int k, int flags, void* out, void* workspace, size_t workspace_bytes,
+                          pm_stream_t stream) {
     const int rule = scale_rule_of(flags);
     if (rule < 0) return PM_ERR_INVALID;
     return forward_fp8_impl(x, router_w, logits, w1, w1_s, w2, w2_s, T, H, I, E, k, nullptr, nullptr, out,
-                            workspace, workspace_bytes, stream, true, rule);
+                            workspace, workspace_bytes, stream, true, rule, bias);
 }
 
 // ------------------------------------------------------------------------------------------- shared expert

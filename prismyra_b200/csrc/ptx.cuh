@@ -9,6 +9,8 @@
 #include <cuda_fp8.h>
 #include <stdint.h>
 
+#include "moe_internal.h"
+
 #ifndef PM_WAIT_TIMEOUT_NS
 #define PM_WAIT_TIMEOUT_NS 2000000000ull  // 2 s: a healthy wait in these kernels lasts microseconds
 #endif

@@ -101,11 +101,12 @@ ACT_SCALES = {"fp32": 0, "ue8m0": _lib.FLAG_ACT_SCALE_UE8M0, "fp32_rcp": _lib.FL
 def forward_fp8(x: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch.Tensor, w2_s: torch.Tensor,
                 top_k: int, router_w: torch.Tensor | None = None, logits: torch.Tensor | None = None,
                 out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
-                act_scale: str = "fp32") -> torch.Tensor:
+                act_scale: str = "fp32", bias: torch.Tensor | None = None) -> torch.Tensor:
     """Routed FP8 experts for x [T, H] bf16; give ``router_w`` [E, H] bf16 or ``logits`` [T, E] bf16.
     ``act_scale`` picks the activation-scale rule (:data:`ACT_SCALES`): "fp32" (default) the correctly rounded
     max(amax, 1e-10)/448, as the reference's fused_experts computes on a GPU; "ue8m0" those scales rounded up to
-    powers of two, as vLLM does when it runs DeepGEMM with E8M0 scales; "fp32_rcp" vLLM's Triton rule."""
+    powers of two, as vLLM does when it runs DeepGEMM with E8M0 scales; "fp32_rcp" vLLM's Triton rule.  ``bias``
+    (fp32 [E]) is added to every logit before the ranking (a benchmark's expert-load skew)."""
     _need(act_scale in ACT_SCALES, f"act_scale must be one of {sorted(ACT_SCALES)}")
     _need(x.dim() == 2, "x must be [T, H]")
     T, H = x.shape
@@ -121,6 +122,8 @@ def forward_fp8(x: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch
         _cuda(logits, "logits", torch.bfloat16, (T, E))
     else:
         _cuda(router_w, "router_w", torch.bfloat16, (E, H))
+    if bias is not None:
+        _cuda(bias, "bias", torch.float32, (E,))
     if out is None:
         out = torch.empty_like(x)
     _cuda(out, "out", torch.bfloat16, (T, H))
@@ -131,7 +134,8 @@ def forward_fp8(x: torch.Tensor, w1: torch.Tensor, w1_s: torch.Tensor, w2: torch
     else:
         nbytes = workspace.numel()
     _lib.call(
-        "pm_moe_forward_fp8_ex", _p(x), _p(router_w), _p(logits), _p(_u8(w1)), _p(w1_s), _p(_u8(w2)), _p(w2_s),
+        "pm_moe_forward_fp8_ex", _p(x), _p(router_w), _p(logits), _p(bias), _p(_u8(w1)), _p(w1_s), _p(_u8(w2)),
+        _p(w2_s),
         T, H, I, E, top_k, ACT_SCALES[act_scale], _p(out), _p(workspace), nbytes, _stream(x.device),
     )
     return out
