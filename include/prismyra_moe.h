@@ -63,7 +63,8 @@ enum pm_region {
     PM_WS_A2_SCALE = 12, /* f32 [max_slots, I/128] (NVFP4: e4m3 [max_slots, I/16]) */
     PM_WS_C3 = 13,      /* bf16 [T*k, H] weighted expert outputs per (token, slot) */
     PM_WS_SLOT_OF = 14, /* i32 [T*k] slot of each flat index (the inverse of PM_WS_SORTED) */
-    PM_WS_ROUTER_PART = 15 /* f32 [H/256, T, E] router partial sums per 256-column chunk (small T; else empty) */
+    PM_WS_ROUTER_PART = 15, /* f32 [H/256, T, E] router partial sums per 256-column chunk (small T; else empty) */
+    PM_WS_SCHED = 16    /* i32 [1 + 2 * max_slots / 128] few-token GEMMs' work queue and per-block-half counters */
 };
 
 /* Version of this ABI; bumped on any incompatible change. */

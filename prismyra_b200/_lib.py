@@ -25,7 +25,7 @@ WS = {
     "status": 0, "logits": 1, "topk_w": 2, "topk_ids": 3, "counts": 4, "expert_off": 5, "sorted": 6,
     "expert_ids": 7, "num_post_pad": 8, "a1": 9, "a1_scale": 10, "a2": 11, "a2_scale": 12, "c3": 13,
     "slot_of": 14,
-    "router_part": 15,
+    "router_part": 15, "sched": 16,
 }
 
 _P = ctypes.c_void_p

@@ -66,7 +66,7 @@ static int current_device_info(DeviceInfo* out) {
 }
 
 // ------------------------------------------------------------------------------------------- workspace
-constexpr int kRegions = PM_WS_ROUTER_PART + 1;
+constexpr int kRegions = PM_WS_SCHED + 1;
 
 struct Layout {
     size_t off[kRegions];
@@ -104,6 +104,7 @@ static Layout layout_of(int T, int H, int I, int E, int k, int fmt) {
     L.len[PM_WS_C3] = (size_t)n * H * 2;
     L.len[PM_WS_SLOT_OF] = (size_t)n * 4;
     L.len[PM_WS_ROUTER_PART] = router_split_bytes(T, H, E);
+    L.len[PM_WS_SCHED] = (size_t)small_sched_ints(ms / kBlockM) * 4;
     size_t o = 0;
     for (int r = 0; r < kRegions; ++r) {
         L.off[r] = o;
@@ -295,6 +296,48 @@ static int small_gemm_fp8(int mode, const uint8_t* a_q, const float* a_s, const 
     return cuda_status(launch_gemm_fp8_small(mode, tt, tw, g, sms, s));
 }
 
+// Both few-tokens-per-expert GEMMs in one launch (the forward's path when use_small_gemm holds); sched has been
+// zeroed by the quantisation launch.
+static int small_fused_fp8(const uint8_t* a1, const float* a1s, const uint8_t* w1, const float* w1_s, uint8_t* a2,
+                           float* a2s, const uint8_t* w2, const float* w2_s, const int32_t* expert_ids,
+                           const int32_t* npp, const int32_t* sorted_ids, const float* topk_w, int max_slots,
+                           int n_valid, int H, int I, int E, void* c3, int32_t* sched, int32_t* err, int sms,
+                           cudaStream_t s, int scale_rule) {
+    CUtensorMap t1, tw1, t2, tw2;
+    if (!encode_tmap_2d_u8(&t1, a1, (uint64_t)H, (uint64_t)max_slots, (uint64_t)H, 128, 32) ||
+        !encode_tmap_2d_u8(&tw1, w1, (uint64_t)H, (uint64_t)E * 2 * I, (uint64_t)H, 128, 128) ||
+        !encode_tmap_2d_u8(&t2, a2, (uint64_t)I, (uint64_t)max_slots, (uint64_t)I, 128, 32) ||
+        !encode_tmap_2d_u8(&tw2, w2, (uint64_t)I, (uint64_t)E * H, (uint64_t)I, 128, 128))
+        return PM_ERR_CUDA;
+    SmallGemmArgs g[2];
+    memset(g, 0, sizeof(g));
+    for (int m = 0; m < 2; ++m) {
+        g[m].expert_ids = expert_ids;
+        g[m].num_post_pad = npp;
+        g[m].sorted_ids = sorted_ids;
+        g[m].n_valid = n_valid;
+        g[m].inter = I;
+        g[m].scale_rule = scale_rule;
+        g[m].err = err;
+    }
+    g[0].a_scale = a1s;
+    g[0].b_scale = w1_s;
+    g[0].n_total = 2 * I;
+    g[0].K = H;
+    g[0].n_tiles = I / 128;
+    g[0].out_q = a2;
+    g[0].out_s = a2s;
+    g[1].a_scale = a2s;
+    g[1].b_scale = w2_s;
+    g[1].n_total = H;
+    g[1].K = I;
+    g[1].n_tiles = H / 128;
+    g[1].topk_w = topk_w;
+    g[1].c3 = static_cast<__nv_bfloat16*>(c3);
+    for (int m = 0; m < 2; ++m) g[m].max_units = (max_slots / kBlockM) * g[m].n_tiles;
+    return cuda_status(launch_gemm_fp8_small_fused(t1, tw1, t2, tw2, g[0], g[1], sched, sms, s));
+}
+
 static int gemm1_fp8_run(const uint8_t* a_q, const float* a_s, const uint8_t* w1, const float* w1_s,
                          const int32_t* expert_ids, const int32_t* num_post_pad, int max_slots, int H, int I, int E,
                          uint8_t* out_q, float* out_s, int32_t* err, pm_stream_t stream, int scale_rule);
@@ -430,17 +473,28 @@ static int forward_fp8_impl(const void* x, const void* router_w, const void* log
     e = launch_align(topk_ids, T * k, E, reinterpret_cast<int32_t*>(R(PM_WS_COUNTS)), sorted, expert_ids, npp,
                      reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_OFF)), slot_of, s);
     if (e != cudaSuccess) return PM_ERR_CUDA;
-    e = launch_quant_fp8(x, T, H, k, slot_of, a1, a1s, s, scale_rule);
+    // Both few-token GEMMs in one launch once most experts are hit (T*k >= 2E); with fewer pairs nearly every down
+    // unit would wait for its block's few gate_up units, and two launches are faster.
+    const bool fused = use_small_gemm((long)T * k, H, I, E) && (long)T * k >= 2L * E &&
+                       gemm_fp8_small_fused_fits(H, I) && a16(a1s) && a16(a2s);
+    int32_t* sched = reinterpret_cast<int32_t*>(R(PM_WS_SCHED));
+    e = launch_quant_fp8(x, T, H, k, slot_of, a1, a1s, s, scale_rule, fused ? sched : nullptr,
+                         fused ? small_sched_ints(L.max_slots / kBlockM) : 0);
     if (e != cudaSuccess) return PM_ERR_CUDA;
-    if (use_small_gemm((long)T * k, H, I, E))
-        st = small_gemm_fp8(0, a1, a1s, w1, w1_s, expert_ids, npp, sorted, nullptr, L.max_slots, T * k, H, I, E, a2,
-                            a2s, nullptr, status, d.sms, s, scale_rule);
-    else
-        st = gemm1_fp8_run(a1, a1s, w1, w1_s, expert_ids, npp, L.max_slots, H, I, E, a2, a2s, status, stream,
-                           scale_rule);
-    if (st != PM_OK) return st;
-    st = pm_moe_gemm2_fp8(a2, a2s, w2, w2_s, expert_ids, npp, sorted, topk_w, L.max_slots, T, k, H, I, E, c3,
-                          status, stream);
+    if (fused) {
+        st = small_fused_fp8(a1, a1s, w1, w1_s, a2, a2s, w2, w2_s, expert_ids, npp, sorted, topk_w, L.max_slots,
+                             T * k, H, I, E, c3, sched, status, d.sms, s, scale_rule);
+    } else {
+        if (use_small_gemm((long)T * k, H, I, E))
+            st = small_gemm_fp8(0, a1, a1s, w1, w1_s, expert_ids, npp, sorted, nullptr, L.max_slots, T * k, H, I, E,
+                                a2, a2s, nullptr, status, d.sms, s, scale_rule);
+        else
+            st = gemm1_fp8_run(a1, a1s, w1, w1_s, expert_ids, npp, L.max_slots, H, I, E, a2, a2s, status, stream,
+                               scale_rule);
+        if (st != PM_OK) return st;
+        st = pm_moe_gemm2_fp8(a2, a2s, w2, w2_s, expert_ids, npp, sorted, topk_w, L.max_slots, T, k, H, I, E, c3,
+                              status, stream);
+    }
     if (st != PM_OK) return st;
     if (add_ready != nullptr && cudaStreamWaitEvent(s, add_ready, 0) != cudaSuccess) return PM_ERR_CUDA;
     return cuda_status(launch_combine(c3, nullptr, T, k, H, out, s, add));

@@ -77,8 +77,9 @@ cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int3
 // Quantise every token row of x to e4m3 with one fp32 scale per 128 columns.  With slot_of, each quantised row
 // is written to the k slots of its token (a_q [slots, H], a_s [slots, H/128]) instead of to row t.
 // scale_rule: how each group's scale is formed (e4m3_group_scale in ptx.cuh; 0 = the correctly rounded quotient).
+// zero (may be null): zero_n int32 counters the launch sets to 0 once its predecessor has completed.
 cudaError_t launch_quant_fp8(const void* x, int T, int H, int k, const int32_t* slot_of, uint8_t* x_q, float* x_s,
-                             cudaStream_t s, int scale_rule = 0);
+                             cudaStream_t s, int scale_rule = 0, int32_t* zero = nullptr, int zero_n = 0);
 // out[t] = bf16(sum_j c3[row(t*k + j)]) in fp32, j ascending; row = identity or row_of.
 cudaError_t launch_combine(const void* c3, const int32_t* row_of, int T, int k, int H, void* out, cudaStream_t s,
                            const void* add = nullptr);
@@ -149,6 +150,15 @@ bool gemm_fp8_small_fits(int mode, int K);
 // tm_tok: the slot-ordered FP8 activations with a {128, 32} box; tm_w: the weights with a {128, 128} box.
 cudaError_t launch_gemm_fp8_small(int mode, const CUtensorMap& tm_tok, const CUtensorMap& tm_w,
                                   const SmallGemmArgs& args, int num_sms, cudaStream_t s);
+// Both GEMMs in one persistent launch: the gate_up units, then the down units, taken from a work queue; a down
+// unit starts once every gate_up unit of its block half has stored its rows.  sched: small_sched_ints(blocks)
+// int32 set to 0 before the launch (the quantisation kernel does it).
+inline int small_sched_ints(int max_blocks) { return 1 + 2 * max_blocks; }
+bool gemm_fp8_small_fused_fits(int H, int I);
+cudaError_t launch_gemm_fp8_small_fused(const CUtensorMap& tm_tok1, const CUtensorMap& tm_w1,
+                                        const CUtensorMap& tm_tok2, const CUtensorMap& tm_w2,
+                                        const SmallGemmArgs& gate_up, const SmallGemmArgs& down, int32_t* sched,
+                                        int num_sms, cudaStream_t s);
 
 struct NvGemmArgs {
     const uint8_t* a_sf;          // blocked e4m3 scales of A: [rows/128][K/64][512]

@@ -17,9 +17,11 @@ namespace {
 __global__ void __launch_bounds__(256) quant_fp8_kernel(const __nv_bfloat16* __restrict__ x, int T, int H, int k,
                                                         const int32_t* __restrict__ slot_of,
                                                         uint8_t* __restrict__ x_q, float* __restrict__ x_s,
-                                                        int scale_rule) {
+                                                        int scale_rule, int32_t* __restrict__ zero, int zero_n) {
     pdl_wait();
     pdl_trigger();
+    // counters the next kernel starts from zero (its work queue and hand-off counters)
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < zero_n; i += gridDim.x * blockDim.x) zero[i] = 0;
     const int lane = threadIdx.x & 31, sub = lane & 15;
     const int G = H / 128;
     const long items = (long)T * G;
@@ -104,15 +106,15 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
 }  // namespace
 
 cudaError_t launch_quant_fp8(const void* x, int T, int H, int k, const int32_t* slot_of, uint8_t* x_q, float* x_s,
-                             cudaStream_t s, int scale_rule) {
-    if (T == 0) return cudaSuccess;
+                             cudaStream_t s, int scale_rule, int32_t* zero, int zero_n) {
+    if (T == 0) return zero_n > 0 ? cudaMemsetAsync(zero, 0, sizeof(int32_t) * (size_t)zero_n, s) : cudaSuccess;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const long pairs = ((long)T * (H / 128) + 1) / 2;  // one warp per two (token, group) items
     const int blocks = (int)min((pairs + 7) / 8, (long)sms * 16);
     PM_TRY(launch_pdl(quant_fp8_kernel, dim3(blocks), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(x), T, H, k,
-                      slot_of, x_q, x_s, scale_rule));
+                      slot_of, x_q, x_s, scale_rule, zero, zero_n));
     return cudaGetLastError();
 }
 

@@ -185,8 +185,8 @@ constexpr int kAlignRounds = 16;  // rounds of 256 indices a chunk may have for 
 // within a round of 256 indices, equal experts are ordered by warp (per-warp counts) and by lane (match mask).
 // The block -> expert table and the padding slots (value n) are written warp-cooperatively, experts spread over
 // the CTAs; CTA 0 writes the expert offsets and the total.  With a single chunk (counts == nullptr) pass 1 is not
-// launched: every CTA counts the (at most one chunk of) indices itself, CTA 0 scatters them and the others only
-// share the padding writes.
+// launched: every CTA counts the (at most one chunk of) indices itself; all CTAs and the scatter: a warp per expert walks the indices in order and places that expert's
+// with ballots (stable without any per-round synchronisation).
 __global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __restrict__ ids, int n, int E, int chunk,
                                                             int nchunks, const int32_t* __restrict__ counts,
                                                             int32_t* __restrict__ sorted,
@@ -200,7 +200,8 @@ __global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __res
     int32_t* base = sm;            // [E]  next slot of each expert for this chunk
     int32_t* pad = sm + E;         // [E]  padded totals, then padded offsets
     int32_t* totv = sm + 2 * E;    // [E]  indices per expert
-    int32_t* wcnt = sm + 3 * E;    // [8][E]
+    int32_t* wcnt = sm + 3 * E;    // [8][E]; single chunk: [E] counts, then the n <= 1024 indices' experts
+    int32_t* sids = wcnt + E;
     __shared__ int32_t wsum[8];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool single = counts == nullptr;
@@ -218,6 +219,8 @@ __global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __res
     }
     int tot[kAlignEPT], pre[kAlignEPT];
     if (counts == nullptr) {  // single chunk: count here
+#pragma unroll
+        for (int r = 0; r < 4; ++r) sids[r * 256 + tid] = idv[r];
         for (int e = tid; e < E; e += 256) wcnt[e] = 0;
         __syncthreads();
 #pragma unroll
@@ -307,6 +310,25 @@ __global__ void __launch_bounds__(256) align_scatter_kernel(const int32_t* __res
     }
     __syncthreads();
 
+    if (single) {
+        // a warp per expert: its indices in ascending order, 32 at a time
+        for (int e = (int)blockIdx.x * 8 + warp; e < E; e += (int)gridDim.x * 8) {
+            int pos = pad[e];
+            for (int i0 = 0; i0 < n; i0 += 32) {
+                const int i = i0 + lane;
+                const bool hit = i < n && sids[i] == e;
+                const uint32_t b = __ballot_sync(0xffffffffu, hit);
+                if (hit) {
+                    const int p = pos + __popc(b & ((1u << lane) - 1u));
+                    sorted[p] = i;
+                    if (slot_of != nullptr) slot_of[i] = p;
+                }
+                pos += __popc(b);
+            }
+        }
+        return;
+    }
+
     // one round of up to 256 indices starting at r0; e_in is this thread's id (or -1 past the chunk)
     auto round = [&](int r0, int e_in) {
         for (int q = tid; q < 8 * E; q += 256) wcnt[q] = 0;
@@ -383,7 +405,8 @@ cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int3
     }
     // a single chunk is scattered by CTA 0; the extra CTAs only share the padding writes
     const int grid = nchunks > 1 ? nchunks : max(1, min(16, E / 8));
-    PM_TRY(launch_pdl(align_scatter_kernel, dim3(grid), dim3(256), sizeof(int32_t) * 11 * E, s, ids, n, E, chunk,
+    const size_t smem = sizeof(int32_t) * (3 * (size_t)E + (size_t)(nchunks > 1 ? 8 * E : max(8 * E, E + 1024)));
+    PM_TRY(launch_pdl(align_scatter_kernel, dim3(grid), dim3(256), smem, s, ids, n, E, chunk,
                       nchunks, nchunks > 1 ? counts : nullptr, sorted, expert_ids, num_post_pad, expert_off,
                       slot_of));
     return cudaGetLastError();

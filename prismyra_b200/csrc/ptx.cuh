@@ -83,6 +83,27 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
+// A counter in global memory that other CTAs of this grid raise (atomically, after a fence): poll it with
+// GPU-scope acquire loads until it reaches `target`.  Returns false (and raises *abort) on timeout, or once another
+// thread of the CTA has raised *abort.
+__device__ __forceinline__ bool wait_counter_gpu(const int* p, int target, volatile int* abort) {
+    const uint64_t t0 = globaltimer();
+    while (true) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        if (v >= target) return true;
+        if (*abort) return false;
+        if (globaltimer() - t0 > PM_WAIT_TIMEOUT_NS) {
+            *abort = 1;
+            return false;
+        }
+    }
+}
+
+// Orders this thread's earlier generic-proxy memory accesses (such as the acquire above) before its later
+// async-proxy (TMA, bulk copy) accesses of global memory.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 // ------------------------------------------------------------------------------------------- TMA
 // 2-D tiled bulk tensor load into this CTA's shared memory, completing on an mbarrier (transaction bytes).
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
