@@ -430,6 +430,32 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
         ms = float(t.item())
     value = world * T_CTX / (ms * 1e-3)
 
+    ep_phases = None
+    if world > 1:
+        # per-phase device times of the expert-parallel step (outside the timed region; medians of a few steps,
+        # then the maximum over the ranks), and the NVLink bytes this rank's rows send: a remote pair's FP8 row
+        # and scales out, its weighted bf16 row back
+        runs = []
+        for _ in range(5):
+            marks = []
+            ep_layer.forward(x, marks=marks)
+            runs.append(marks)
+        torch.cuda.synchronize()
+        names = ep.PeerExpertParallelLayer.PHASES
+        per = torch.tensor([[m[i].elapsed_time(m[i + 1]) for i in range(len(names))] for m in runs])
+        med = per.median(dim=0).values.to(dev)
+        torch.distributed.all_reduce(med, op=torch.distributed.ReduceOp.MAX)
+        own = torch.div(ep_layer.b.route(x)[1].reshape(-1), epr, rounding_mode="floor")
+        remote = int((own != rank).sum().item())
+        sent = remote * (H + (H // 128) * 4 + H * 2)
+        t = torch.tensor([float(sent)], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ep_phases = {"ms": {n: round(float(v), 4) for n, v in zip(names, med.tolist())},
+                     "nvlink_bytes_per_rank_max": int(t.item()),
+                     "nvlink_ms_at_770_gbs": float(t.item()) / 770e9 * 1e3,
+                     "note": "median of 5 steps per rank, max over ranks; count/dispatch/down end with a device "
+                             "barrier across the ranks"}
+
     # end to end through the public calls with host buffers: every step uploads its pinned x and downloads its
     # result to pinned memory, consecutive steps overlapping (a step's upload runs during the previous step's
     # layer, its download during the next step's layer): ops.forward_fp8_host_async on one GPU, ops.host_async
@@ -599,6 +625,8 @@ def run_b200(args, rank: int, world: int, local: int) -> None:
         "clocks": clk.summary(),
     }
     line["nvfp4_prepare"] = prep
+    if ep_phases is not None:
+        line["ep_phases"] = ep_phases
     if block is not None:
         line["block_t5120"] = block
     if vllm_ref is not None:

@@ -303,9 +303,20 @@ class PeerExpertParallelLayer:
         if (self.x.E, self.x.k, self.x.H, self.x.I, self.x.world) != (num_experts, top_k, H, I2 // 2, world):
             raise ValueError("the exchange was made for another layer shape")
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    PHASES = ("route", "count", "dispatch", "gate_up", "down", "combine")
+
+    def forward(self, x: torch.Tensor, marks: list | None = None) -> torch.Tensor:
+        """``marks`` (a list, optional): a CUDA event is recorded on the stream after each phase of :data:`PHASES`
+        (preceded by one at the start) and appended, for per-phase device times; the work is unchanged."""
         from . import _lib, ops
 
+        def mark():
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks.append(ev)
+
+        mark()
         X = self.x
         T, H = x.shape
         if T > X.max_tokens or H != X.H:
@@ -315,24 +326,31 @@ class PeerExpertParallelLayer:
         stream = torch.cuda.current_stream(X.dev).cuda_stream
         w, ids = self.b.route(x)
         _, _, _, off, slot_of, _ = ops.align(ids, E)  # own pairs by global expert: rank within the expert
+        mark()
         X.meta.fill_(-1)
         _lib.call("pm_ep_count", P(ids), T * k, E, G, self.rank, P(X.peer["cm"]), stream)
         X.barrier(stream)
+        mark()
         _lib.call("pm_ep_offsets", P(X.cm), G, E, X.epr, self.rank, P(X.base), P(X.eids), P(X.npp), X.cap,
                   P(X.err), stream)
         _lib.call("pm_ep_dispatch_quant", P(x), T, H, k, P(ids), P(w), P(slot_of), P(off), P(X.base), E, X.epr,
                   self.rank, X.cap, P(X.peer["a1"]), P(X.peer["a1s"]), P(X.peer["meta"]), P(X.peer["wgt"]),
                   P(X.err), stream)
         X.barrier(stream)
+        mark()
         _lib.call("pm_ep_local_rows", P(X.meta), P(X.npp), X.cap, H, G, X.max_tokens * k, P(X.peer["back"]),
                   P(X.dst_rows), P(X.err), stream)
         ops.gemm1_fp8(X.a1, X.a1s, self.b.w1, self.b.w1_s, X.eids, X.npp, out=(X.a2, X.a2s, X.err[1:2]))
+        mark()
         # the down GEMM stores each weighted row straight into its source rank's result row
         w2 = self.b.w2
         _lib.call("pm_ep_gemm2_fp8", P(X.a2), P(X.a2s), P(ops._u8(w2)), P(self.b.w2_s), P(X.eids), P(X.npp),
                   P(X.wgt), P(X.dst_rows), X.cap, H, X.I, w2.shape[0], P(X.err[2:3]), stream)
         X.barrier(stream)
-        return ops.combine(X.back[: T * k], T, k)
+        mark()
+        out = ops.combine(X.back[: T * k], T, k)
+        mark()
+        return out
 
     def errors(self) -> int:
         return self.x.errors()
