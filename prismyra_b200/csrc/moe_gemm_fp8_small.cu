@@ -23,11 +23,10 @@
 // rows) and token columns of half (w-4)/4 of the unit.  TMEM is a ring of eight 64-column slots: a down K block
 // takes one, a gate_up K block one (gate at +0, up at +32) when the half holds one token sub-block and two (gate,
 // up) when it holds two; the MMA thus runs up to eight K blocks ahead of the promotion, through a unit's epilogue.
-// An M=128 MMA with a token-sized N costs about as much as one with N=128, and a dependent chain on one accumulator
-// issues at about half the rate of two interleaved ones, so the MMA thread issues the K blocks of a unit in pairs,
-// their accumulators' chains interleaved (each accumulator still sums its K block's four steps in order: the bits
-// do not change).  setmaxnreg gives warpgroup 0 64 registers and the promotion warpgroups 216 (64*128 + 216*256 =
-// 63488 <= 168*384, the launch's total).  Every wait is bounded.
+// An M=128 FP8 MMA with N <= 128 costs ~107 cycles in a chain on one accumulator whatever N is, but ~196 when
+// consecutive instructions alternate between two accumulators (~143 over four): the MMA thread issues each
+// accumulator's four K steps back to back (gate, then up).  setmaxnreg gives warpgroup 0 64 registers and the
+// promotion warpgroups 216 (64*128 + 216*256 = 63488 <= 168*384, the launch's total).  Every wait is bounded.
 #include <atomic>
 
 #include "moe_internal.h"
@@ -50,9 +49,20 @@ constexpr uint32_t kSlotCols = 64;
 constexpr int kQueue = 4;            // units handed from the producer to the MMA and promotion warps
 constexpr int kMaxBlocks = 512;      // 128-slot blocks a launch may have (the few-token regime has far fewer)
 // Stage bytes: two weight tiles (gate, up) or one (down), and up to 64 token rows.
-template <int MODE> __host__ __device__ constexpr int stage_bytes() { return (MODE == 1 ? 1 : 2) * kWBytes + kTokBytes; }
+template <int MODE> __host__ __device__ constexpr int stage_bytes() {
+    return (MODE == 1 ? 1 : 2) * kWBytes + kTokBytes;
+}
 // TMEM slots one K block of a unit with nsub token sub-blocks takes (m: 0 gate_up, 1 down).
 __device__ __forceinline__ int slots_per_kblock(int m, int nsub) { return m == 0 ? nsub : 1; }
+
+// Per-unit values the promotion warps need, loaded ahead by warp 2: the unit's two weight-scale rows (gate and up;
+// down: one) and, for a down unit, the flat index and routing weight of each of the half's 64 slots.
+struct UnitRec {
+    float bg[64];
+    float bu[64];
+    int fl[64];
+    float wl[64];
+};
 
 struct SmallTail {
     uint64_t full[kMaxStages];
@@ -65,6 +75,8 @@ struct SmallTail {
     uint64_t dbar[2];     // fused: every promotion thread has stored its rows of a gate_up unit (by parity)
     uint64_t qfull[kQueue];
     uint64_t qempty[kQueue];
+    uint64_t ufull[2];    // the unit record (by unit parity) is loaded
+    uint64_t uempty[2];   // the promotion warps are done with it
     uint64_t drain;
     int2 queue[kQueue];   // (unit index or -1 at the end, expert * 8 + real token sub-blocks)
     uint32_t tmem_base;
@@ -73,6 +85,7 @@ struct SmallTail {
     int n_second;               // blocks whose second half holds tokens, listed in ascending order:
     int second[kMaxBlocks];
     int wcount[kThreads / 32];  // per-warp counts of the listing
+    UnitRec urec[2];
 };
 
 // A launch's units, in order: per GEMM (gate_up, then down when fused), the first 64-slot halves of all blocks, then
@@ -147,25 +160,24 @@ __device__ __forceinline__ bool run_unit(const SmallGemmArgs& a, SmallTail* tail
     const int q = warp & 3, half = (warp - kEpiWarp0) >> 2;
     const int r = q * 32 + lane;  // weight row of the unit (output column nt*128 + r)
     const int KB = a.K / 128;
-    const int nb_total = a.n_total / 128;
     const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
     const int col0 = half * C;                  // first token column of this thread within the unit
     const int row0 = un.hp * 64 + col0;         // ... as a slot of block mb
     const uint32_t par = (uint32_t)ring.local & 1u, use = (uint32_t)ring.local >> 1;
     const uint32_t xpar = (uint32_t)ring.n0 & 1u, xuse = (uint32_t)ring.n0 >> 1;  // gate_up units only
 
-    // weight block scales of the unit, lane-distributed (lane l holds K blocks l and l + 32)
-    const float* bsg = a.b_scale + ((size_t)e * nb_total + un.nt) * KB;
-    const float* bsu = a.b_scale + ((size_t)e * nb_total + (MODE == 0 ? a.inter / 128 : 0) + un.nt) * KB;
-    const float g0 = lane < KB ? bsg[lane] : 0.0f, g1 = lane + 32 < KB ? bsg[lane + 32] : 0.0f;
-    const float u0 = (MODE == 0 && lane < KB) ? bsu[lane] : 0.0f;
-    const float u1 = (MODE == 0 && lane + 32 < KB) ? bsu[lane + 32] : 0.0f;
-    // down: flat index and routing weight of each token column (lane l: column col0 + l)
+    // the unit record: weight block scales lane-distributed (lane l holds K blocks l and l + 32) and, down, the flat
+    // index and routing weight of each token column (lane l: column col0 + l)
+    if (!mbar_wait(smem_u32(&tail->ufull[par]), use & 1u, abort)) return false;
+    const UnitRec& R = tail->urec[par];
+    const float g0 = lane < KB ? R.bg[lane] : 0.0f, g1 = lane + 32 < KB ? R.bg[lane + 32] : 0.0f;
+    const float u0 = (MODE == 0 && lane < KB) ? R.bu[lane] : 0.0f;
+    const float u1 = (MODE == 0 && lane + 32 < KB) ? R.bu[lane + 32] : 0.0f;
     int fl = 0;
     float wl = 0.0f;
     if (MODE == 1) {
-        fl = lane < C ? a.sorted_ids[un.mb * 128 + row0 + lane] : a.n_valid;
-        wl = fl < a.n_valid ? a.topk_w[fl] : 0.0f;
+        fl = lane < C ? R.fl[col0 + lane] : a.n_valid;
+        wl = lane < C ? R.wl[col0 + lane] : 0.0f;
     }
 
     float accg[C], accu[MODE == 0 ? C : 1];
@@ -272,6 +284,8 @@ __device__ __forceinline__ bool run_unit(const SmallGemmArgs& a, SmallTail* tail
             if (f < a.n_valid) a.c3[(size_t)f * H + un.nt * 128 + r] = __float2bfloat16_rn(accg[i] * w);
         }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&tail->uempty[par]));
     return true;
 }
 
@@ -316,7 +330,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < kQueue; ++b) {
             mbar_init(smem_u32(&tail->qfull[b]), 1);
-            mbar_init(smem_u32(&tail->qempty[b]), 1 + kEpiWarps);  // the MMA thread and the promotion warps
+            mbar_init(smem_u32(&tail->qempty[b]), 2 + kEpiWarps);  // the MMA thread, warp 2, the promotion warps
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&tail->ufull[b]), 1);
+            mbar_init(smem_u32(&tail->uempty[b]), kEpiWarps);
         }
         mbar_init(smem_u32(&tail->drain), 1);
         tail->abort = 0;
@@ -470,6 +488,39 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
+        } else if (warp == 2) {
+            // ---------------------------------------------------------------- unit records (warp 2)
+            for (int nq = 0, local = 0;; ++nq) {
+                const uint32_t qs = (uint32_t)nq % kQueue, qu = (uint32_t)nq / kQueue;
+                if (!mbar_wait(smem_u32(&tail->qfull[qs]), qu & 1u, abort)) break;
+                const int2 ref = tail->queue[qs];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&tail->qempty[qs]));
+                if (ref.x < 0) break;
+                int ph = 0;
+                const Unit un = sp.resolve(tail->second, ref.x, ph);
+                const SmallGemmArgs& A = ph ? a1 : a0;
+                const int m = MODE == 2 ? ph : MODE, e = ref.y >> 3;
+                const uint32_t par = (uint32_t)local & 1u, use = (uint32_t)local >> 1;
+                ++local;
+                if (!mbar_wait(smem_u32(&tail->uempty[par]), (use & 1u) ^ 1u, abort)) break;
+                UnitRec& R = tail->urec[par];
+                const int KB = A.K / 128, nb_total = A.n_total / 128;
+                const float* bs = A.b_scale + (size_t)e * nb_total * KB;
+                for (int j = lane; j < KB; j += 32) {
+                    R.bg[j] = bs[(size_t)un.nt * KB + j];
+                    if (m == 0) R.bu[j] = bs[(size_t)(A.inter / 128 + un.nt) * KB + j];
+                }
+                if (m == 1) {
+                    for (int j = lane; j < 64; j += 32) {
+                        const int f = A.sorted_ids[un.mb * 128 + un.hp * 64 + j];
+                        R.fl[j] = f;
+                        R.wl[j] = f < A.n_valid ? A.topk_w[f] : 0.0f;
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&tail->ufull[par]));
+            }
         } else if (warp == 1 && lane == 0) {
             // ---------------------------------------------------------------- MMA issuer
             int stage = 0;
@@ -487,55 +538,39 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int nsub = ref.y & 7, KB = (ph ? a1.K : a0.K) / 128;
                 const uint32_t idesc = idesc_f32acc(0 /*e4m3*/, 0 /*e4m3*/, 128, 32u * (uint32_t)nsub);
                 const int spk = slots_per_kblock(m, nsub);
-                for (int kb = 0; kb < KB && ok; kb += 2) {
-                    // two K blocks (one at an odd end): their slots and stages, then the interleaved chains
-                    const int np = KB - kb >= 2 ? 2 : 1;
-                    uint32_t sl[2][2] = {{0, 0}, {0, 0}}, st[2] = {0, 0};
+                for (int kb = 0; kb < KB && ok; ++kb) {
+                    uint32_t sl[2] = {0, 0};
 #pragma unroll
-                    for (int p = 0; p < 2; ++p) {
-                        if (p >= np || !ok) break;
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            if (h >= spk) break;
-                            const uint32_t slot = it % kSlots, use = it / kSlots;
-                            ++it;
-                            if (!mbar_wait(smem_u32(&tail->tempty[slot]), (use & 1u) ^ 1u, abort)) { ok = false; break; }
-                            sl[p][h] = slot;
-                        }
-                        if (!ok) break;
-                        if (!mbar_wait(smem_u32(&tail->full[stage]), phase, abort)) { ok = false; break; }
-                        st[p] = (uint32_t)stage;
-                        if (++stage == stages) { stage = 0; phase ^= 1u; }
+                    for (int h = 0; h < 2; ++h) {
+                        if (h >= spk) break;
+                        const uint32_t slot = it % kSlots, use = it / kSlots;
+                        ++it;
+                        if (!mbar_wait(smem_u32(&tail->tempty[slot]), (use & 1u) ^ 1u, abort)) { ok = false; break; }
+                        sl[h] = slot;
                     }
                     if (!ok) break;
+                    if (!mbar_wait(smem_u32(&tail->full[stage]), phase, abort)) { ok = false; break; }
                     tc_fence_after();
-                    uint64_t dwg[2], dwu[2], dt[2];
-                    uint32_t dg[2], du[2];
+                    const uint32_t base = sbase + stage * kStageBytes;
+                    const uint64_t dwg = desc_kmajor_sw128(base);
+                    const uint64_t dwu = desc_kmajor_sw128(base + kWBytes);
+                    const uint64_t dt = desc_kmajor_sw128(base + (m == 0 ? 2 : 1) * kWBytes);
+                    const uint32_t dg = tmem_base + sl[0] * kSlotCols;
+                    const uint32_t du = spk == 1 ? dg + 32 : tmem_base + sl[1] * kSlotCols;
+                    // each accumulator's four K steps back to back: a chain on one accumulator issues at ~107
+                    // cycles per MMA, alternating accumulators at every instruction at ~196
 #pragma unroll
-                    for (int p = 0; p < 2; ++p) {
-                        const uint32_t base = sbase + st[p] * kStageBytes;
-                        dwg[p] = desc_kmajor_sw128(base);
-                        dwu[p] = desc_kmajor_sw128(base + kWBytes);
-                        dt[p] = desc_kmajor_sw128(base + (m == 0 ? 2 : 1) * kWBytes);
-                        dg[p] = tmem_base + sl[p][0] * kSlotCols;
-                        du[p] = spk == 1 ? dg[p] + 32 : tmem_base + sl[p][1] * kSlotCols;
+                    for (int k = 0; k < 4; ++k)  // 32 e4m3 (32 bytes) of K per instruction
+                        mma_f8f6f4(dg, dwg + 2 * k, dt + 2 * k, idesc, k > 0 ? 1u : 0u);
+                    if (m == 0) {
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            mma_f8f6f4(du, dwu + 2 * k, dt + 2 * k, idesc, k > 0 ? 1u : 0u);
                     }
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {  // 32 e4m3 (32 bytes) of K per instruction
-#pragma unroll
-                        for (int p = 0; p < 2; ++p) {
-                            if (p >= np) break;
-                            mma_f8f6f4(dg[p], dwg[p] + 2 * k, dt[p] + 2 * k, idesc, k > 0 ? 1u : 0u);
-                            if (m == 0) mma_f8f6f4(du[p], dwu[p] + 2 * k, dt[p] + 2 * k, idesc, k > 0 ? 1u : 0u);
-                        }
-                    }
-#pragma unroll
-                    for (int p = 0; p < 2; ++p) {
-                        if (p >= np) break;
-                        mma_commit(smem_u32(&tail->empty[st[p]]));
-                        mma_commit(smem_u32(&tail->tfull[sl[p][0]]));
-                        if (spk == 2) mma_commit(smem_u32(&tail->tfull[sl[p][1]]));
-                    }
+                    mma_commit(smem_u32(&tail->empty[stage]));
+                    mma_commit(smem_u32(&tail->tfull[sl[0]]));
+                    if (spk == 2) mma_commit(smem_u32(&tail->tfull[sl[1]]));
+                    if (++stage == stages) { stage = 0; phase ^= 1u; }
                 }
             }
             mma_commit(smem_u32(&tail->drain));
