@@ -273,9 +273,14 @@ int pm_moe_align_noalloc(const int32_t *topk_ids, int T, int k, int E, int32_t *
  *                     wait_limit_ns nanoseconds (0: the library's 2 s); on timeout *err = 1 and the kernel returns
  *   pm_ep_offsets     from the full count matrix: for each global expert, where this rank's pairs of it start in
  *                     the owner's slot space (experts padded to 128 slots, sources in rank order), and the block
- *                     table and slot count of this rank's own experts
+ *                     table and slot count of this rank's own experts; with bounds (int32 [groups + 1], may be
+ *                     NULL) also the first slot of each of `groups` equal groups of its experts and the slot count
  *   pm_ep_dispatch_quant  per-token per-128 e4m3 quantisation (as pm_moe_quant_fp8) stored straight into the
- *                     owners' slots, with each slot's (source rank << 24 | pair index) and routing weight; T*k < 2^24
+ *                     owners' slots, with each slot's (source rank << 24 | pair index) and routing weight; T*k < 2^24;
+ *                     only pairs whose expert is local expert [local_lo, local_hi) of its owner; on at most max_sms
+ *                     SMs' worth of blocks (0: all), so that it can run beside a GEMM that leaves those SMs free
+ *   pm_ep_gemm1_fp8   the gate_up GEMM of pm_moe_gemm1_fp8 over slots [bounds[group], bounds[group + 1]) of this
+ *                     rank's slot space, on at most max_sms SMs (0: all)
  *   pm_ep_local_rows  per slot, the address of its source rank's result row for its pair (0 for padding)
  *   pm_ep_gemm2_fp8   the down GEMM of pm_moe_gemm2_fp8 over this rank's slots, each weighted bf16 row stored to
  *                     dst_rows[slot] (another rank's memory over NVLink) instead of a local C3 */
@@ -287,11 +292,16 @@ int pm_ep_count(const int32_t *ids, int n, int E, int G, int rank, const uint64_
 int pm_ep_barrier(const uint64_t *peer_flag, unsigned *own_flag, int G, unsigned target, int32_t *err,
                   uint64_t wait_limit_ns, pm_stream_t stream);
 int pm_ep_offsets(const int32_t *cm, int G, int E, int epr, int rank, int32_t *base, int32_t *expert_ids,
-                  int32_t *num_post_pad, int cap_slots, int32_t *err, pm_stream_t stream);
+                  int32_t *num_post_pad, int cap_slots, int32_t *err, int32_t *bounds, int groups,
+                  pm_stream_t stream);
 int pm_ep_dispatch_quant(const void *x, int T, int H, int k, const int32_t *topk_ids, const float *topk_w,
                          const int32_t *slot_local, const int32_t *expert_off_local, const int32_t *base, int E,
                          int epr, int rank, int cap_slots, const uint64_t *peer_a1, const uint64_t *peer_a1_scale,
-                         const uint64_t *peer_meta, const uint64_t *peer_weight, int32_t *err, pm_stream_t stream);
+                         const uint64_t *peer_meta, const uint64_t *peer_weight, int32_t *err, int local_lo,
+                         int local_hi, int max_sms, pm_stream_t stream);
+int pm_ep_gemm1_fp8(const uint8_t *a_q, const float *a_s, const uint8_t *w1, const float *w1_s,
+                    const int32_t *expert_ids, const int32_t *bounds, int group, int cap_slots, int H, int I, int E,
+                    uint8_t *out_q, float *out_s, int32_t *err, int max_sms, pm_stream_t stream);
 int pm_ep_local_rows(const int32_t *meta, const int32_t *num_post_pad, int cap_slots, int H, int G, int n_pairs,
                      const uint64_t *peer_back, uint64_t *dst_rows, int32_t *err, pm_stream_t stream);
 int pm_ep_gemm2_fp8(const uint8_t *a_q, const float *a_s, const uint8_t *w2, const float *w2_s,

@@ -72,8 +72,10 @@ SIGNATURES: dict[str, tuple] = {
     "pm_ep_free": (_I, [_P]),
     "pm_ep_count": (_I, [_P, _I, _I, _I, _I, _P, _P]),
     "pm_ep_barrier": (_I, [_P, _P, _I, ctypes.c_uint, _P, ctypes.c_uint64, _P]),
-    "pm_ep_offsets": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _I, _P, _P]),
-    "pm_ep_dispatch_quant": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
+    "pm_ep_offsets": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _I, _P, _P, _I, _P]),
+    "pm_ep_dispatch_quant": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _I,
+                                  _P]),
+    "pm_ep_gemm1_fp8": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _I, _P]),
     "pm_ep_local_rows": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "pm_ep_gemm2_fp8": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
 }

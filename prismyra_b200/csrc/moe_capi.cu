@@ -941,19 +941,23 @@ int pm_ep_barrier(const uint64_t* peer_flag, unsigned* own_flag, int G, unsigned
 }
 
 int pm_ep_offsets(const int32_t* cm, int G, int E, int epr, int rank, int32_t* base, int32_t* expert_ids,
-                  int32_t* num_post_pad, int cap_slots, int32_t* err, pm_stream_t stream) {
+                  int32_t* num_post_pad, int cap_slots, int32_t* err, int32_t* bounds, int groups,
+                  pm_stream_t stream) {
     if (!cm || !base || !expert_ids || !num_post_pad || !err || G <= 0 || epr <= 0 || E != G * epr ||
         E > kMaxExperts || rank < 0 || rank >= G || cap_slots % kBlockM != 0)
         return PM_ERR_INVALID;
+    if (bounds != nullptr && (groups < 1 || epr % groups != 0)) return PM_ERR_INVALID;
     return cuda_status(launch_ep_offsets(cm, G, E, epr, rank, base, expert_ids, num_post_pad, cap_slots / kBlockM,
-                                         err, (cudaStream_t)stream));
+                                         err, bounds, groups, (cudaStream_t)stream));
 }
 
 int pm_ep_dispatch_quant(const void* x, int T, int H, int k, const int32_t* topk_ids, const float* topk_w,
                          const int32_t* slot_local, const int32_t* expert_off_local, const int32_t* base, int E,
                          int epr, int rank, int cap_slots, const uint64_t* peer_a1, const uint64_t* peer_a1_scale,
-                         const uint64_t* peer_meta, const uint64_t* peer_weight, int32_t* err, pm_stream_t stream) {
-    if (T < 0 || H <= 0 || H % 128 != 0 || k <= 0 || epr <= 0 || E <= 0 || rank < 0 || cap_slots <= 0)
+                         const uint64_t* peer_meta, const uint64_t* peer_weight, int32_t* err, int local_lo,
+                         int local_hi, int max_sms, pm_stream_t stream) {
+    if (T < 0 || H <= 0 || H % 128 != 0 || k <= 0 || epr <= 0 || E <= 0 || rank < 0 || cap_slots <= 0 ||
+        local_lo < 0 || local_hi > epr || local_lo >= local_hi || max_sms < 0)
         return PM_ERR_INVALID;
     if ((long)T * k >= (1L << 24) || rank >= 128) return PM_ERR_TOO_LARGE;
     if (T == 0) return PM_OK;
@@ -964,9 +968,11 @@ int pm_ep_dispatch_quant(const void* x, int T, int H, int k, const int32_t* topk
     DeviceInfo d;
     const int st = current_device_info(&d);
     if (st != PM_OK) return st;
+    // max_sms: one 1024-thread CTA per SM left free beside a GEMM; 0: the whole GPU
+    const int ctas = max_sms > 0 && max_sms < d.sms ? max_sms : 0;
     return cuda_status(launch_ep_dispatch_quant(x, T, H, k, topk_ids, topk_w, slot_local, expert_off_local, base, E,
                                                 epr, rank, cap_slots, peer_a1, peer_a1_scale, peer_meta, peer_weight,
-                                                err, d.sms, (cudaStream_t)stream));
+                                                err, d.sms, local_lo, local_hi, ctas, (cudaStream_t)stream));
 }
 
 int pm_ep_local_rows(const int32_t* meta, const int32_t* num_post_pad, int cap_slots, int H, int G, int n_pairs,
@@ -978,6 +984,30 @@ int pm_ep_local_rows(const int32_t* meta, const int32_t* num_post_pad, int cap_s
     if (st != PM_OK) return st;
     return cuda_status(launch_ep_local_rows(meta, num_post_pad, cap_slots, H, G, n_pairs, peer_back, dst_rows, err,
                                             d.sms, (cudaStream_t)stream));
+}
+
+int pm_ep_gemm1_fp8(const uint8_t* a_q, const float* a_s, const uint8_t* w1, const float* w1_s,
+                    const int32_t* expert_ids, const int32_t* bounds, int group, int cap_slots, int H, int I, int E,
+                    uint8_t* out_q, float* out_s, int32_t* err, int max_sms, pm_stream_t stream) {
+    int st = check_dims(1, H, I, E, 1);
+    if (st != PM_OK) return st;
+    if (cap_slots <= 0 || cap_slots % kBlockM != 0 || group < 0 || max_sms < 0) return PM_ERR_SHAPE;
+    if (!a_q || !a_s || !w1 || !w1_s || !expert_ids || !bounds || !out_q || !out_s) return PM_ERR_INVALID;
+    if (!a16(a_q) || !a16(w1) || !a16(out_q)) return PM_ERR_ALIGN;
+    DeviceInfo d;
+    st = current_device_info(&d);
+    if (st != PM_OK) return st;
+    CUtensorMap ta, tb;
+    if (!encode_tmap_2d_u8(&ta, a_q, (uint64_t)H, (uint64_t)cap_slots, (uint64_t)H, 128, 128) ||
+        !encode_tmap_2d_u8(&tb, w1, (uint64_t)H, (uint64_t)E * 2 * I, (uint64_t)H, 128, 128))
+        return PM_ERR_CUDA;
+    // slots [bounds[group], bounds[group + 1]): the GEMM starts at the first and ends at the second
+    GemmArgs g = gemm_args_common(a_s, w1_s, expert_ids, bounds + group + 1, 2 * I, H, I / 128, cap_slots, I, err);
+    g.slot_lo = bounds + group;
+    g.out_q = out_q;
+    g.out_s = out_s;
+    const int sms = max_sms > 0 && max_sms < d.sms ? max_sms : d.sms;
+    return cuda_status(launch_gemm_fp8(0, ta, tb, g, sms, (cudaStream_t)stream));
 }
 
 int pm_ep_gemm2_fp8(const uint8_t* a_q, const float* a_s, const uint8_t* w2, const float* w2_s,

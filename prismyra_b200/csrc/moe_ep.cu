@@ -67,11 +67,14 @@ __global__ void ep_barrier_kernel(const uint64_t* __restrict__ peer_flag, unsign
 
 // ---------------------------------------------------------------------------------------------- offsets
 // cm [G][E] counts; own bases base[e] for every global expert; block table / slot count of this rank's experts.
+// bounds (may be null): with `groups` groups of epr / groups local experts each, bounds[g] = the first slot of group
+// g's experts and bounds[groups] = the slot count (a group's tiles can then run while a later group is dispatched).
 __global__ void __launch_bounds__(kMaxExperts) ep_offsets_kernel(const int32_t* __restrict__ cm, int G, int E,
                                                                  int epr, int rank, int32_t* __restrict__ base,
                                                                  int32_t* __restrict__ expert_ids,
                                                                  int32_t* __restrict__ npp, int cap_blocks,
-                                                                 int32_t* err) {
+                                                                 int32_t* err, int32_t* __restrict__ bounds,
+                                                                 int groups) {
     pdl_wait();
     pdl_trigger();
     __shared__ int padded[kMaxExperts];
@@ -97,7 +100,11 @@ __global__ void __launch_bounds__(kMaxExperts) ep_offsets_kernel(const int32_t* 
             if (b < cap_blocks) expert_ids[b] = el;
             else atomicExch(err, 1);
         }
-        if (el == epr - 1) *npp = off + padded[e];
+        if (bounds != nullptr && el % (epr / groups) == 0) bounds[el / (epr / groups)] = off;
+        if (el == epr - 1) {
+            *npp = off + padded[e];
+            if (bounds != nullptr) bounds[groups] = off + padded[e];
+        }
     }
 }
 
@@ -111,69 +118,109 @@ struct PeerPtrs {
     const uint64_t* wgt;   // [G] f32 [cap]
 };
 
-__global__ void __launch_bounds__(256) ep_dispatch_quant_kernel(
-    const __nv_bfloat16* __restrict__ x, int T, int H, int k, const int32_t* __restrict__ ids,
-    const float* __restrict__ topk_w, const int32_t* __restrict__ slot_local, const int32_t* __restrict__ off_local,
-    const int32_t* __restrict__ base, int E, int epr, int rank, int cap, PeerPtrs peers, int32_t* err) {
-    pdl_wait();
-    pdl_trigger();
+// One (token, 128-column group) item per half-warp: a lane's 8 columns, the group's amax over the half-warp, the
+// quantised row stored to the owners' slots of the pairs in [le_lo, le_hi).  ILP items per lane are loaded before
+// any is processed (a launch on few SMs keeps that many loads in flight per warp).
+template <int ILP>
+__device__ __forceinline__ void ep_dispatch_items(const __nv_bfloat16* __restrict__ x, int T, int H, int k,
+                                                  const int32_t* __restrict__ ids, const float* __restrict__ topk_w,
+                                                  const int32_t* __restrict__ slot_local,
+                                                  const int32_t* __restrict__ off_local,
+                                                  const int32_t* __restrict__ base, int E, int epr, int rank,
+                                                  int cap, const PeerPtrs& peers, int32_t* err, int le_lo, int le_hi) {
     const int lane = threadIdx.x & 31, sub = lane & 15;
     const int G128 = H / 128;
     const long items = (long)T * G128;
     const long pairs = (items + 1) / 2;
     const long nwarps = ((long)gridDim.x * blockDim.x) >> 5;
-    for (long wp = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; wp < pairs; wp += nwarps) {
-        const long item = 2 * wp + (lane >> 4);
-        const bool valid = item < items;
-        const long t = valid ? item / G128 : 0;
-        const int g = valid ? (int)(item % G128) : 0;
-        const int col = g * 128 + sub * 8;
-        float v[8];
-        float amax = 0.0f;
-        if (valid) {
-            const uint4 w = *reinterpret_cast<const uint4*>(x + t * H + col);
-            const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&w);
+    for (long wp0 = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; wp0 < pairs; wp0 += nwarps * ILP) {
+        uint4 raw[ILP];
+#pragma unroll
+        for (int u = 0; u < ILP; ++u) {
+            const long item = 2 * (wp0 + u * nwarps) + (lane >> 4);
+            raw[u] = make_uint4(0, 0, 0, 0);
+            if (wp0 + u * nwarps < pairs && item < items)
+                raw[u] = *reinterpret_cast<const uint4*>(x + (item / G128) * H + (int)(item % G128) * 128 + sub * 8);
+        }
+#pragma unroll
+        for (int u = 0; u < ILP; ++u) {
+            const long wp = wp0 + u * nwarps;
+            const long item = 2 * wp + (lane >> 4);
+            const bool valid = wp < pairs && item < items;
+            const long t = valid ? item / G128 : 0;
+            const int g = valid ? (int)(item % G128) : 0;
+            const int col = g * 128 + sub * 8;
+            float v[8];
+            float amax = 0.0f;
+            const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw[u]);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 v[i] = __bfloat162float(b[i]);
                 amax = fmaxf(amax, fabsf(v[i]));
             }
-        }
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        if (!valid) continue;
-        const float sc = e4m3_group_scale(amax, kScaleDiv);
-        uint32_t packed[2];
+            for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            // (an invalid half-warp item goes through the shuffles below with every destination skipped)
+            const float sc = e4m3_group_scale(amax, kScaleDiv);
+            uint32_t packed[2];
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const float q0 = fminf(fmaxf(__fdiv_rn(v[4 * i + 0], sc), -448.0f), 448.0f);
-            const float q1 = fminf(fmaxf(__fdiv_rn(v[4 * i + 1], sc), -448.0f), 448.0f);
-            const float q2 = fminf(fmaxf(__fdiv_rn(v[4 * i + 2], sc), -448.0f), 448.0f);
-            const float q3 = fminf(fmaxf(__fdiv_rn(v[4 * i + 3], sc), -448.0f), 448.0f);
-            packed[i] = (uint32_t)e4m3x2(q0, q1) | ((uint32_t)e4m3x2(q2, q3) << 16);
-        }
-        for (int j = 0; j < k; ++j) {
-            const long p = t * k + j;
-            const int e = ids[p];
-            if (e < 0 || e >= E) {
-                atomicExch(err, 1);
-                continue;
+            for (int i = 0; i < 2; ++i) {
+                const float q0 = fminf(fmaxf(__fdiv_rn(v[4 * i + 0], sc), -448.0f), 448.0f);
+                const float q1 = fminf(fmaxf(__fdiv_rn(v[4 * i + 1], sc), -448.0f), 448.0f);
+                const float q2 = fminf(fmaxf(__fdiv_rn(v[4 * i + 2], sc), -448.0f), 448.0f);
+                const float q3 = fminf(fmaxf(__fdiv_rn(v[4 * i + 3], sc), -448.0f), 448.0f);
+                packed[i] = (uint32_t)e4m3x2(q0, q1) | ((uint32_t)e4m3x2(q2, q3) << 16);
             }
-            const int d = e / epr;
-            const int slot = base[e] + (slot_local[p] - off_local[e]);
-            if (slot < 0 || slot >= cap) {
-                atomicExch(err, 1);
-                continue;
+            // lane j of the half-warp resolves pair j's owner and slot (-1: skipped), all k at once
+            int my_d = -1, my_slot = -1;
+            float my_w = 0.0f;
+            if (valid && sub < k) {
+                const long p = t * k + sub;
+                const int e = ids[p];
+                if (e < 0 || e >= E) {
+                    atomicExch(err, 1);
+                } else {
+                    const int d = e / epr;
+                    if (e - d * epr >= le_lo && e - d * epr < le_hi) {  // else another group's pair
+                        const int slot = base[e] + (slot_local[p] - off_local[e]);
+                        if (slot < 0 || slot >= cap) {
+                            atomicExch(err, 1);
+                        } else {
+                            my_d = d;
+                            my_slot = slot;
+                            my_w = topk_w[p];
+                        }
+                    }
+                }
             }
-            uint8_t* a1 = reinterpret_cast<uint8_t*>(peers.a1[d]);
-            *reinterpret_cast<uint2*>(a1 + (size_t)slot * H + col) = make_uint2(packed[0], packed[1]);
-            if (sub == 0) reinterpret_cast<float*>(peers.a1s[d])[(size_t)slot * G128 + g] = sc;
-            if (sub == 0 && g == 0) {
-                reinterpret_cast<int32_t*>(peers.meta[d])[slot] = (rank << 24) | (int)p;
-                reinterpret_cast<float*>(peers.wgt[d])[slot] = topk_w[p];
+            for (int j = 0; j < k; ++j) {
+                const long p = t * k + j;
+                const int d = __shfl_sync(0xffffffffu, my_d, j, 16);
+                const int slot = __shfl_sync(0xffffffffu, my_slot, j, 16);
+                const float wj = __shfl_sync(0xffffffffu, my_w, j, 16);
+                if (slot < 0) continue;
+                uint8_t* a1 = reinterpret_cast<uint8_t*>(peers.a1[d]);
+                *reinterpret_cast<uint2*>(a1 + (size_t)slot * H + col) = make_uint2(packed[0], packed[1]);
+                if (sub == 0) reinterpret_cast<float*>(peers.a1s[d])[(size_t)slot * G128 + g] = sc;
+                if (sub == 0 && g == 0) {
+                    reinterpret_cast<int32_t*>(peers.meta[d])[slot] = (rank << 24) | (int)p;
+                    reinterpret_cast<float*>(peers.wgt[d])[slot] = wj;
+                }
             }
         }
     }
+}
+
+template <int ILP>
+__global__ void __launch_bounds__(1024) ep_dispatch_quant_kernel(
+    const __nv_bfloat16* __restrict__ x, int T, int H, int k, const int32_t* __restrict__ ids,
+    const float* __restrict__ topk_w, const int32_t* __restrict__ slot_local, const int32_t* __restrict__ off_local,
+    const int32_t* __restrict__ base, int E, int epr, int rank, int cap, PeerPtrs peers, int32_t* err, int le_lo,
+    int le_hi) {
+    pdl_wait();
+    pdl_trigger();
+    ep_dispatch_items<ILP>(x, T, H, k, ids, topk_w, slot_local, off_local, base, E, epr, rank, cap, peers, err, le_lo,
+                           le_hi);
 }
 
 // ---------------------------------------------------------------------------------------------- local rows
@@ -221,10 +268,12 @@ cudaError_t launch_ep_barrier(const uint64_t* peer_flag, unsigned* own_flag, int
 }
 
 cudaError_t launch_ep_offsets(const int32_t* cm, int G, int E, int epr, int rank, int32_t* base, int32_t* expert_ids,
-                              int32_t* npp, int cap_blocks, int32_t* err, cudaStream_t s) {
+                              int32_t* npp, int cap_blocks, int32_t* err, int32_t* bounds, int groups,
+                              cudaStream_t s) {
     if (E > kMaxExperts) return cudaErrorInvalidValue;
+    if (bounds != nullptr && (groups < 1 || epr % groups != 0)) return cudaErrorInvalidValue;
     PM_TRY(launch_pdl(ep_offsets_kernel, dim3(1), dim3(kMaxExperts), 0, s, cm, G, E, epr, rank, base, expert_ids,
-                      npp, cap_blocks, err));
+                      npp, cap_blocks, err, bounds, groups));
     return cudaGetLastError();
 }
 
@@ -232,13 +281,18 @@ cudaError_t launch_ep_dispatch_quant(const void* x, int T, int H, int k, const i
                                      const int32_t* slot_local, const int32_t* off_local, const int32_t* base,
                                      int E, int epr, int rank, int cap, const uint64_t* peer_a1, const uint64_t* peer_a1s,
                                      const uint64_t* peer_meta, const uint64_t* peer_wgt, int32_t* err, int sms,
-                                     cudaStream_t s) {
+                                     int le_lo, int le_hi, int ctas, cudaStream_t s) {
     if (T == 0) return cudaSuccess;
     PeerPtrs p{peer_a1, peer_a1s, peer_meta, peer_wgt};
     const long pairs = ((long)T * (H / 128) + 1) / 2;
-    PM_TRY(launch_pdl(ep_dispatch_quant_kernel, dim3(grid_for(pairs, 8, sms * 2)), dim3(256), 0, s,
-                      static_cast<const __nv_bfloat16*>(x), T, H, k, ids, topk_w, slot_local, off_local, base, E,
-                      epr, rank, cap, p, err));
+    if (ctas > 0)  // a few wide CTAs (one per SM left free beside a GEMM), four items in flight per warp
+        PM_TRY(launch_pdl(ep_dispatch_quant_kernel<4>, dim3(ctas), dim3(1024), 0, s,
+                          static_cast<const __nv_bfloat16*>(x), T, H, k, ids, topk_w, slot_local, off_local, base, E,
+                          epr, rank, cap, p, err, le_lo, le_hi));
+    else
+        PM_TRY(launch_pdl(ep_dispatch_quant_kernel<1>, dim3(grid_for(pairs, 8, sms * 2)), dim3(256), 0, s,
+                          static_cast<const __nv_bfloat16*>(x), T, H, k, ids, topk_w, slot_local, off_local, base, E,
+                          epr, rank, cap, p, err, le_lo, le_hi));
     return cudaGetLastError();
 }
 

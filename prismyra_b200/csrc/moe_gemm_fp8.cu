@@ -170,7 +170,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_trigger();
 
     const int KB = args.K / kBK;
-    const int num_tiles = (*args.num_post_pad / kBM) * args.n_tiles;
+    const int mb0 = args.slot_lo != nullptr ? *args.slot_lo / kBM : 0;  // first block of this launch
+    const int num_tiles = (*args.num_post_pad / kBM - mb0) * args.n_tiles;
 
     if (warp < kEpiWarp0) {
       asm volatile("setmaxnreg.dec.sync.aligned.u32 64;" ::: "memory");
@@ -180,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t phase = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-            const int mb = tile / args.n_tiles, nt = tile % args.n_tiles;
+            const int mb = mb0 + tile / args.n_tiles, nt = tile % args.n_tiles;
             const int e = args.expert_ids[mb];
             const int row0 = e * args.n_total + (MODE == 0 ? nt * 128 : nt * kBN);
             const int row1 = (MODE == 0) ? e * args.n_total + args.inter + nt * 128 : row0 + 128;
@@ -250,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t chunk = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-            const int mb = tile / args.n_tiles, nt = tile % args.n_tiles;
+            const int mb = mb0 + tile / args.n_tiles, nt = tile % args.n_tiles;
             const int e = args.expert_ids[mb];
             const float* bs = args.b_scale + (size_t)e * nb_total * KB;
             const float* brow0 = bs + (size_t)(MODE == 0 ? nt : nt * 2) * KB;
@@ -299,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int local = 0;
         float acc[128];
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-            const int mb = tile / args.n_tiles, nt = tile % args.n_tiles;
+            const int mb = mb0 + tile / args.n_tiles, nt = tile % args.n_tiles;
             const int grow = mb * kBM + row;
             // down: the row's flat index (the slot itself when there is no row map), its routing weight and, with a
             // destination table, the address its weighted row is stored to (0: the slot holds no row)

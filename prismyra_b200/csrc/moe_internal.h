@@ -117,6 +117,7 @@ struct GemmArgs {
     int round_first;          // down epilogue: bf16(bf16(acc) * w) instead of bf16(acc * w) (a bf16 product)
     int scale_rule;           // gate_up epilogue: how requantisation scales are formed (e4m3_group_scale)
     int* err;                 // set to 1 when a wait timed out
+    const int32_t* slot_lo;   // optional (null: 0): the launch covers slots [*slot_lo, *num_post_pad) only
 };
 
 cudaError_t launch_gemm_fp8(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, const GemmArgs& args,
@@ -203,12 +204,13 @@ cudaError_t launch_ep_count(const int32_t* ids, int n, int E, int G, int rank, c
 cudaError_t launch_ep_barrier(const uint64_t* peer_flag, unsigned* own_flag, int G, unsigned target, int32_t* err,
                               uint64_t limit_ns, cudaStream_t s);
 cudaError_t launch_ep_offsets(const int32_t* cm, int G, int E, int epr, int rank, int32_t* base, int32_t* expert_ids,
-                              int32_t* npp, int cap_blocks, int32_t* err, cudaStream_t s);
+                              int32_t* npp, int cap_blocks, int32_t* err, int32_t* bounds, int groups,
+                              cudaStream_t s);
 cudaError_t launch_ep_dispatch_quant(const void* x, int T, int H, int k, const int32_t* ids, const float* topk_w,
                                      const int32_t* slot_local, const int32_t* off_local, const int32_t* base,
                                      int E, int epr, int rank, int cap, const uint64_t* peer_a1,
                                      const uint64_t* peer_a1s, const uint64_t* peer_meta, const uint64_t* peer_wgt,
-                                     int32_t* err, int sms, cudaStream_t s);
+                                     int32_t* err, int sms, int le_lo, int le_hi, int ctas, cudaStream_t s);
 cudaError_t launch_ep_local_rows(const int32_t* meta, const int32_t* npp, int cap, int H, int G, int n_pairs,
                                  const uint64_t* peer_back, uint64_t* dst_rows, int32_t* err, int sms,
                                  cudaStream_t s);

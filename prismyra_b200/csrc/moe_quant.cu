@@ -9,8 +9,9 @@ namespace {
 
 // One half-warp per (token, 128-column group), two groups per warp: each lane converts 8 columns, the group's amax
 // is a half-warp reduction, and every copy of the group is one coalesced 128-byte segment (so small token counts
-// still spread over the whole GPU).  s = max(amax, 1e-10) * (1/448); q = e4m3(clamp(x / s, -448, 448)) with an
-// IEEE division, exactly as the reference's Triton kernel states it.  With slot_of the row is written to the
+// still spread over the whole GPU).  s = e4m3_group_scale(amax, scale_rule) (ptx.cuh: by default the correctly
+// rounded max(amax, 1e-10) / 448 of vLLM's compiled quantiser); q = e4m3(clamp(x / s, -448, 448)) with an IEEE
+// division.  With slot_of the row is written to the
 // token's k slots (its expert-ordered copies for the gate_up GEMM; vLLM reads the same rows through
 // sorted_ids // top_k); the padding slots are left unwritten -- their GEMM rows are computed and discarded, never
 // stored.  Without slot_of the single copy goes to row t.
@@ -33,7 +34,7 @@ __global__ void __launch_bounds__(256) quant_fp8_kernel(const __nv_bfloat16* __r
         const bool valid = item < items;
         const long row = valid ? item / G : 0;
         const int col = valid ? (int)(item % G) * 128 + sub * 8 : 0;
-        float v[8];
+        float v[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
         float amax = 0.0f;
         if (valid) {
             const uint4 w = *reinterpret_cast<const uint4*>(x + row * H + col);

@@ -179,6 +179,9 @@ def _view(ptr: int, nbytes: int, dev: torch.device) -> torch.Tensor:
     return torch.as_tensor(_DeviceMemory(ptr, nbytes), device=dev)
 
 
+kMaxGroups = 4  # expert groups of the overlapped dispatch (one barrier counter each in the flag region)
+
+
 def _align256(n: int) -> int:
     return (n + 255) // 256 * 256
 
@@ -251,18 +254,24 @@ class PeerExchange:
         self.eids = torch.zeros(cap // 128, dtype=torch.int32, device=device)
         self.npp = torch.zeros(1, dtype=torch.int32, device=device)
         self.err = torch.zeros(4, dtype=torch.int32, device=device)
-        self.epoch = 0
+        self.bounds = torch.zeros(kMaxGroups + 1, dtype=torch.int32, device=device)
+        self.sms = torch.cuda.get_device_properties(device).multi_processor_count
+        # four barrier counters, 64 bytes apart in the flag region: one per stream of barriers that may run at once
+        self.peer_flag = [self.peer["flag"] + 64 * c for c in range(kMaxGroups)]
+        self.epochs = [0] * kMaxGroups
         torch.cuda.synchronize(device)
         dist.barrier(group=group)  # every rank has mapped every region
 
-    def barrier(self, stream: int, wait_limit_ns: int = 0) -> None:
+    def barrier(self, stream: int, wait_limit_ns: int = 0, counter: int = 0) -> None:
         """Device barrier over the ranks (stream-ordered; the wait gives up after ``wait_limit_ns``, 0 = the
-        library's 2 s, and then sets the error word)."""
+        library's 2 s, and then sets the error word).  Barriers on one counter pair up by count across the ranks;
+        barriers that may run at the same time (on different streams) use different counters."""
         from . import _lib
 
-        self.epoch += 1
-        _lib.call("pm_ep_barrier", self.peer["flag"].data_ptr(), self.flag.data_ptr(), self.world,
-                  (self.epoch * self.world) & 0xFFFFFFFF, self.err.data_ptr(), wait_limit_ns, stream)
+        self.epochs[counter] += 1
+        _lib.call("pm_ep_barrier", self.peer_flag[counter].data_ptr(), self.flag.data_ptr() + 64 * counter,
+                  self.world, (self.epochs[counter] * self.world) & 0xFFFFFFFF, self.err.data_ptr(), wait_limit_ns,
+                  stream)
 
     def errors(self) -> int:
         """Non-zero if any kernel gave up on a bounded wait or met an out-of-range slot (synchronises)."""
@@ -294,7 +303,20 @@ class PeerExpertParallelLayer:
     its own, released by ``close()``."""
 
     def __init__(self, backend: CudaBackend, num_experts: int, top_k: int, rank: int, world: int,
-                 max_tokens: int = 0, group=None, exchange: PeerExchange | None = None):
+                 max_tokens: int = 0, group=None, exchange: PeerExchange | None = None, groups: int | None = None,
+                 reserve_sms: int = 16):
+        """``groups`` (1-4, dividing the experts per rank): the owners' experts are dispatched in that many groups;
+        group g + 1 is dispatched and its barrier passed on a side stream, on ``reserve_sms`` SMs, while the
+        gate_up GEMM of group g runs on the others.  1 (the default): one dispatch, then the GEMMs.  Measured on two
+        B200s the grouped form is slower: a dispatch kernel confined to a few SMs cannot keep its stores in flight,
+        and one spread over the GPU holds the SMs the GEMM needs."""
+        epr = num_experts // world
+        if groups is None:
+            groups = 1
+        if not 1 <= groups <= kMaxGroups or epr % groups:
+            raise ValueError(f"groups must be 1..{kMaxGroups} and divide the {epr} experts per rank")
+        self.groups, self.reserve_sms = groups, reserve_sms
+        self._side = None
         self.b, self.E, self.k, self.rank, self.world = backend, num_experts, top_k, rank, world
         _, I2, H = backend.w1.shape
         self._own_exchange = exchange is None
@@ -331,16 +353,47 @@ class PeerExpertParallelLayer:
         _lib.call("pm_ep_count", P(ids), T * k, E, G, self.rank, P(X.peer["cm"]), stream)
         X.barrier(stream)
         mark()
-        _lib.call("pm_ep_offsets", P(X.cm), G, E, X.epr, self.rank, P(X.base), P(X.eids), P(X.npp), X.cap,
-                  P(X.err), stream)
-        _lib.call("pm_ep_dispatch_quant", P(x), T, H, k, P(ids), P(w), P(slot_of), P(off), P(X.base), E, X.epr,
-                  self.rank, X.cap, P(X.peer["a1"]), P(X.peer["a1s"]), P(X.peer["meta"]), P(X.peer["wgt"]),
-                  P(X.err), stream)
+        ng, epr = self.groups, X.epr
+        _lib.call("pm_ep_offsets", P(X.cm), G, E, epr, self.rank, P(X.base), P(X.eids), P(X.npp), X.cap,
+                  P(X.err), P(X.bounds), ng, stream)
+
+        def dispatch(g, s_, max_sms):
+            lo, hi = g * epr // ng, (g + 1) * epr // ng
+            _lib.call("pm_ep_dispatch_quant", P(x), T, H, k, P(ids), P(w), P(slot_of), P(off), P(X.base), E, epr,
+                      self.rank, X.cap, P(X.peer["a1"]), P(X.peer["a1s"]), P(X.peer["meta"]), P(X.peer["wgt"]),
+                      P(X.err), lo, hi, max_sms, s_)
+
+        def gate_up(g, max_sms):
+            _lib.call("pm_ep_gemm1_fp8", P(X.a1), P(X.a1s), P(ops._u8(self.b.w1)), P(self.b.w1_s), P(X.eids),
+                      P(X.bounds), g, X.cap, H, X.I, self.b.w1.shape[0], P(X.a2), P(X.a2s), P(X.err[1:2]), max_sms,
+                      stream)
+
+        dispatch(0, stream, 0)
+        done = []
+        if ng > 1:
+            # groups 1.. are dispatched on a side stream (on reserve_sms SMs) while group 0's gate_up runs
+            if self._side is None:
+                self._side = torch.cuda.Stream(X.dev)
+            side = self._side
+            ev = torch.cuda.Event()
+            ev.record()
+            side.wait_event(ev)
+            with torch.cuda.stream(side):
+                for g in range(1, ng):
+                    dispatch(g, side.cuda_stream, self.reserve_sms)
+                    X.barrier(side.cuda_stream, counter=g)
+                    d = torch.cuda.Event()
+                    d.record(side)
+                    done.append(d)
         X.barrier(stream)
         mark()
+        for g in range(ng):
+            if g > 0:
+                torch.cuda.current_stream(X.dev).wait_event(done[g - 1])
+            # while a later group is still being dispatched, leave reserve_sms SMs to its kernels
+            gate_up(g, X.sms - self.reserve_sms if (g < ng - 1 and 0 < self.reserve_sms < X.sms) else 0)
         _lib.call("pm_ep_local_rows", P(X.meta), P(X.npp), X.cap, H, G, X.max_tokens * k, P(X.peer["back"]),
                   P(X.dst_rows), P(X.err), stream)
-        ops.gemm1_fp8(X.a1, X.a1s, self.b.w1, self.b.w1_s, X.eids, X.npp, out=(X.a2, X.a2s, X.err[1:2]))
         mark()
         # the down GEMM stores each weighted row straight into its source rank's result row
         w2 = self.b.w2

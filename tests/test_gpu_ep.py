@@ -91,7 +91,7 @@ def test_two_nccl_ranks_match_the_single_gpu_layer():
         assert dict(errors) == {}
 
 
-def _peer_rank(rank, world, port, errors):
+def _peer_rank(rank, world, port, errors, groups):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -105,7 +105,7 @@ def _peer_rank(rank, world, port, errors):
         lo, hi = rank * epr, (rank + 1) * epr
         b = ep.CudaBackend(L["w1"][lo:hi].contiguous(), L["w1_s"][lo:hi].contiguous(), L["w2"][lo:hi].contiguous(),
                            L["w2_s"][lo:hi].contiguous(), L["router_w"], K)
-        layer = ep.PeerExpertParallelLayer(b, E, K, rank, world, max_tokens=T)
+        layer = ep.PeerExpertParallelLayer(b, E, K, rank, world, max_tokens=T, groups=groups)
         for call, (seed, n) in enumerate(((100 + rank, T), (200 + rank, T - 37))):  # buffers reused, fewer tokens
             g = torch.Generator("cuda").manual_seed(seed)
             x = torch.randn(n, H, generator=g, device=dev).to(torch.bfloat16)
@@ -123,16 +123,18 @@ def _peer_rank(rank, world, port, errors):
 
 
 @pytest.mark.skipif(not cuda_ok() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_ranks_over_peer_memory_match_the_single_gpu_layer():
+@pytest.mark.parametrize("groups", [1, 2, 4])
+def test_two_ranks_over_peer_memory_match_the_single_gpu_layer(groups):
     """The peer-memory expert-parallel layer (rows stored straight into the owners' slots and back over NVLink,
-    device barriers, no host synchronisation): bit-identical to one GPU, twice in a row on the same buffers."""
+    device barriers, no host synchronisation): bit-identical to one GPU, twice in a row on the same buffers; with
+    the experts dispatched in 1, 2 or 4 groups (later groups on a side stream beside the earlier groups' GEMMs)."""
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     with ctx.Manager() as mgr:
         errors = mgr.dict()
-        procs = [ctx.Process(target=_peer_rank, args=(r, 2, port, errors)) for r in range(2)]
+        procs = [ctx.Process(target=_peer_rank, args=(r, 2, port, errors, groups)) for r in range(2)]
         for p in procs:
             p.start()
         for p in procs:
