@@ -284,7 +284,7 @@ static int small_gemm_fp8(int mode, const uint8_t* a_q, const float* a_s, const 
     g.n_valid = n_valid;
     g.n_total = n_total;
     g.K = K;
-    g.n_tiles = (mode == 0 ? I : H) / 128;
+    g.n_tiles = mode == 0 ? I / 128 : H / 256;  // down units are 256 hidden rows
     g.max_units = (max_slots / kBlockM) * g.n_tiles;
     g.inter = I;
     g.out_q = out_q;
@@ -331,7 +331,7 @@ static int small_fused_fp8(const uint8_t* a1, const float* a1s, const uint8_t* w
     g[1].b_scale = w2_s;
     g[1].n_total = H;
     g[1].K = I;
-    g[1].n_tiles = H / 128;
+    g[1].n_tiles = H / 256;
     g[1].topk_w = topk_w;
     g[1].c3 = static_cast<__nv_bfloat16*>(c3);
     for (int m = 0; m < 2; ++m) g[m].max_units = (max_slots / kBlockM) * g[m].n_tiles;

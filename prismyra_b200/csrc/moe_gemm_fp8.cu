@@ -356,21 +356,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
 
             if (MODE == 0) {
-                // bf16(gate), bf16(up) -> silu(gate) * up in bf16 -> e4m3 with one scale per 128 columns.
-                // Pairs share each rounding instruction (the conversion pipe, not the FMA pipe, bounds this loop).
-                float amax = 0.0f;
+                // bf16(gate), bf16(up) -> silu(gate) * up in bf16 -> e4m3 with one scale per 128 columns, a
+                // pair of columns per instruction.  The loop is bound by its instruction count, so up, silu(gate)
+                // and their product stay packed bf16: the product of two bf16 values is exact in fp32, so one
+                // correctly rounded bf16 multiply gives the same bits as the fp32 product rounded to bf16, and the
+                // row maximum of |y| is taken on the packed values.
+                __nv_bfloat162 amax2 = __float2bfloat162_rn(0.0f);
 #pragma unroll
                 for (int c = 0; c < 64; c += 2) {
-                    const float2 g = bf16x2_round(acc[c], acc[c + 1]);
-                    const float2 u = bf16x2_round(acc[64 + c], acc[64 + c + 1]);
-                    const float2 s2 = silu2(g);
-                    const float2 sg = bf16x2_round(s2.x, s2.y);
-                    const float2 p2 = __fmul2_rn(sg, u);
-                    const float2 y = bf16x2_round(p2.x, p2.y);
+                    const __nv_bfloat162 gb = __floats2bfloat162_rn(acc[c], acc[c + 1]);
+                    const __nv_bfloat162 ub = __floats2bfloat162_rn(acc[64 + c], acc[64 + c + 1]);
+                    const float2 s2 = silu2(__bfloat1622float2(gb));
+                    const __nv_bfloat162 yb = __hmul2(__floats2bfloat162_rn(s2.x, s2.y), ub);
+                    amax2 = __hmax2(amax2, __habs2(yb));
+                    const float2 y = __bfloat1622float2(yb);
                     acc[c] = y.x;
                     acc[c + 1] = y.y;
-                    amax = fmaxf(amax, fmaxf(fabsf(y.x), fabsf(y.y)));
                 }
+                float amax = fmaxf(__low2float(amax2), __high2float(amax2));
                 // The other column half of this row lives in another warp: exchange the half maxima through
                 // shared memory, synchronised by an mbarrier (a bounded wait, unlike a named barrier).
                 tail->amax_x[local & 1][half][row] = amax;

@@ -16,13 +16,14 @@
 //   mode 0 (gate_up): gate rows nt*128.. and up rows I + nt*128.. of expert e: two MMAs per K step into two TMEM
 //          accumulators; epilogue bf16 -> silu(gate)*up -> bf16 -> e4m3 with one scale per token over the unit's
 //          128 output columns (exactly one requantisation group), written to the down GEMM's A operand.
-//   mode 1 (down): hidden rows nt*128.. of expert e; epilogue multiplies by the token's routing weight in fp32,
-//          rounds to bf16 and writes c3[flat index, nt*128 ..].
+//   mode 1 (down): hidden rows nt*256.. and nt*256+128.. of expert e, as two tiles and two accumulators like
+//          gate_up (a unit twice as large as one tile halves its fixed costs per byte); epilogue multiplies by the
+//          token's routing weight in fp32, rounds to bf16 and writes c3[flat index, nt*256 ..].
 // Warp roles (384 threads): warp 0 TMA (weight tiles, token tiles, and per unit the block's activation scales as
 // one bulk copy), warp 1 TMEM + MMA, warps 4-11 promotion and epilogue: warp w reads TMEM lanes 32*(w%4).. (weight
-// rows) and token columns of half (w-4)/4 of the unit.  TMEM is a ring of eight 64-column slots: a down K block
-// takes one, a gate_up K block one (gate at +0, up at +32) when the half holds one token sub-block and two (gate,
-// up) when it holds two; the MMA thus runs up to eight K blocks ahead of the promotion, through a unit's epilogue.
+// rows) and token columns of half (w-4)/4 of the unit.  TMEM is a ring of eight 64-column slots: a K block takes
+// one (first tile at +0, second at +32) when the half holds one token sub-block and two when it holds two; the MMA
+// thus runs up to eight K blocks ahead of the promotion, through a unit's epilogue.
 // An M=128 FP8 MMA with N <= 128 costs ~107 cycles in a chain on one accumulator whatever N is, but ~196 when
 // consecutive instructions alternate between two accumulators (~143 over four): the MMA thread issues each
 // accumulator's four K steps back to back (gate, then up).  setmaxnreg gives warpgroup 0 64 registers and the
@@ -48,12 +49,14 @@ constexpr int kSlots = 8;            // TMEM slots of kSlotCols columns
 constexpr uint32_t kSlotCols = 64;
 constexpr int kQueue = 4;            // units handed from the producer to the MMA and promotion warps
 constexpr int kMaxBlocks = 512;      // 128-slot blocks a launch may have (the few-token regime has far fewer)
-// Stage bytes: two weight tiles (gate, up) or one (down), and up to 64 token rows.
-template <int MODE> __host__ __device__ constexpr int stage_bytes() {
-    return (MODE == 1 ? 1 : 2) * kWBytes + kTokBytes;
-}
-// TMEM slots one K block of a unit with nsub token sub-blocks takes (m: 0 gate_up, 1 down).
-__device__ __forceinline__ int slots_per_kblock(int m, int nsub) { return m == 0 ? nsub : 1; }
+// Stage bytes: a unit's two weight tiles (gate and up rows; down: two consecutive 128-row tiles) and up to 64
+// token rows.
+template <int MODE> __host__ __device__ constexpr int stage_bytes() { return 2 * kWBytes + kTokBytes; }
+// TMEM slots one K block of a unit with nsub token sub-blocks takes: its two accumulators share a 64-column slot
+// (at +0 and +32) for one sub-block, or take one slot each for two.
+__device__ __forceinline__ int slots_per_kblock(int nsub) { return nsub; }
+// First weight row of a unit's second tile, relative to its first: the up rows (gate_up), or the next 128 rows.
+__device__ __forceinline__ int second_tile_rows(int m, int inter) { return m == 0 ? inter : 128; }
 
 // Per-unit values the promotion warps need, loaded ahead by warp 2: the unit's two weight-scale rows (gate and up;
 // down: one) and, for a down unit, the flat index and routing weight of each of the half's 64 slots.
@@ -158,7 +161,7 @@ __device__ __forceinline__ bool run_unit(const SmallGemmArgs& a, SmallTail* tail
     constexpr int C = 16 * NSUB;  // token columns of this thread
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = warp & 3, half = (warp - kEpiWarp0) >> 2;
-    const int r = q * 32 + lane;  // weight row of the unit (output column nt*128 + r)
+    const int r = q * 32 + lane;  // weight row of the unit's tiles (gate_up: output column nt*128 + r)
     const int KB = a.K / 128;
     const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
     const int col0 = half * C;                  // first token column of this thread within the unit
@@ -171,8 +174,8 @@ __device__ __forceinline__ bool run_unit(const SmallGemmArgs& a, SmallTail* tail
     if (!mbar_wait(smem_u32(&tail->ufull[par]), use & 1u, abort)) return false;
     const UnitRec& R = tail->urec[par];
     const float g0 = lane < KB ? R.bg[lane] : 0.0f, g1 = lane + 32 < KB ? R.bg[lane + 32] : 0.0f;
-    const float u0 = (MODE == 0 && lane < KB) ? R.bu[lane] : 0.0f;
-    const float u1 = (MODE == 0 && lane + 32 < KB) ? R.bu[lane + 32] : 0.0f;
+    const float u0 = lane < KB ? R.bu[lane] : 0.0f;
+    const float u1 = lane + 32 < KB ? R.bu[lane + 32] : 0.0f;
     int fl = 0;
     float wl = 0.0f;
     if (MODE == 1) {
@@ -180,11 +183,11 @@ __device__ __forceinline__ bool run_unit(const SmallGemmArgs& a, SmallTail* tail
         wl = lane < C ? R.wl[col0 + lane] : 0.0f;
     }
 
-    float accg[C], accu[MODE == 0 ? C : 1];
+    float accg[C], accu[C];  // the unit's first and second tile (gate and up)
 #pragma unroll
     for (int i = 0; i < C; ++i) accg[i] = 0.0f;
 #pragma unroll
-    for (int i = 0; i < (MODE == 0 ? C : 1); ++i) accu[i] = 0.0f;
+    for (int i = 0; i < C; ++i) accu[i] = 0.0f;
 
     if (!mbar_wait(smem_u32(&tail->safull[par]), use & 1u, abort)) return false;
     const float* sa = sa_tab + (size_t)par * 128 * kb_max + (size_t)row0 * KB;
@@ -193,26 +196,26 @@ __device__ __forceinline__ bool run_unit(const SmallGemmArgs& a, SmallTail* tail
         const uint32_t s0 = ring.it % kSlots, p0 = (ring.it / kSlots) & 1u;
         ++ring.it;
         uint32_t s1 = s0, p1 = p0;
-        if (MODE == 0 && NSUB == 2) {
+        if (NSUB == 2) {
             s1 = ring.it % kSlots;
             p1 = (ring.it / kSlots) & 1u;
             ++ring.it;
         }
         const float swg = __shfl_sync(0xffffffffu, kb < 32 ? g0 : g1, kb & 31);
-        const float swu = MODE == 0 ? __shfl_sync(0xffffffffu, kb < 32 ? u0 : u1, kb & 31) : 0.0f;
+        const float swu = __shfl_sync(0xffffffffu, kb < 32 ? u0 : u1, kb & 31);
         float sak[C];  // the token columns' activation scales (loaded before the TMEM wait)
 #pragma unroll
         for (int i = 0; i < C; ++i) sak[i] = sa[(size_t)i * KB + kb];
         if (!mbar_wait(smem_u32(&tail->tfull[s0]), p0, abort)) return false;
-        if (MODE == 0 && NSUB == 2 && !mbar_wait(smem_u32(&tail->tfull[s1]), p1, abort)) return false;
+        if (NSUB == 2 && !mbar_wait(smem_u32(&tail->tfull[s1]), p1, abort)) return false;
         tc_fence_after();
         const uint32_t tg = t_lane + s0 * kSlotCols + (uint32_t)col0;
         const uint32_t tu = NSUB == 1 ? tg + 32 : t_lane + s1 * kSlotCols + (uint32_t)col0;
-        uint32_t dg[NSUB][16], du[MODE == 0 ? NSUB : 1][16];
+        uint32_t dg[NSUB][16], du[NSUB][16];
 #pragma unroll
         for (int c = 0; c < NSUB; ++c) {
             tmem_ld16(tg + 16 * c, dg[c]);
-            if (MODE == 0) tmem_ld16(tu + 16 * c, du[c]);
+            tmem_ld16(tu + 16 * c, du[c]);
         }
         tmem_ld_wait();
         // the values are in registers: hand the slots back to the MMA before the FMAs
@@ -220,12 +223,12 @@ __device__ __forceinline__ bool run_unit(const SmallGemmArgs& a, SmallTail* tail
         __syncwarp();
         if (lane == 0) {
             mbar_arrive(smem_u32(&tail->tempty[s0]));
-            if (MODE == 0 && NSUB == 2) mbar_arrive(smem_u32(&tail->tempty[s1]));
+            if (NSUB == 2) mbar_arrive(smem_u32(&tail->tempty[s1]));
         }
 #pragma unroll
         for (int c = 0; c < NSUB; ++c) {
             fma16(dg[c], sak + 16 * c, swg, accg + 16 * c);
-            if (MODE == 0) fma16(du[MODE == 0 ? c : 0], sak + 16 * c, swu, accu + 16 * c);
+            fma16(du[c], sak + 16 * c, swu, accu + 16 * c);
         }
     }
     __syncwarp();
@@ -281,7 +284,10 @@ __device__ __forceinline__ bool run_unit(const SmallGemmArgs& a, SmallTail* tail
         for (int i = 0; i < C; ++i) {
             const int f = __shfl_sync(0xffffffffu, fl, i);
             const float w = __shfl_sync(0xffffffffu, wl, i);
-            if (f < a.n_valid) a.c3[(size_t)f * H + un.nt * 128 + r] = __float2bfloat16_rn(accg[i] * w);
+            if (f < a.n_valid) {
+                a.c3[(size_t)f * H + un.nt * 256 + r] = __float2bfloat16_rn(accg[i] * w);
+                a.c3[(size_t)f * H + un.nt * 256 + 128 + r] = __float2bfloat16_rn(accu[i] * w);
+            }
         }
     }
     __syncwarp();
@@ -449,16 +455,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bulk_copy_g2s(smem_u32(sa_tab) + par * (128 * kb_max * 4), A.a_scale + (size_t)cur.mb * 128 * KB,
                               sa_bytes, smem_u32(&tail->safull[par]));
                 ++sa_issued[par];
-                const int wrow = e * A.n_total + cur.nt * 128;
-                const uint32_t bytes = (uint32_t)((m == 0 ? 2 : 1) * kWBytes + nsub * 32 * 128);
+                const int wrow = e * A.n_total + cur.nt * (m == 0 ? 128 : 256);
+                const uint32_t bytes = (uint32_t)(2 * kWBytes + nsub * 32 * 128);
                 for (int kb = 0; kb < KB; ++kb) {
                     if (!mbar_wait(smem_u32(&tail->empty[stage]), phase ^ 1u, abort)) { ok = false; break; }
                     const uint32_t dst = sbase + stage * kStageBytes;
                     const uint32_t fb = smem_u32(&tail->full[stage]);
                     mbar_arrive_expect_tx(fb, bytes);
                     tma_load_2d(dst, tm_w, fb, kb * 128, wrow);
-                    if (m == 0) tma_load_2d(dst + kWBytes, tm_w, fb, kb * 128, wrow + A.inter);
-                    const uint32_t tok = dst + (m == 0 ? 2 : 1) * kWBytes;
+                    tma_load_2d(dst + kWBytes, tm_w, fb, kb * 128, wrow + second_tile_rows(m, A.inter));
+                    const uint32_t tok = dst + 2 * kWBytes;
                     for (int s = 0; s < nsub; ++s)
                         tma_load_2d(tok + s * 4096, tm_tok, fb, kb * 128, cur.mb * 128 + cur.hp * 64 + 32 * s);
                     if (++stage == stages) { stage = 0; phase ^= 1u; }
@@ -507,9 +513,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 UnitRec& R = tail->urec[par];
                 const int KB = A.K / 128, nb_total = A.n_total / 128;
                 const float* bs = A.b_scale + (size_t)e * nb_total * KB;
+                const int r0 = m == 0 ? un.nt : 2 * un.nt;  // the two tiles' 128-row scale blocks
+                const int r1 = r0 + second_tile_rows(m, A.inter) / 128;
                 for (int j = lane; j < KB; j += 32) {
-                    R.bg[j] = bs[(size_t)un.nt * KB + j];
-                    if (m == 0) R.bu[j] = bs[(size_t)(A.inter / 128 + un.nt) * KB + j];
+                    R.bg[j] = bs[(size_t)r0 * KB + j];
+                    R.bu[j] = bs[(size_t)r1 * KB + j];
                 }
                 if (m == 1) {
                     for (int j = lane; j < 64; j += 32) {
@@ -537,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int m = MODE == 2 ? ph : MODE;
                 const int nsub = ref.y & 7, KB = (ph ? a1.K : a0.K) / 128;
                 const uint32_t idesc = idesc_f32acc(0 /*e4m3*/, 0 /*e4m3*/, 128, 32u * (uint32_t)nsub);
-                const int spk = slots_per_kblock(m, nsub);
+                const int spk = slots_per_kblock(nsub);
                 for (int kb = 0; kb < KB && ok; ++kb) {
                     uint32_t sl[2] = {0, 0};
 #pragma unroll
@@ -554,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t base = sbase + stage * kStageBytes;
                     const uint64_t dwg = desc_kmajor_sw128(base);
                     const uint64_t dwu = desc_kmajor_sw128(base + kWBytes);
-                    const uint64_t dt = desc_kmajor_sw128(base + (m == 0 ? 2 : 1) * kWBytes);
+                    const uint64_t dt = desc_kmajor_sw128(base + 2 * kWBytes);
                     const uint32_t dg = tmem_base + sl[0] * kSlotCols;
                     const uint32_t du = spk == 1 ? dg + 32 : tmem_base + sl[1] * kSlotCols;
                     // each accumulator's four K steps back to back: a chain on one accumulator issues at ~107
@@ -562,11 +570,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int k = 0; k < 4; ++k)  // 32 e4m3 (32 bytes) of K per instruction
                         mma_f8f6f4(dg, dwg + 2 * k, dt + 2 * k, idesc, k > 0 ? 1u : 0u);
-                    if (m == 0) {
 #pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            mma_f8f6f4(du, dwu + 2 * k, dt + 2 * k, idesc, k > 0 ? 1u : 0u);
-                    }
+                    for (int k = 0; k < 4; ++k)
+                        mma_f8f6f4(du, dwu + 2 * k, dt + 2 * k, idesc, k > 0 ? 1u : 0u);
                     mma_commit(smem_u32(&tail->empty[stage]));
                     mma_commit(smem_u32(&tail->tfull[sl[0]]));
                     if (spk == 2) mma_commit(smem_u32(&tail->tfull[sl[1]]));
