@@ -48,11 +48,11 @@ enum pm_format { PM_FMT_FP8 = 0, PM_FMT_NVFP4 = 1 };
 
 /* Workspace regions, for callers that want to inspect intermediates (pm_moe_workspace_region). */
 enum pm_region {
-    PM_WS_STATUS = 0,   /* i32 [4]: [0] = timeout flag */
+    PM_WS_STATUS = 0,   /* i32 [4]: [0] = timeout flag, [2] = grid barrier of the few-token front end */
     PM_WS_LOGITS = 1,   /* bf16 [T, E] */
     PM_WS_TOPK_W = 2,   /* f32 [T, k] */
     PM_WS_TOPK_IDS = 3, /* i32 [T, k] */
-    PM_WS_COUNTS = 4,   /* i32 [chunks, E] */
+    PM_WS_COUNTS = 4,   /* i32 [chunks, E] (not written when 512 <= T*k <= 4096: one-launch front end) */
     PM_WS_EXPERT_OFF = 5, /* i32 [E + 1] first slot of each expert, padded total last */
     PM_WS_SORTED = 6,   /* i32 [max_slots] flat index t*k+j per slot, T*k = padding */
     PM_WS_EXPERT_IDS = 7, /* i32 [max_slots / 128] expert of each 128-slot block */

@@ -462,25 +462,42 @@ static int forward_fp8_impl(const void* x, const void* router_w, const void* log
     void* c3 = R(PM_WS_C3);
 
     if (clear_status && cudaMemsetAsync(status, 0, L.len[PM_WS_STATUS], s) != cudaSuccess) return PM_ERR_CUDA;
-    cudaError_t e;
-    if (logits != nullptr)
-        e = launch_topk(logits, bias, T, E, k, topk_w, topk_ids, s);
-    else
-        e = launch_router_topk(x, router_w, bias, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s,
-                               router_part);
-    if (e != cudaSuccess) return PM_ERR_CUDA;
     int32_t* slot_of = reinterpret_cast<int32_t*>(R(PM_WS_SLOT_OF));
-    e = launch_align(topk_ids, T * k, E, reinterpret_cast<int32_t*>(R(PM_WS_COUNTS)), sorted, expert_ids, npp,
-                     reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_OFF)), slot_of, s);
-    if (e != cudaSuccess) return PM_ERR_CUDA;
     // Both few-token GEMMs in one launch once most experts are hit (T*k >= 2E); with fewer pairs nearly every down
     // unit would wait for its block's few gate_up units, and two launches are faster.
     const bool fused = use_small_gemm((long)T * k, H, I, E) && (long)T * k >= 2L * E &&
                        gemm_fp8_small_fused_fits(H, I) && a16(a1s) && a16(a2s);
     int32_t* sched = reinterpret_cast<int32_t*>(R(PM_WS_SCHED));
-    e = launch_quant_fp8(x, T, H, k, slot_of, a1, a1s, s, scale_rule, fused ? sched : nullptr,
-                         fused ? small_sched_ints(L.max_slots / kBlockM) : 0);
-    if (e != cudaSuccess) return PM_ERR_CUDA;
+    int32_t* zero = fused ? sched : nullptr;
+    const int zero_n = fused ? small_sched_ints(L.max_slots / kBlockM) : 0;
+    cudaError_t e;
+    if ((long)T * k >= kFrontMinIndices && (long)T * k <= kFrontMaxIndices) {
+        // few tokens: the top-k, the alignment and the quantisation in one launch after the router projection
+        const bool split = logits == nullptr && router_part != nullptr && router_split_bytes(T, H, E) > 0;
+        if (logits == nullptr) {
+            e = launch_router_topk(x, router_w, bias, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s,
+                                   router_part, false);
+            if (e != cudaSuccess) return PM_ERR_CUDA;
+        }
+        const void* lg_in = split ? nullptr : (logits != nullptr ? logits : R(PM_WS_LOGITS));
+        e = launch_front_small(split ? router_part : nullptr, router_chunks(H), lg_in, R(PM_WS_LOGITS), bias, T, E,
+                               k, topk_w, topk_ids, sorted, expert_ids, npp,
+                               reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_OFF)), slot_of, x, H, a1, a1s, scale_rule,
+                               zero, zero_n, status + 2, status, s);
+        if (e != cudaSuccess) return PM_ERR_CUDA;
+    } else {
+        if (logits != nullptr)
+            e = launch_topk(logits, bias, T, E, k, topk_w, topk_ids, s);
+        else
+            e = launch_router_topk(x, router_w, bias, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s,
+                                   router_part);
+        if (e != cudaSuccess) return PM_ERR_CUDA;
+        e = launch_align(topk_ids, T * k, E, reinterpret_cast<int32_t*>(R(PM_WS_COUNTS)), sorted, expert_ids, npp,
+                         reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_OFF)), slot_of, s);
+        if (e != cudaSuccess) return PM_ERR_CUDA;
+        e = launch_quant_fp8(x, T, H, k, slot_of, a1, a1s, s, scale_rule, zero, zero_n);
+        if (e != cudaSuccess) return PM_ERR_CUDA;
+    }
     if (fused) {
         st = small_fused_fp8(a1, a1s, w1, w1_s, a2, a2s, w2, w2_s, expert_ids, npp, sorted, topk_w, L.max_slots,
                              T * k, H, I, E, c3, sched, status, d.sms, s, scale_rule);

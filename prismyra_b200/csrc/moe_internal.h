@@ -41,6 +41,10 @@ constexpr int kBlockM = 128;  // rows of one GEMM tile == the alignment block of
 // Activation-scale rules of the FP8 quantisations (e4m3_group_scale in ptx.cuh).
 constexpr int kScaleDiv = 0, kScaleUe8m0 = 1, kScaleRcp = 2;
 constexpr int kMaxExperts = 256;
+// T*k range in which the forward runs the top-k, the alignment and the quantisation as one launch (below it the
+// three short launches measured faster: at T*k = 256 the one launch's grid barrier costs more than it saves)
+constexpr int kFrontMinIndices = 512;
+constexpr int kFrontMaxIndices = 4096;
 constexpr int kMaxTopK = 16;
 // The alignment kernels split the n flat (token, slot) indices into at most kAlignMaxChunks chunks of
 // align_chunk(n) indices (one chunk up to 1024 indices, else at least 512, a multiple of 256); the per-chunk count
@@ -59,11 +63,13 @@ inline int cdiv(long a, long b) { return static_cast<int>((a + b - 1) / b); }
 // Router projection (bf16, fp32 accumulation in a fixed order per row) fused with softmax / top-k.
 // bias (may be null): fp32 [E] added to each logit before the ranking.
 // part: fp32 scratch of router_split_bytes(T, H, E) bytes for the split launch shape, or nullptr (fused shape);
-// both give the same bits.
+// both give the same bits.  Without topk only the projection runs: the bf16 logits (fused shape) or the fp32
+// partials (split shape, router_split_bytes > 0) are left for launch_front_small.
 size_t router_split_bytes(int T, int H, int E);
+int router_chunks(int H);  // the split shape's partials per token
 cudaError_t launch_router_topk(const void* x, const void* w, const float* bias, int T, int H, int E, int k,
                                void* logits, float* topk_w, int32_t* topk_ids, int32_t* err, cudaStream_t s,
-                               float* part = nullptr);
+                               float* part = nullptr, bool topk = true);
 // Softmax / top-k / renormalise from given bf16 logits (+ optional fp32 bias per expert).
 cudaError_t launch_topk(const void* logits, const float* bias, int T, int E, int k, float* topk_w, int32_t* topk_ids,
                         cudaStream_t s);
@@ -80,6 +86,16 @@ cudaError_t launch_align(const int32_t* ids, int n, int E, int32_t* counts, int3
 // zero (may be null): zero_n int32 counters the launch sets to 0 once its predecessor has completed.
 cudaError_t launch_quant_fp8(const void* x, int T, int H, int k, const int32_t* slot_of, uint8_t* x_q, float* x_s,
                              cudaStream_t s, int scale_rule = 0, int32_t* zero = nullptr, int zero_n = 0);
+// The few-token front end in one launch (T*k <= kFrontMaxIndices, E <= kMaxExperts): the top-k (from the
+// router's fp32 partials, which also gives the bf16 logits, from bf16 logits_in, or skipped when both are null and
+// topk_w/topk_ids are given), the alignment (launch_align's outputs; counts not written) and the quantisation into
+// slots (launch_quant_fp8 with slot_of), with one grid barrier on the counter *bar, which must be zero when the
+// launch starts.  A barrier that times out sets *err.
+cudaError_t launch_front_small(const float* part, int chunks, const void* logits_in, void* logits_out,
+                               const float* bias, int T, int E, int k, float* topk_w, int32_t* topk_ids,
+                               int32_t* sorted, int32_t* expert_ids, int32_t* num_post_pad, int32_t* expert_off,
+                               int32_t* slot_of, const void* x, int H, uint8_t* x_q, float* x_s, int scale_rule,
+                               int32_t* zero, int zero_n, int32_t* bar, int32_t* err, cudaStream_t s);
 // out[t] = bf16(sum_j c3[row(t*k + j)]) in fp32, j ascending; row = identity or row_of.
 cudaError_t launch_combine(const void* c3, const int32_t* row_of, int T, int k, int H, void* out, cudaStream_t s,
                            const void* add = nullptr);

@@ -3,18 +3,17 @@
 // fused_moe.py:1864).
 #include "moe_internal.h"
 #include "ptx.cuh"
+#include "quant_dev.cuh"
 
 namespace pm {
 namespace {
 
-// One half-warp per (token, 128-column group), two groups per warp: each lane converts 8 columns, the group's amax
-// is a half-warp reduction, and every copy of the group is one coalesced 128-byte segment (so small token counts
-// still spread over the whole GPU).  s = e4m3_group_scale(amax, scale_rule) (ptx.cuh: by default the correctly
-// rounded max(amax, 1e-10) / 448 of vLLM's compiled quantiser); q = e4m3(clamp(x / s, -448, 448)) with an IEEE
-// division.  With slot_of the row is written to the
-// token's k slots (its expert-ordered copies for the gate_up GEMM; vLLM reads the same rows through
-// sorted_ids // top_k); the padding slots are left unwritten -- their GEMM rows are computed and discarded, never
-// stored.  Without slot_of the single copy goes to row t.
+// Two (token, 128-column group) items per warp (quant_fp8_item, quant_dev.cuh): every copy of a group is one
+// coalesced 128-byte segment, so small token counts still spread over the whole GPU.  s = e4m3_group_scale(amax,
+// scale_rule) (ptx.cuh: by default the correctly rounded max(amax, 1e-10) / 448 of vLLM's compiled quantiser).
+// With slot_of the row is written to the token's k slots (its expert-ordered copies for the gate_up GEMM; vLLM reads
+// the same rows through sorted_ids // top_k); the padding slots are left unwritten -- their GEMM rows are computed
+// and discarded, never stored.  Without slot_of the single copy goes to row t.
 __global__ void __launch_bounds__(256) quant_fp8_kernel(const __nv_bfloat16* __restrict__ x, int T, int H, int k,
                                                         const int32_t* __restrict__ slot_of,
                                                         uint8_t* __restrict__ x_q, float* __restrict__ x_s,
@@ -23,45 +22,15 @@ __global__ void __launch_bounds__(256) quant_fp8_kernel(const __nv_bfloat16* __r
     pdl_trigger();
     // counters the next kernel starts from zero (its work queue and hand-off counters)
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < zero_n; i += gridDim.x * blockDim.x) zero[i] = 0;
-    const int lane = threadIdx.x & 31, sub = lane & 15;
-    const int G = H / 128;
-    const long items = (long)T * G;
-    const long pairs = (items + 1) / 2;
+    const long pairs = ((long)T * (H / 128) + 1) / 2;
     const long nwarps = ((long)gridDim.x * blockDim.x) >> 5;
-    const int ncopies = slot_of != nullptr ? k : 1;
     for (long wp = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; wp < pairs; wp += nwarps) {
-        const long item = 2 * wp + (lane >> 4);
-        const bool valid = item < items;
-        const long row = valid ? item / G : 0;
-        const int col = valid ? (int)(item % G) * 128 + sub * 8 : 0;
-        float v[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-        float amax = 0.0f;
-        if (valid) {
-            const uint4 w = *reinterpret_cast<const uint4*>(x + row * H + col);
-            const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&w);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                v[i] = __bfloat162float(b[i]);
-                amax = fmaxf(amax, fabsf(v[i]));
-            }
-        }
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        if (!valid) continue;
-        const float sc = e4m3_group_scale(amax, scale_rule);
-        uint32_t packed[2];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const float q0 = fminf(fmaxf(__fdiv_rn(v[4 * i + 0], sc), -448.0f), 448.0f);
-            const float q1 = fminf(fmaxf(__fdiv_rn(v[4 * i + 1], sc), -448.0f), 448.0f);
-            const float q2 = fminf(fmaxf(__fdiv_rn(v[4 * i + 2], sc), -448.0f), 448.0f);
-            const float q3 = fminf(fmaxf(__fdiv_rn(v[4 * i + 3], sc), -448.0f), 448.0f);
-            packed[i] = (uint32_t)e4m3x2(q0, q1) | ((uint32_t)e4m3x2(q2, q3) << 16);
-        }
-        for (int c = 0; c < ncopies; ++c) {
-            const size_t dst = slot_of != nullptr ? (size_t)slot_of[row * k + c] : (size_t)row;
-            *reinterpret_cast<uint2*>(x_q + dst * H + col) = make_uint2(packed[0], packed[1]);
-            if (sub == 0) x_s[dst * G + col / 128] = sc;
+        const QuantItem it = quant_fp8_item(x, T, H, scale_rule, wp);
+        if (!it.valid) continue;
+        if (slot_of == nullptr) {
+            store_quant_item(it, H, (size_t)it.row, x_q, x_s);
+        } else {
+            for (int c = 0; c < k; ++c) store_quant_item(it, H, (size_t)slot_of[it.row * k + c], x_q, x_s);
         }
     }
 }

@@ -196,6 +196,8 @@ cudaError_t configure_router() {
 
 }  // namespace
 
+int router_chunks(int H) { return H / kChunkK; }
+
 size_t router_split_bytes(int T, int H, int E) {
     // the split shape when the fused grid would occupy few SMs
     if (T <= 0 || (long)cdiv(T, kTM) * cdiv(E, kTN) > 64) return 0;
@@ -204,7 +206,7 @@ size_t router_split_bytes(int T, int H, int E) {
 
 cudaError_t launch_router_topk(const void* x, const void* w, const float* bias, int T, int H, int E, int k,
                                void* logits, float* topk_w, int32_t* topk_ids, int32_t* err, cudaStream_t s,
-                               float* part) {
+                               float* part, bool topk) {
     if (T == 0) return cudaSuccess;
     if (logits == nullptr || H % kChunkK != 0) return cudaErrorInvalidValue;
     CUtensorMap tx, tw;
@@ -231,7 +233,7 @@ cudaError_t launch_router_topk(const void* x, const void* w, const float* bias, 
         PM_TRY(launch_pdl(router_tc_kernel<kStepsPerChunk, true>, dim3(grid), dim3(kRouterThreads),
                           router_smem<kStepsPerChunk>(), s, tx, tw, T, H, E, lg, part, err));
         cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess) return e;
+        if (e != cudaSuccess || !topk) return e;
         return launch_topk_partials(part, chunks, lg, bias, T, E, k, topk_w, topk_ids, s);
     }
     const dim3 grid(cdiv(T, kTM), cdiv(E, kTN));
@@ -242,7 +244,7 @@ cudaError_t launch_router_topk(const void* x, const void* w, const float* bias, 
         PM_TRY(launch_pdl(router_tc_kernel<kTStagesWide, false>, dim3(grid), dim3(kRouterThreads),
                           router_smem<kTStagesWide>(), s, tx, tw, T, H, E, lg, nullptr, err));
     cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess || !topk) return e;
     return launch_topk(logits, bias, T, E, k, topk_w, topk_ids, s);
 }
 
