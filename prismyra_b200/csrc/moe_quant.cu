@@ -39,12 +39,15 @@ __global__ void __launch_bounds__(256) quant_fp8_kernel(const __nv_bfloat16* __r
 // identity or the row_of map (rows returned by expert-parallel ranks arrive in their send order).  With add, the
 // rounded sum is then added to add[t] and rounded again: `routed + shared` of two bf16 tensors (reference
 // prismyra/kernels/qwen3_moe.py:199).
+// KT: the top-k as a compile-time constant (all k rows' loads issued before the sum), or 0 for any k.
+template <int KT>
 __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ c3,
-                                                      const int32_t* __restrict__ row_of, int T, int k, int H,
+                                                      const int32_t* __restrict__ row_of, int T, int k_rt, int H,
                                                       const __nv_bfloat16* __restrict__ add,
                                                       __nv_bfloat16* __restrict__ out) {
     pdl_wait();
     pdl_trigger();
+    const int k = KT > 0 ? KT : k_rt;
     const long total = (long)T * (H / 8);
     for (long q = (long)blockIdx.x * blockDim.x + threadIdx.x; q < total; q += (long)gridDim.x * blockDim.x) {
         const long t = q / (H / 8);
@@ -52,12 +55,26 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
         float acc[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-        for (int j = 0; j < k; ++j) {
-            const size_t rrow = row_of != nullptr ? (size_t)row_of[(size_t)t * k + j] : (size_t)t * k + j;
-            const uint4 u = *reinterpret_cast<const uint4*>(c3 + rrow * H + c);
-            const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+        auto row = [&](int j) {
+            return row_of != nullptr ? (size_t)row_of[(size_t)t * k + j] : (size_t)t * k + j;
+        };
+        if (KT > 0) {
+            uint4 u[KT > 0 ? KT : 1];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] += __bfloat162float(b[i]);
+            for (int j = 0; j < KT; ++j) u[j] = *reinterpret_cast<const uint4*>(c3 + row(j) * H + c);
+#pragma unroll
+            for (int j = 0; j < KT; ++j) {
+                const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u[j]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[i] += __bfloat162float(b[i]);
+            }
+        } else {
+            for (int j = 0; j < k; ++j) {
+                const uint4 u = *reinterpret_cast<const uint4*>(c3 + row(j) * H + c);
+                const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[i] += __bfloat162float(b[i]);
+            }
         }
         uint4 o;
         __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
@@ -128,8 +145,12 @@ cudaError_t launch_combine(const void* c3, const int32_t* row_of, int T, int k, 
     const long total = (long)T * (H / 8);
     const long want = (total + 255) / 256;
     const int blocks = (int)(want < (long)sms * 16 ? want : (long)sms * 16);
-    PM_TRY(launch_pdl(combine_kernel, dim3(blocks), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(c3), row_of, T,
-                      k, H, static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out)));
+    if (k == 8)
+        PM_TRY(launch_pdl(combine_kernel<8>, dim3(blocks), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(c3),
+                          row_of, T, k, H, static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out)));
+    else
+        PM_TRY(launch_pdl(combine_kernel<0>, dim3(blocks), dim3(256), 0, s, static_cast<const __nv_bfloat16*>(c3),
+                          row_of, T, k, H, static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out)));
     return cudaGetLastError();
 }
 
