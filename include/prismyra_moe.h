@@ -250,6 +250,14 @@ int pm_moe_forward_nvfp4(const void *x, const void *router_w, const void *logits
 int pm_nvfp4_prepare(const uint8_t *w, const float *s, int E, int R, int C, uint8_t *packed, uint8_t *scales,
                      float *g, pm_stream_t stream);
 
+/* The same with the importance search: prismyra/kernels/nvfp4.py:57-94 (quantize_search, which prepare_layer uses
+ * when it is given importance weights, nvfp4.py:322-325): each 16-group's e4m3 scale is the first of the fractions
+ * 1, 0.95, ..., 0.7 of its plain scale whose decoded group has the smallest importance-weighted squared error.
+ * importance: fp32 [E, C] per input column of each matrix (16-byte aligned), or NULL for weight 1 everywhere (the
+ * reference's choice for an expert that saw no tokens is a row of ones). */
+int pm_nvfp4_prepare_search(const uint8_t *w, const float *s, const float *importance, int E, int R, int C,
+                            uint8_t *packed, uint8_t *scales, float *g, pm_stream_t stream);
+
 /* Expert alignment that allocates nothing -- no counterpart in the reference.  Same results as pm_moe_align,
  * for callers that cannot hand the library scratch memory on demand: hosts that route every device byte through
  * their own pool and forbid library allocations, and latency-critical loops that cannot afford the implicit

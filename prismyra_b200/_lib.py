@@ -59,6 +59,7 @@ SIGNATURES: dict[str, tuple] = {
     "pm_moe_forward_nvfp4": (_I, [_P, _P, _P, _P, _P, _P, ctypes.c_float, _P, _P, _P, ctypes.c_float, _I, _I, _I,
                                   _I, _I, _P, _P, _Z, _P]),
     "pm_nvfp4_prepare": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P]),
+    "pm_nvfp4_prepare_search": (_I, [_P, _P, _P, _I, _I, _I, _P, _P, _P, _P]),
     "pm_fp8_linear_workspace_bytes": (_Z, [_I, _I, _I]),
     "pm_fp8_linear": (_I, [_P, _P, _P, _I, _I, _I, _P, _P, _Z, _P]),
     "pm_moe_shared_workspace_bytes": (_Z, [_I, _I, _I]),

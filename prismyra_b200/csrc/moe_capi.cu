@@ -900,8 +900,8 @@ int pm_fp8_linear(const void* x, const uint8_t* w, const float* w_s, int T, int 
     return cuda_status(launch_gemm_fp8(1, ta, tb, g, d.sms, s));
 }
 
-int pm_nvfp4_prepare(const uint8_t* w, const float* s, int E, int R, int C, uint8_t* packed, uint8_t* scales,
-                     float* g, pm_stream_t stream) {
+static int nvfp4_prepare_impl(const uint8_t* w, const float* s, int E, int R, int C, uint8_t* packed,
+                              uint8_t* scales, float* g, pm_stream_t stream, bool search, const float* imp) {
     if (E < 0 || R < 0 || C < 0) return PM_ERR_INVALID;
     if (R % 128 != 0 || C % 128 != 0 || (long)E * R > (1L << 31) || (long)E * R * C / 16 > (1L << 31))
         return PM_ERR_SHAPE;
@@ -913,7 +913,19 @@ int pm_nvfp4_prepare(const uint8_t* w, const float* s, int E, int R, int C, uint
     DeviceInfo d;
     const int st = current_device_info(&d);
     if (st != PM_OK) return st;
-    return cuda_status(launch_nvfp4_prepare(w, s, E, R, C, packed, scales, g, d.sms, (cudaStream_t)stream));
+    if (imp != nullptr && !a16(imp)) return PM_ERR_ALIGN;
+    return cuda_status(
+        launch_nvfp4_prepare(w, s, E, R, C, packed, scales, g, d.sms, (cudaStream_t)stream, search, imp));
+}
+
+int pm_nvfp4_prepare(const uint8_t* w, const float* s, int E, int R, int C, uint8_t* packed, uint8_t* scales,
+                     float* g, pm_stream_t stream) {
+    return nvfp4_prepare_impl(w, s, E, R, C, packed, scales, g, stream, false, nullptr);
+}
+
+int pm_nvfp4_prepare_search(const uint8_t* w, const float* s, const float* importance, int E, int R, int C,
+                            uint8_t* packed, uint8_t* scales, float* g, pm_stream_t stream) {
+    return nvfp4_prepare_impl(w, s, E, R, C, packed, scales, g, stream, true, importance);
 }
 
 // ---------------------------------------------------------------------------------------- expert parallelism

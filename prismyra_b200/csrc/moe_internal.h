@@ -202,8 +202,10 @@ cudaError_t launch_quant_nvfp4(const void* x, int T, int H, int k, const int32_t
 cudaError_t launch_gemm_nvfp4(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, const NvGemmArgs& args,
                               int num_sms, cudaStream_t s);
 // NVFP4 weight preparation of E FP8 block-scaled matrices of R x C (g doubles as the scratch of the maxima).
+// search: each 16-group's scale chosen by the importance search (imp [E, C] per input column, or null: weight 1).
 cudaError_t launch_nvfp4_prepare(const uint8_t* w, const float* s, int E, int R, int C, uint8_t* packed,
-                                 uint8_t* sf, float* g, int sms, cudaStream_t stream);
+                                 uint8_t* sf, float* g, int sms, cudaStream_t stream, bool search = false,
+                                 const float* imp = nullptr);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda): a 2-D row-major
 // tensor of `outer` rows x `inner` elements, rows `row_bytes` apart, 128-byte swizzled boxes.

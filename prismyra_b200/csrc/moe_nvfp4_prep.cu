@@ -15,7 +15,8 @@
 //
 // Launches: a zeroing of the per-matrix maxima, the maxima (byte-wise magnitude maxima of the e4m3 codes, then an
 // unsigned max on the bit patterns of non-negative floats -- exact and order-free), the global scales, and the
-// quantisation of every 16-element group (one thread per group, 16-byte loads, no division per weight).
+// quantisation of every 16-element group (one thread per group, 16-byte loads, no division per weight) -- or, with
+// the importance search, the same with each group's scale chosen among seven candidates (prep_search_kernel).
 #include "moe_internal.h"
 #include "ptx.cuh"
 
@@ -159,10 +160,122 @@ __global__ void __launch_bounds__(256) prep_quant_kernel(const uint8_t* __restri
     }
 }
 
+// The importance search (prismyra/kernels/nvfp4.py:57-94, quantize_search): each 16-group's scale is the first of
+// the SEARCH fractions c of its plain value, sf_c = e4m3(min(((amax16 / 6) * g) * c, 448)), that minimises the
+// importance-weighted squared error of the decoded group, err_c = sum_j imp_j * (back_j - d_j)^2 with
+// back_j = (E2M1[code_j] * sign_j) * eff_c, every step rounded in fp32 as torch evaluates it (the fraction is an fp32
+// scalar; (x)^2 is x * x; amax / 6 a true division) and the 16 products added as torch's last-dimension sum adds
+// them on the CPU, where the reference's golden outputs were made: eight strided partial sums p_j + p_{j+8}, added
+// in order (checked against torch on 200,000 rows).  torch on a GPU computes amax / 6 as amax * fl(1/6) and adds
+// the products by halving steps, so the reference run on a GPU can choose differently where candidates nearly tie;
+// this kernel follows the CPU, like the plain preparation above.  imp: [E, C] per input column, or null (every
+// column weighs 1).
+__device__ __constant__ float kSearchFrac[7] = {1.0f, 0.95f, 0.9f, 0.85f, 0.8f, 0.75f, 0.7f};
+
+// The e2m1 magnitude of a 3-bit code (0, 0.5, 1, 1.5, 2, 3, 4, 6), exactly, without a table lookup.
+__device__ __forceinline__ float e2m1_value(uint32_t m) {
+    const float pow2 = __int_as_float((int)(((m >> 1) + 126u) << 23));  // 2^((m >> 1) - 1)
+    return m < 2u ? 0.5f * (float)m : pow2 * (1.0f + 0.5f * (float)(m & 1u));
+}
+
+__device__ __forceinline__ float e4m3_scale(float amax, float gm, float frac, __nv_fp8_storage_t* byte) {
+    const float scale = fminf(__fmul_rn(__fmul_rn(__fdiv_rn(amax, 6.0f), gm), frac), 448.0f);
+    *byte = __nv_cvt_float_to_fp8(scale, __NV_SATFINITE, __NV_E4M3);
+    return __fdiv_rn(e4m3_to_f32(*byte), gm);
+}
+
+__global__ void __launch_bounds__(256) prep_search_kernel(const uint8_t* __restrict__ w, const float* __restrict__ s,
+                                                          const float* __restrict__ g,
+                                                          const float* __restrict__ imp, int E, int R, int C,
+                                                          uint8_t* __restrict__ packed, uint8_t* __restrict__ sf) {
+    const unsigned per_row = C / 16, cb = C / 128, rows = (unsigned)E * R;
+    for (VecWalk it(blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x, per_row); it.row < rows;
+         it.next()) {
+        const size_t i = (size_t)it.row * per_row + it.cv;
+        const uint4 q = *reinterpret_cast<const uint4*>(w + i * 16);
+        const float sb = s[(it.row / 128) * cb + it.cv / 8];
+        const float amax = fabsf(__fmul_rn(e4m3_to_f32(max_magnitude_code(q)), sb));
+        const unsigned m = it.row / (unsigned)R;
+        const float gm = g[m];
+        float d[16], wt[16];
+        const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+            const __half2_raw h2 = __nv_cvt_fp8x2_to_halfraw2(
+                static_cast<__nv_fp8x2_storage_t>((words[p / 2] >> (16 * (p % 2))) & 0xffffu), __NV_E4M3);
+            const float2 v = __half22float2(__half2(h2));
+            d[2 * p] = __fmul_rn(v.x, sb);
+            d[2 * p + 1] = __fmul_rn(v.y, sb);
+        }
+        if (imp != nullptr) {
+            const float4* ip = reinterpret_cast<const float4*>(imp + (size_t)m * C + (size_t)it.cv * 16);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float4 f = ip[u];
+                wt[4 * u] = f.x;
+                wt[4 * u + 1] = f.y;
+                wt[4 * u + 2] = f.z;
+                wt[4 * u + 3] = f.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) wt[j] = 1.0f;
+        }
+        __nv_fp8_storage_t best_byte = 0;
+        float best_eff = 0.0f, best_err = 0.0f;
+        for (int c = 0; c < 7; ++c) {
+            __nv_fp8_storage_t byte;
+            const float eff = e4m3_scale(amax, gm, kSearchFrac[c], &byte);
+            const bool live = eff > 0.0f;
+            float F[7];
+            if (live) {
+                e2m1_bounds(eff, F);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 7; ++j) F[j] = __int_as_float(0x7f800000);
+            }
+            float e[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const uint32_t code = e2m1_code(d[j], F, live);
+                const float sgn = (code & 8u) ? -1.0f : 1.0f;
+                const float back = __fmul_rn(__fmul_rn(e2m1_value(code & 7u), sgn), eff);
+                const float diff = __fsub_rn(back, d[j]);
+                e[j] = __fmul_rn(wt[j], __fmul_rn(diff, diff));
+            }
+            float err = __fadd_rn(e[0], e[8]);
+#pragma unroll
+            for (int j = 1; j < 8; ++j) err = __fadd_rn(err, __fadd_rn(e[j], e[j + 8]));
+            if (c == 0 || err < best_err) {
+                best_err = err;
+                best_byte = byte;
+                best_eff = eff;
+            }
+        }
+        const bool live = best_eff > 0.0f;
+        float F[7];
+        if (live) {
+            e2m1_bounds(best_eff, F);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 7; ++j) F[j] = __int_as_float(0x7f800000);
+        }
+        uint32_t out[2] = {0u, 0u};
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+            const uint32_t c0 = e2m1_code(d[2 * p], F, live);
+            const uint32_t c1 = e2m1_code(d[2 * p + 1], F, live);
+            out[p / 4] |= (c0 | (c1 << 4)) << (8 * (p % 4));
+        }
+        *reinterpret_cast<uint2*>(packed + i * 8) = make_uint2(out[0], out[1]);
+        sf[i] = static_cast<uint8_t>(best_byte);
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_nvfp4_prepare(const uint8_t* w, const float* s, int E, int R, int C, uint8_t* packed,
-                                 uint8_t* sf, float* g, int sms, cudaStream_t stream) {
+                                 uint8_t* sf, float* g, int sms, cudaStream_t stream, bool search, const float* imp) {
     cudaError_t e = cudaMemsetAsync(g, 0, sizeof(float) * (size_t)E, stream);
     if (e != cudaSuccess) return e;
     const long groups = (long)R * C / 16;  // per matrix
@@ -170,7 +283,10 @@ cudaError_t launch_nvfp4_prepare(const uint8_t* w, const float* s, int E, int R,
     prep_amax_kernel<<<dim3(per_matrix, E), 256, 0, stream>>>(w, s, R, C, reinterpret_cast<unsigned*>(g));
     prep_global_kernel<<<(E + 255) / 256, 256, 0, stream>>>(g, E);
     const long blocks = std::min<long>((long)sms * 8, (groups * E + 255) / 256);
-    prep_quant_kernel<<<(int)blocks, 256, 0, stream>>>(w, s, g, E, R, C, packed, sf);
+    if (search)
+        prep_search_kernel<<<(int)blocks, 256, 0, stream>>>(w, s, g, imp, E, R, C, packed, sf);
+    else
+        prep_quant_kernel<<<(int)blocks, 256, 0, stream>>>(w, s, g, E, R, C, packed, sf);
     return cudaGetLastError();
 }
 

@@ -122,24 +122,30 @@ def prepare_layer(w13, s13, w2, s2, device, imp_in=None, imp_mid=None, tok=None)
     """One layer's FP8 experts -> NVFP4 tensors (row-major scales) and one global scale per expert matrix
     (the reference's nvfp4.py:315-331, same arguments and results).
 
-    On a CUDA device without importance weights the whole stack goes through the library's preparation kernels
+    On a CUDA device the whole stack goes through the library's preparation kernels
     (:func:`prismyra_b200.ops.nvfp4_prepare`, bit-identical to the torch arithmetic of :func:`_prepare_stack`);
     with importance weights (imp_in for w13's input columns, imp_mid for w2's) each 16-group's scale is searched,
     experts whose token count ``tok`` is 0 weighing every column 1."""
     dev = torch.device(device)
-    if dev.type == "cuda" and imp_in is None:
-        out = {}
-        for w, s, tag in ((w13, s13, "1"), (w2, s2, "2")):
-            packed, scale, g = ops.nvfp4_prepare(w.to(dev).contiguous(), s.to(dev, torch.float32).contiguous())
+    def importance(imp):
+        if imp is None:
+            return None
+        imp = imp.float().clone()
+        if tok is not None:
+            imp[torch.as_tensor(tok) <= 0] = 1.0  # experts without tokens: plain squared error
+        return imp
+
+    out = {}
+    if dev.type == "cuda":
+        for w, s, imp, tag in ((w13, s13, imp_in, "1"), (w2, s2, imp_mid, "2")):
+            imp = importance(imp)
+            packed, scale, g = ops.nvfp4_prepare(w.to(dev).contiguous(), s.to(dev, torch.float32).contiguous(),
+                                                 importance=imp.to(dev).contiguous() if imp is not None else None,
+                                                 search=imp_in is not None)
             out["w" + tag], out["s" + tag], out["g" + tag] = packed, scale, g
         return {k: v.cpu() for k, v in out.items()}
-    out = {}
     for w, s, imp, tag in ((w13, s13, imp_in, "1"), (w2, s2, imp_mid, "2")):
-        if imp is not None:
-            imp = imp.float().clone()
-            if tok is not None:
-                imp[torch.as_tensor(tok) <= 0] = 1.0  # experts without tokens: plain squared error
-        out["w" + tag], out["s" + tag], out["g" + tag] = _prepare_stack(w, s, dev, imp)
+        out["w" + tag], out["s" + tag], out["g" + tag] = _prepare_stack(w, s, dev, importance(imp))
     return out
 
 

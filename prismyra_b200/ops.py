@@ -569,16 +569,24 @@ def gemm2_nvfp4(a_q, a_sf, w2, w2_sf, alpha2, expert_ids, npp, sorted_ids, topk_
     return c3, err
 
 
-def nvfp4_prepare(w: torch.Tensor, s: torch.Tensor):
+def nvfp4_prepare(w: torch.Tensor, s: torch.Tensor, importance: torch.Tensor | None = None, search: bool = False):
     """FP8 expert stack -> NVFP4 on the GPU: w e4m3 (or its bytes) [E, R, C], s fp32 [E, R/128, C/128] ->
     (packed u8 [E, R, C/2], row-major e4m3 scales [E, R, C/16], g fp32 [E]); bit for bit the reference's
-    prepare_layer arithmetic (prismyra/kernels/nvfp4.py:315-331)."""
+    prepare_layer arithmetic (prismyra/kernels/nvfp4.py:315-331).  With ``importance`` (fp32 [E, C] per input
+    column) or ``search``, each 16-group's scale comes from the importance search (quantize_search,
+    nvfp4.py:57-94; without importance every column weighs 1)."""
     _cuda(w, "w", (torch.float8_e4m3fn, torch.uint8))
     _need(w.dim() == 3, "w must be [E, R, C]")
     E, R, C = w.shape
     _cuda(s, "s", torch.float32, (E, R // 128, C // 128))
+    if importance is not None:
+        _cuda(importance, "importance", torch.float32, (E, C))
     packed = torch.empty(E, R, C // 2, dtype=torch.uint8, device=w.device)
     scales = torch.empty(E, R, C // 16, dtype=torch.float8_e4m3fn, device=w.device)
     g = torch.empty(E, dtype=torch.float32, device=w.device)
-    _lib.call("pm_nvfp4_prepare", _p(w), _p(s), E, R, C, _p(packed), _p(scales), _p(g), _stream(w.device))
+    if importance is not None or search:
+        _lib.call("pm_nvfp4_prepare_search", _p(w), _p(s), _p(importance), E, R, C, _p(packed), _p(scales), _p(g),
+                  _stream(w.device))
+    else:
+        _lib.call("pm_nvfp4_prepare", _p(w), _p(s), E, R, C, _p(packed), _p(scales), _p(g), _stream(w.device))
     return packed, scales, g

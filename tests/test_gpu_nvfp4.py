@@ -182,3 +182,38 @@ def test_prepare_on_gpu_matches_reference_fixture(golden):
         assert np.array_equal(bits(packed), g["prep_w" + tag])
         assert np.array_equal(bits(sf), g["prep_s" + tag])
         assert np.array_equal(bits(gs), g["prep_g" + tag])
+
+
+@pytest.mark.parametrize("stack", ["w1", "w2"])
+def test_prepare_search_on_gpu_matches_torch_restatement(layer, stack):
+    """The search kernel on two experts of each layer stack with spread-out importance weights (and, for the
+    second, a weight of 1 everywhere) against the torch restatement (_prepare_stack, the reference's
+    quantize_search arithmetic) on the CPU, where the reference's outputs were made: bit-exact.  Also the search
+    without importance against the restatement with a weight of 1."""
+    _, cpu, _, _ = layer
+    fp8 = cpu["fp8"]
+    w, s = fp8[stack][:2].contiguous(), fp8[stack + "_s"][:2].float().contiguous()
+    C = w.shape[2]
+    gen = torch.Generator(device="cpu").manual_seed(11)
+    imp = torch.exp(torch.randn(2, C, generator=gen) * 2.0).float()
+    imp[1] = 1.0
+    packed, sf, gs = ops.nvfp4_prepare(w.to(DEV).view(torch.uint8), s.to(DEV), importance=imp.to(DEV))
+    rp, rs, rg = nvfp4._prepare_stack(w, s, "cpu", imp)
+    assert np.array_equal(bits(packed), bits(rp)) and np.array_equal(bits(sf), bits(rs))
+    assert np.array_equal(bits(gs), bits(rg))
+    p1, s1, _ = ops.nvfp4_prepare(w.to(DEV).view(torch.uint8), s.to(DEV), search=True)
+    rp1, rs1, _ = nvfp4._prepare_stack(w, s, "cpu", torch.ones(2, C))
+    assert np.array_equal(bits(p1), bits(rp1)) and np.array_equal(bits(s1), bits(rs1))
+
+
+def test_prepare_search_on_gpu_matches_reference_fixture(golden):
+    """pm_nvfp4_prepare_search through prepare_layer(imp_in=..., imp_mid=..., tok=...) on the GPU against the
+    reference's own prepare_layer outputs with importance weights (tests/golden/nvfp4_search.npz; one expert there
+    saw no tokens and is searched with weight 1): codes, scale bytes and global scales bit-exact."""
+    g = golden("nvfp4_search")
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    got = nvfp4.prepare_layer(t(g["fp8_w"]).view(torch.float8_e4m3fn), t(g["fp8_s"]),
+                              t(g["fp8_w2"]).view(torch.float8_e4m3fn), t(g["fp8_s2"]), DEV,
+                              imp_in=t(g["imp_in"]), imp_mid=t(g["imp_mid"]), tok=t(g["tok"]))
+    for k in ("w1", "s1", "g1", "w2", "s2", "g2"):
+        assert np.array_equal(bits(got[k]), g["prep_" + k]), k
