@@ -327,6 +327,7 @@ static int small_fused_fp8(const uint8_t* a1, const float* a1s, const uint8_t* w
     g[0].n_tiles = I / 128;
     g[0].out_q = a2;
     g[0].out_s = a2s;
+    g[0].prefetch_units = E * (I / 128);
     g[1].a_scale = a2s;
     g[1].b_scale = w2_s;
     g[1].n_total = H;

@@ -318,6 +318,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort = &tail->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+    if (MODE == 2 && threadIdx.x == 96 && (int)blockIdx.x < a0.prefetch_units) {
+        // The weights of this CTA's likely first gate_up unit (unit = CTA index, block b taken to hold expert b, as
+        // when every expert has one block), into L2 while the predecessor runs: constant data, so no need to wait
+        // for it; a wrong guess only costs the prefetch.
+        const int e = (int)blockIdx.x / a0.n_tiles, nt = (int)blockIdx.x % a0.n_tiles;
+        const int wrow = e * a0.n_total + nt * 128;
+        for (int kb = 0; kb < a0.K / 128; ++kb) {
+            tma_prefetch_l2(&tm_w0, kb * 128, wrow);
+            tma_prefetch_l2(&tm_w0, kb * 128, wrow + a0.inter);
+        }
+    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
             mbar_init(smem_u32(&tail->full[s]), 1);

@@ -160,6 +160,7 @@ struct SmallGemmArgs {
     __nv_bfloat16* c3;           // down: [n_valid, H]
     int scale_rule;              // gate_up: how requantisation scales are formed (e4m3_group_scale)
     int* err;
+    int prefetch_units;          // fused, gate_up: units whose weights CTA b (b < this) prefetches before it waits
 };
 // The small-token path is used when T*k <= kSmallTokensPerExpert * E and the K-block scale table fits.
 constexpr int kSmallTokensPerExpert = 32;
