@@ -462,7 +462,11 @@ static int forward_fp8_impl(const void* x, const void* router_w, const void* log
     float* a2s = reinterpret_cast<float*>(R(PM_WS_A2_SCALE));
     void* c3 = R(PM_WS_C3);
 
-    if (clear_status && cudaMemsetAsync(status, 0, L.len[PM_WS_STATUS], s) != cudaSuccess) return PM_ERR_CUDA;
+    // The status words start at zero: with the router projection, its kernel (the forward's first) zeroes them, so
+    // that the previous forward's last kernel and this forward's first still overlap; with given logits, a memset.
+    int32_t* clear = clear_status && logits == nullptr ? status : nullptr;
+    if (clear_status && clear == nullptr && cudaMemsetAsync(status, 0, L.len[PM_WS_STATUS], s) != cudaSuccess)
+        return PM_ERR_CUDA;
     int32_t* slot_of = reinterpret_cast<int32_t*>(R(PM_WS_SLOT_OF));
     // Both few-token GEMMs in one launch once most experts are hit (T*k >= 2E); with fewer pairs nearly every down
     // unit would wait for its block's few gate_up units, and two launches are faster.
@@ -477,7 +481,7 @@ static int forward_fp8_impl(const void* x, const void* router_w, const void* log
         const bool split = logits == nullptr && router_part != nullptr && router_split_bytes(T, H, E) > 0;
         if (logits == nullptr) {
             e = launch_router_topk(x, router_w, bias, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s,
-                                   router_part, false);
+                                   router_part, false, clear);
             if (e != cudaSuccess) return PM_ERR_CUDA;
         }
         const void* lg_in = split ? nullptr : (logits != nullptr ? logits : R(PM_WS_LOGITS));
@@ -491,7 +495,7 @@ static int forward_fp8_impl(const void* x, const void* router_w, const void* log
             e = launch_topk(logits, bias, T, E, k, topk_w, topk_ids, s);
         else
             e = launch_router_topk(x, router_w, bias, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s,
-                                   router_part);
+                                   router_part, true, clear);
         if (e != cudaSuccess) return PM_ERR_CUDA;
         e = launch_align(topk_ids, T * k, E, reinterpret_cast<int32_t*>(R(PM_WS_COUNTS)), sorted, expert_ids, npp,
                          reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_OFF)), slot_of, s);

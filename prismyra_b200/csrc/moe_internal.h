@@ -67,9 +67,10 @@ inline int cdiv(long a, long b) { return static_cast<int>((a + b - 1) / b); }
 // partials (split shape, router_split_bytes > 0) are left for launch_front_small.
 size_t router_split_bytes(int T, int H, int E);
 int router_chunks(int H);  // the split shape's partials per token
+// clear (may be null): four status words the launch zeroes first (the forward's, instead of a memset).
 cudaError_t launch_router_topk(const void* x, const void* w, const float* bias, int T, int H, int E, int k,
                                void* logits, float* topk_w, int32_t* topk_ids, int32_t* err, cudaStream_t s,
-                               float* part = nullptr, bool topk = true);
+                               float* part = nullptr, bool topk = true, int32_t* clear = nullptr);
 // Softmax / top-k / renormalise from given bf16 logits (+ optional fp32 bias per expert).
 cudaError_t launch_topk(const void* logits, const float* bias, int T, int E, int k, float* topk_w, int32_t* topk_ids,
                         cudaStream_t s);

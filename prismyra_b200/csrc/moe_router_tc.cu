@@ -52,12 +52,13 @@ constexpr size_t router_smem() {
 
 // SPLIT: this CTA computes the single chunk blockIdx.z and stores it to part[c][t][e] (fp32); otherwise it
 // computes every chunk and stores bf16 logits.
-constexpr int kRouterThreads = 192;  // warp 0 TMA, warp 1 TMEM + MMA, warps 2-5 epilogue (lane quarter = warp % 4)
+constexpr int kRouterThreads = 192;
+constexpr int kClearWords = 4;  // status words a launch given `clear` zeroes  // warp 0 TMA, warp 1 TMEM + MMA, warps 2-5 epilogue (lane quarter = warp % 4)
 
 template <int STAGES, bool SPLIT>
 __global__ void __launch_bounds__(kRouterThreads, 1)
     router_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w, int T, int H,
-                     int E, __nv_bfloat16* __restrict__ logits, float* __restrict__ part, int* err) {
+                     int E, __nv_bfloat16* __restrict__ logits, float* __restrict__ part, int* err, int* clear) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -94,6 +95,13 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
     const uint32_t tmem = tail->tmem_base;
     pdl_wait();
     pdl_trigger();
+    // the forward's status words, zeroed by its first kernel in place of a memset (which would stop the previous
+    // forward's last kernel and this one from overlapping): CTA 0 does it at once, long before any wait of this
+    // grid could time out and raise them
+    if (clear != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0) {
+#pragma unroll
+        for (int i = 0; i < kClearWords; ++i) clear[i] = 0;
+    }
 
     if (warp == 0 && lane == 0) {
         int stage = 0;
@@ -206,7 +214,7 @@ size_t router_split_bytes(int T, int H, int E) {
 
 cudaError_t launch_router_topk(const void* x, const void* w, const float* bias, int T, int H, int E, int k,
                                void* logits, float* topk_w, int32_t* topk_ids, int32_t* err, cudaStream_t s,
-                               float* part, bool topk) {
+                               float* part, bool topk, int32_t* clear) {
     if (T == 0) return cudaSuccess;
     if (logits == nullptr || H % kChunkK != 0) return cudaErrorInvalidValue;
     CUtensorMap tx, tw;
@@ -231,7 +239,7 @@ cudaError_t launch_router_topk(const void* x, const void* w, const float* bias, 
     if (part != nullptr && router_split_bytes(T, H, E) > 0) {
         const dim3 grid(cdiv(T, kTM), cdiv(E, kTN), chunks);
         PM_TRY(launch_pdl(router_tc_kernel<kStepsPerChunk, true>, dim3(grid), dim3(kRouterThreads),
-                          router_smem<kStepsPerChunk>(), s, tx, tw, T, H, E, lg, part, err));
+                          router_smem<kStepsPerChunk>(), s, tx, tw, T, H, E, lg, part, err, clear));
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess || !topk) return e;
         return launch_topk_partials(part, chunks, lg, bias, T, E, k, topk_w, topk_ids, s);
@@ -239,10 +247,10 @@ cudaError_t launch_router_topk(const void* x, const void* w, const float* bias, 
     const dim3 grid(cdiv(T, kTM), cdiv(E, kTN));
     if ((long)grid.x * grid.y <= sms)
         PM_TRY(launch_pdl(router_tc_kernel<kTStagesDeep, false>, dim3(grid), dim3(kRouterThreads),
-                          router_smem<kTStagesDeep>(), s, tx, tw, T, H, E, lg, nullptr, err));
+                          router_smem<kTStagesDeep>(), s, tx, tw, T, H, E, lg, nullptr, err, clear));
     else
         PM_TRY(launch_pdl(router_tc_kernel<kTStagesWide, false>, dim3(grid), dim3(kRouterThreads),
-                          router_smem<kTStagesWide>(), s, tx, tw, T, H, E, lg, nullptr, err));
+                          router_smem<kTStagesWide>(), s, tx, tw, T, H, E, lg, nullptr, err, clear));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || !topk) return e;
     return launch_topk(logits, bias, T, E, k, topk_w, topk_ids, s);
