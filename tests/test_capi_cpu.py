@@ -75,6 +75,10 @@ def test_null_pointers_are_rejected_without_a_device():
     assert lib.pm_nvfp4_prepare(None, None, 4, 200, 256, None, None, None, None) == 2
     assert lib.pm_nvfp4_prepare(None, None, 4, 256, 100, None, None, None, None) == 2
     assert lib.pm_nvfp4_prepare(None, None, 0, 256, 256, None, None, None, None) == 0
+    assert lib.pm_nvfp4_prepare_search(None, None, None, 4, 256, 256, None, None, None, None) == 1
+    assert lib.pm_nvfp4_prepare_search(None, None, None, 4, 200, 256, None, None, None, None) == 2
+    assert lib.pm_nvfp4_prepare_search(None, None, None, 4, 256, 100, None, None, None, None) == 2
+    assert lib.pm_nvfp4_prepare_search(None, None, None, 0, 256, 256, None, None, None, None) == 0
     assert lib.pm_fp8_linear(None, None, None, 4, 2048, 2048, None, None, 0, None) == 1
     assert lib.pm_fp8_linear(None, None, None, 4, 2000, 2048, None, None, 0, None) == 2
     assert lib.pm_fp8_linear(None, None, None, 4, 2048, 1920, None, None, 0, None) == 2
