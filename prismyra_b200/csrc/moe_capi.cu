@@ -815,12 +815,14 @@ int pm_moe_forward_nvfp4(const void* x, const void* router_w, const void* logits
     int32_t* expert_ids = reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_IDS));
     int32_t* npp = reinterpret_cast<int32_t*>(R(PM_WS_NUM_POST_PAD));
     int32_t* slot_of = reinterpret_cast<int32_t*>(R(PM_WS_SLOT_OF));
-    if (cudaMemsetAsync(status, 0, L.len[PM_WS_STATUS], s) != cudaSuccess) return PM_ERR_CUDA;
+    // the status words start at zero: zeroed by the router kernel when it runs (no memset between this forward's
+    // first kernel and the previous one's last), else by a memset
+    if (logits != nullptr && cudaMemsetAsync(status, 0, L.len[PM_WS_STATUS], s) != cudaSuccess) return PM_ERR_CUDA;
     cudaError_t e =
         logits != nullptr
             ? launch_topk(logits, nullptr, T, E, k, topk_w, topk_ids, s)
             : launch_router_topk(x, router_w, nullptr, T, H, E, k, R(PM_WS_LOGITS), topk_w, topk_ids, status, s,
-                               router_part);
+                                 router_part, true, status);
     if (e != cudaSuccess) return PM_ERR_CUDA;
     e = launch_align(topk_ids, T * k, E, reinterpret_cast<int32_t*>(R(PM_WS_COUNTS)), sorted, expert_ids, npp,
                      reinterpret_cast<int32_t*>(R(PM_WS_EXPERT_OFF)), slot_of, s);
